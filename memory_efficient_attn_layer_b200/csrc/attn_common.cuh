@@ -1,0 +1,32 @@
+// Shared-memory tile geometry shared by the attention kernels.
+//
+// A [rows x HD] bf16 tile is stored as HD/64 column chunks (one chunk when
+// HD <= 64), each chunk `rows` rows of SWB = min(128, 2*HD) bytes with the
+// matching TMA/UMMA swizzle.  The same bytes serve as a K-major operand
+// (reduction over HD) and as an MN-major operand (reduction over rows).
+#pragma once
+#include "ptx.cuh"
+
+namespace mea {
+
+template <int HD>
+struct HeadTile {
+  static constexpr int SWB = HD * 2 >= 128 ? 128 : HD * 2;   // bytes per swizzled row
+  static constexpr int CHUNK_ELEMS = SWB / 2;                  // elements per row chunk
+  static constexpr int NCHUNK = HD / CHUNK_ELEMS;
+  static constexpr uint32_t SWZ = SWB == 128 ? SW_128B : (SWB == 64 ? SW_64B : SW_32B);
+
+  // K-major descriptor (reduce over HD), k-step of 16 elements.
+  __device__ static __forceinline__ uint64_t kmajor(uint32_t base, int rows, int kk) {
+    const int e = kk * 16;
+    const int chunk = e / CHUNK_ELEMS;
+    const int within = (e - chunk * CHUNK_ELEMS) * 2;
+    return smem_desc(base + chunk * rows * SWB + within, 16, 8 * SWB, SWZ);
+  }
+  // MN-major descriptor (reduce over rows; HD is the N/M side), k-step of 16 rows.
+  __device__ static __forceinline__ uint64_t mnmajor(uint32_t base, int rows, int kk) {
+    return smem_desc(base + kk * 16 * SWB, rows * SWB, 8 * SWB, SWZ);
+  }
+};
+
+}  // namespace mea

@@ -1,0 +1,112 @@
+// Host-side set-up and dispatch of the tcgen05 GEMM (gemm.cuh).
+#include "gemm.cuh"
+#include "launch.h"
+#include "tma.h"
+
+namespace mea {
+
+template <int BN, int AM, int BMD, int EPI>
+static int launch_gemm_t(const GemmMaps& maps, const GemmParams& p, cudaStream_t st) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_kernel<BN, AM, BMD, EPI>;
+  if (!smem_attr_set(reinterpret_cast<const void*>(kern), int(Cfg::SMEM)))
+    return set_error(MEA_ERR_CUDA, "cudaFuncSetAttribute(gemm) failed");
+  const int ntiles = p.m_tiles * p.n_tiles * p.k_splits;
+  const int grid = ntiles < num_sms() ? ntiles : num_sms();
+  kern<<<grid, GEMM_THREADS, Cfg::SMEM, st>>>(maps, p);
+  return check_launch("gemm_kernel");
+}
+
+#define MEA_GEMM_CASE(BN_, AM_, BMD_, EPI_)                                   \
+  if (bn == BN_ && am == AM_ && bmd == BMD_ && epi == EPI_)                   \
+    return launch_gemm_t<BN_, AM_, BMD_, EPI_>(maps, p, st);
+
+static int dispatch(int bn, int am, int bmd, int epi, const GemmMaps& maps, const GemmParams& p, cudaStream_t st) {
+  // forward: fused projections, o_proj
+  MEA_GEMM_CASE(256, A_K, B_SLABS, EPI_QKVG)
+  MEA_GEMM_CASE(128, A_K, B_SLABS, EPI_QKVG)
+  MEA_GEMM_CASE(256, A_K, B_K, EPI_BF16)
+  MEA_GEMM_CASE(128, A_K, B_K, EPI_BF16)
+  // backward: dGated (+ gate bwd), dx_normed, weight gradients
+  MEA_GEMM_CASE(256, A_K, B_MN, EPI_DGATE)
+  MEA_GEMM_CASE(128, A_K, B_MN, EPI_DGATE)
+  MEA_GEMM_CASE(256, A_K, B_MN_KSPLIT4, EPI_BF16)
+  MEA_GEMM_CASE(128, A_K, B_MN_KSPLIT4, EPI_BF16)
+  MEA_GEMM_CASE(256, A_MN, B_MN, EPI_RED_F32)
+  MEA_GEMM_CASE(128, A_MN, B_MN, EPI_RED_F32)
+  // generic fp32-output GEMMs (unit tests of every operand layout)
+  MEA_GEMM_CASE(256, A_K, B_K, EPI_F32)
+  MEA_GEMM_CASE(128, A_K, B_K, EPI_F32)
+  MEA_GEMM_CASE(256, A_MN, B_MN, EPI_F32)
+  MEA_GEMM_CASE(128, A_MN, B_MN, EPI_F32)
+  MEA_GEMM_CASE(256, A_K, B_MN, EPI_F32)
+  MEA_GEMM_CASE(128, A_K, B_MN, EPI_F32)
+  MEA_GEMM_CASE(256, A_MN, B_K, EPI_F32)
+  MEA_GEMM_CASE(128, A_MN, B_K, EPI_F32)
+  return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: no kernel for bn=%d amode=%d bmode=%d epi=%d", bn, am, bmd, epi);
+}
+#undef MEA_GEMM_CASE
+
+int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
+  const int bn = L.bn;
+  if (bn != 128 && bn != 256) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: bn must be 128 or 256");
+  if (L.M % GEMM_BM || L.N % bn || L.K % GEMM_BK || L.M <= 0 || L.N <= 0 || L.K <= 0)
+    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: M=%d N=%d K=%d must be multiples of 128/%d/64", L.M, L.N, L.K, bn);
+  GemmMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  int rc;
+  // A operand: K-major [M rows, K] or MN-major [K rows, M]
+  if (L.amode == A_K)
+    rc = make_tmap_2d(&maps.a, L.a, L.K, L.M, uint64_t(L.lda) * 2, 64, 128, sw);
+  else
+    rc = make_tmap_2d(&maps.a, L.a, L.M, L.K, uint64_t(L.lda) * 2, 64, 64, sw);
+  if (rc) return set_error(MEA_ERR_CUDA, "gemm: A tensor map failed (%d)", rc);
+  // B operand
+  const int nb = (L.bmode == B_K || L.bmode == B_MN) ? 1 : 4;
+  for (int i = 0; i < nb; ++i) {
+    const void* src = L.b[i];
+    if (!src) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: B tensor %d is null", i);
+    if (L.bmode == B_K)
+      rc = make_tmap_2d(&maps.b[i], src, L.K, L.N, uint64_t(L.ldb) * 2, 64, bn, sw);
+    else if (L.bmode == B_MN)
+      rc = make_tmap_2d(&maps.b[i], src, L.N, L.K, uint64_t(L.ldb) * 2, 64, 64, sw);
+    else if (L.bmode == B_SLABS)
+      rc = make_tmap_2d(&maps.b[i], src, L.K, L.b_rows, uint64_t(L.ldb) * 2, 64, L.slab_rows, sw);
+    else
+      rc = make_tmap_2d(&maps.b[i], src, L.N, L.b_rows, uint64_t(L.ldb) * 2, 64, 64, sw);
+    if (rc) return set_error(MEA_ERR_CUDA, "gemm: B tensor map %d failed (%d)", i, rc);
+  }
+  for (int i = nb; i < 4; ++i) maps.b[i] = maps.b[0];
+
+  p.M = L.M;
+  p.N = L.N;
+  p.K = L.K;
+  p.m_tiles = L.M / GEMM_BM;
+  p.n_tiles = L.N / bn;
+  p.kb_total = L.K / GEMM_BK;
+  int splits = L.k_splits < 1 ? 1 : L.k_splits;
+  if (splits > p.kb_total) splits = p.kb_total;
+  p.kb_per_split = (p.kb_total + splits - 1) / splits;
+  p.k_splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;  // every split non-empty
+  p.slab_rows = L.slab_rows;
+  p.b_kb_per_src = L.b_rows / GEMM_BK;
+  if (p.k_splits > 1 && L.epi != EPI_RED_F32)
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: split-K needs the reducing epilogue");
+  if (L.bmode == B_SLABS && (L.slab_rows % 8 || bn % L.slab_rows))
+    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: slab rows %d must divide %d", L.slab_rows, bn);
+  if (L.bmode == B_MN_KSPLIT4 && (L.b_rows % GEMM_BK || 4 * L.b_rows != L.K))
+    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: K must be 4 x rows of each B tensor");
+  return dispatch(bn, L.amode, L.bmode, L.epi, maps, p, st);
+}
+
+// Split count for a long-K GEMM with few output tiles: about `waves` work
+// units per SM, at least 8 k-blocks per unit.
+int auto_splits(int m_tiles, int n_tiles, int kb_total, int waves) {
+  const int tiles = m_tiles * n_tiles;
+  int s = (num_sms() * waves + tiles - 1) / tiles;
+  if (s > kb_total / 8) s = kb_total / 8;
+  return s < 1 ? 1 : s;
+}
+
+}  // namespace mea

@@ -1,0 +1,56 @@
+// Host-side helpers shared by the kernels' launch code: error reporting, the
+// SM count, and the internal (C++) launch functions behind the C-ABI.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+#include "mea.h"
+
+namespace mea {
+
+// Records a formatted message as this thread's last error; returns `code`.
+int set_error(int code, const char* fmt, ...);
+// Returns MEA_OK, or MEA_ERR_CUDA with the launch error recorded.
+int check_launch(const char* what);
+// SM count of the current device (cached per device).
+int num_sms();
+// Sets the dynamic shared-memory limit of `kernel` once per device.
+bool smem_attr_set(const void* kernel, int bytes);
+
+// ---- tcgen05 GEMM (gemm.cu) ----
+struct GemmParams;
+struct GemmLaunch {
+  int M, N, K;
+  int bn;      // 128 or 256
+  int amode;   // A_K / A_MN
+  int bmode;   // B_K / B_MN / B_SLABS / B_MN_KSPLIT4
+  int epi;     // EpiMode
+  const void* a;
+  long long lda;        // elements between rows of A as stored
+  const void* b[4];
+  long long ldb;        // elements between rows of B as stored
+  int b_rows;           // B_SLABS / B_MN_KSPLIT4: rows of each B tensor
+  int slab_rows;        // B_SLABS: head dim
+  int k_splits;         // > 1 only with EPI_RED_F32
+};
+int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st);
+int auto_splits(int m_tiles, int n_tiles, int kb_total, int waves);
+
+// ---- attention (attn_fwd.cu, attn_bwd.cu) ----
+int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* gs, void* gated,
+                 float* lse2, void* o_out, int* status, cudaStream_t st);
+int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
+                 const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv, int* status,
+                 cudaStream_t st);
+
+// ---- elementwise (elementwise.cu) ----
+int run_rmsnorm_fwd(int rows, int C, float eps, const void* x, void* xn, float* r, cudaStream_t st);
+int run_rmsnorm_bwd(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, cudaStream_t st);
+int run_qk_norm_rope_bwd(int B, int H, int T, int HD, const float* dq_acc, const void* dk, const void* q_rot,
+                         const void* k_rot, const float* rq, const float* rk, const void* f1, const void* f2,
+                         long long ldf, void* dacc, long long ld_dacc, float* df1, float* df2, cudaStream_t st);
+int run_cast_f32_bf16(long long n, const float* src, void* dst, cudaStream_t st);
+
+}  // namespace mea
