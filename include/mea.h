@@ -1,0 +1,137 @@
+/*
+ * mea.h -- C ABI of libmea.so, the sm_100a (B200) implementation of the gated
+ * causal attention block of xTimeCrystal/memory_efficient_attn_layer.
+ *
+ * Plain pointers, sizes and a cudaStream_t passed as void*; no framework types.
+ * All tensors live in device memory, are contiguous and row-major, and are bf16
+ * unless a parameter says fp32.  No function allocates device memory: callers
+ * pass a workspace sized by the matching *_workspace_size() query.  Every
+ * function returns MEA_OK (0) or an MEA_ERR_* code; mea_last_error_string()
+ * describes the last failure of the calling thread.
+ *
+ * Device-side waits are bounded: a kernel that gives up writes a non-zero code
+ * into the optional `status` word (device int, zero it before the call) and
+ * returns early; read it with mea_read_status().
+ *
+ * Shapes (B batch, T sequence, C model dim, H heads, N head dim):
+ *   T % 128 == 0, N in {32, 64, 128}, C % 128 == 0, (H*N) % 128 == 0.
+ * The rotary tables factor1/factor2 are [T_max >= T, N].
+ *
+ * Reference interfaces cited below are files of the reference project.
+ */
+#ifndef MEA_H_
+#define MEA_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MEA_OK = 0,
+  MEA_ERR_INVALID_ARGUMENT = 1,
+  MEA_ERR_UNSUPPORTED_SHAPE = 2,
+  MEA_ERR_ALIGNMENT = 3,
+  MEA_ERR_CUDA = 4,
+  MEA_ERR_DEVICE_TIMEOUT = 5,
+  MEA_ERR_UNSUPPORTED_DEVICE = 6,
+  MEA_ERR_WORKSPACE = 7
+};
+
+typedef struct mea_block_dims {
+  int B, T, C, H, N;
+  int T_max; /* rows of the rotary tables */
+  float eps; /* RMSNorm epsilon (reference default 1e-6, fast_triton_attn.py:681) */
+} mea_block_dims;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int mea_version(void);
+/* Message of the last failure on the calling thread ("" if none). */
+const char* mea_last_error_string(void);
+/* MEA_OK when the current device is an sm_100 part the kernels were built for. */
+int mea_device_check(void);
+/* Synchronises `stream` and copies the device status word to *out. */
+int mea_read_status(const int* status_dev, int* out, void* stream);
+
+/* ---------------------------------------------------------------- block level */
+
+/* Bytes of workspace for mea_block_forward. */
+size_t mea_forward_workspace_size(const mea_block_dims* d);
+/* FusedAttentionFunction.forward (fast_triton_attn.py:374-479):
+ * y[B,T,C] = o_proj(attn(norm-rope(proj(norm(x)))) * sigmoid(g)).
+ * Writes lse2[B,H,T] (fp32 row log-sum-exp in log2 units), the only
+ * activation kept for the backward besides x. */
+int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                      const void* wg, const void* wo, const void* factor1, const void* factor2, void* y, float* lse2,
+                      void* workspace, size_t workspace_bytes, int* status, void* stream);
+
+/* Bytes of workspace for mea_block_backward. */
+size_t mea_backward_workspace_size(const mea_block_dims* d);
+/* FusedAttentionFunction.backward (fast_triton_attn.py:481-675): recomputes
+ * the block from x and lse2, then writes dx and the five weight gradients
+ * (bf16, same shapes as the weights).  dfactor1/dfactor2 (fp32 [T_max, N],
+ * rows >= T zero) are written when non-NULL.  dweights_f32, when non-NULL,
+ * receives the fp32 weight gradients too: [4*H*N, C] for q,k,v,g followed by
+ * [C, H*N] for o. */
+int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                       const void* wg, const void* wo, const void* factor1, const void* factor2, const float* lse2,
+                       const void* dy, void* dx, void* dwq, void* dwk, void* dwv, void* dwg, void* dwo,
+                       float* dfactor1, float* dfactor2, float* dweights_f32, void* workspace,
+                       size_t workspace_bytes, int* status, void* stream);
+
+/* ---------------------------------------------------------------- kernel level */
+
+/* rms_norm_kernel / rms_norm_kernel_recompute (fast_triton_attn.py:12-34, :181-210):
+ * xn = bf16(x * r), r[row] = rsqrt(mean(x^2) + eps).  xn may be NULL. */
+int mea_rmsnorm_forward(int rows, int C, float eps, const void* x, void* xn, float* r, void* stream);
+
+/* fused_qkvg_norm_rope_kernel(_recompute) (fast_triton_attn.py:36-144, :212-332):
+ * from normalised input xn[B*T, C] write q, k (per-head RMSNorm + rotary), v and
+ * sigmoid(g), each [B,H,T,N]; rq/rk[B,H,T] (fp32 inverse RMS) when non-NULL. */
+int mea_qkvg_forward(const mea_block_dims* d, const void* xn, const void* wq, const void* wk, const void* wv,
+                     const void* wg, const void* factor1, const void* factor2, void* q, void* k, void* v, void* gs,
+                     float* rq, float* rk, int* status, void* stream);
+
+/* ATen flash-attention forward + gate_repack_kernel (fast_triton_attn.py:425-457):
+ * causal softmax(q k^T / sqrt(N)) v, times gs, repacked to gated[B,T,H*N];
+ * lse2[B,H,T] fp32 (log2 units); o[B,H,T,N] (ungated output) when non-NULL. */
+int mea_attention_forward(int B, int H, int T, int N, const void* q, const void* k, const void* v, const void* gs,
+                          void* gated, float* lse2, void* o, int* status, void* stream);
+
+/* F.linear / Tensor.matmul (fast_triton_attn.py:460, :578-579, :649-660):
+ * out[M,N] (fp32) = sum_k A[m,k] B[n,k].  A is stored [M,K] (a_mn = 0) or
+ * [K,M] (a_mn = 1) with row pitch lda; B is stored [N,K] (b_mn = 0) or [K,N]
+ * (b_mn = 1) with row pitch ldb.  accumulate != 0 adds into out (split-K). */
+int mea_gemm(int M, int N, int K, const void* a, long long lda, int a_mn, const void* b, long long ldb, int b_mn,
+             float* out, long long ldo, int accumulate, int* status, void* stream);
+
+/* o_proj backward + gate backward (fast_triton_attn.py:576-584, :601):
+ * dGated = dy * wo, then dO = dGated*gs ([B,H,T,N]), dg_pre = dGated*o*gs*(1-gs)
+ * into dg[(b*T+t)*ld_dg + h*N + n], delta[B,H,T] = rowsum(dO*o) (fp32). */
+int mea_gate_backward(const mea_block_dims* d, const void* dy, const void* wo, const void* o, const void* gs,
+                      void* dO, void* dg, long long ld_dg, float* delta, int* status, void* stream);
+
+/* ATen flash-attention backward (fast_triton_attn.py:586-596): adds dq into
+ * dq_acc[B,H,T,N] (fp32, caller zeroes it), writes dk[B,H,T,N] and
+ * dv[(b*T+t)*ld_dv + h*N + n]. */
+int mea_attention_backward(int B, int H, int T, int N, const void* q, const void* k, const void* v, const void* dO,
+                           const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv,
+                           int* status, void* stream);
+
+/* Per-head RMSNorm + rotary backward and rotary-table gradients
+ * (fast_triton_attn.py:603-639): d acc_q, d acc_k into dacc[(b*T+t)*ld_dacc +
+ * {0, H*N} + h*N + n]; dfactor1/2 (fp32 [T_max, N], caller zeroes) when non-NULL. */
+int mea_qk_norm_rope_backward(const mea_block_dims* d, const float* dq_acc, const void* dk, const void* q,
+                              const void* k, const float* rq, const float* rk, const void* factor1,
+                              const void* factor2, void* dacc, long long ld_dacc, float* dfactor1, float* dfactor2,
+                              void* stream);
+
+/* rms_norm_backward_new (fast_triton_attn.py:663-669): dx from d(xn), x and r. */
+int mea_rmsnorm_backward(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEA_H_ */

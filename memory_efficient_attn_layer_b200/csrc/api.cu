@@ -1,0 +1,479 @@
+// The extern "C" entry points of libmea.so (declared in include/mea.h) and
+// the block-level orchestration of the forward and the memory-saving backward.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "gemm.cuh"
+#include "launch.h"
+
+namespace mea {
+
+static thread_local char g_err[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(MEA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return MEA_OK;
+}
+
+static int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+int num_sms() {
+  static int cache[64] = {0};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+bool smem_attr_set(const void* kernel, int bytes) {
+  // cudaFuncSetAttribute is per device; remember (kernel, device) pairs done.
+  static std::mutex mu;
+  static const void* done_k[256];
+  static int done_d[256];
+  static int n_done = 0;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n_done; ++i)
+    if (done_k[i] == kernel && done_d[i] == dev) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  if (n_done < 256) {
+    done_k[n_done] = kernel;
+    done_d[n_done] = dev;
+    ++n_done;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Shapes, workspace layouts
+// ---------------------------------------------------------------------------
+static int pick_bn(int n) { return n % 256 == 0 ? 256 : 128; }
+
+static int validate(const mea_block_dims* d) {
+  if (!d) return set_error(MEA_ERR_INVALID_ARGUMENT, "dims is NULL");
+  if (d->B <= 0 || d->T <= 0 || d->C <= 0 || d->H <= 0 || d->N <= 0)
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "dims must be positive (B=%d T=%d C=%d H=%d N=%d)", d->B, d->T, d->C,
+                     d->H, d->N);
+  if (d->T % 128) return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "T=%d must be a multiple of 128", d->T);
+  if (d->N != 32 && d->N != 64 && d->N != 128)
+    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "head dim N=%d must be 32, 64 or 128", d->N);
+  if (d->C % 128) return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "C=%d must be a multiple of 128", d->C);
+  if ((d->H * d->N) % 128) return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "H*N=%d must be a multiple of 128", d->H * d->N);
+  if (d->T_max < d->T) return set_error(MEA_ERR_INVALID_ARGUMENT, "rotary tables have %d rows < T=%d", d->T_max, d->T);
+  if (size_t(d->B) * d->T * d->H * d->N > (size_t(1) << 31))
+    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "B*T*H*N must stay below 2^31");
+  return MEA_OK;
+}
+
+struct Carve {
+  size_t off = 0;
+  size_t take(size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  }
+};
+
+struct FwdWs {
+  size_t xn, rx, q, k, v, gs, gated, total;
+};
+static FwdWs fwd_layout(const mea_block_dims& d) {
+  const size_t M = size_t(d.B) * d.T, HN = size_t(d.H) * d.N;
+  FwdWs w;
+  Carve c;
+  w.xn = c.take(M * d.C * 2);
+  w.rx = c.take(M * 4);
+  w.q = c.take(M * HN * 2);
+  w.k = c.take(M * HN * 2);
+  w.v = c.take(M * HN * 2);
+  w.gs = c.take(M * HN * 2);
+  w.gated = c.take(M * HN * 2);
+  w.total = c.off;
+  return w;
+}
+
+struct BwdWs {
+  size_t xn, rx, q, k, v, gs, rq, rk, gated, o, lse, dO, delta, dacc, dqacc, dk, dxn, dw32, total;
+};
+static BwdWs bwd_layout(const mea_block_dims& d) {
+  const size_t M = size_t(d.B) * d.T, HN = size_t(d.H) * d.N, BHT = size_t(d.B) * d.H * d.T;
+  BwdWs w;
+  Carve c;
+  w.xn = c.take(M * d.C * 2);
+  w.rx = c.take(M * 4);
+  w.q = c.take(M * HN * 2);
+  w.k = c.take(M * HN * 2);
+  w.v = c.take(M * HN * 2);
+  w.gs = c.take(M * HN * 2);
+  w.rq = c.take(BHT * 4);
+  w.rk = c.take(BHT * 4);
+  w.gated = c.take(M * HN * 2);
+  w.o = c.take(M * HN * 2);
+  w.lse = c.take(BHT * 4);
+  w.dO = c.take(M * HN * 2);
+  w.delta = c.take(BHT * 4);
+  w.dacc = c.take(M * 4 * HN * 2);
+  w.dqacc = c.take(M * HN * 4);
+  w.dk = c.take(M * HN * 2);
+  w.dxn = c.take(M * d.C * 2);
+  w.dw32 = c.take(5 * HN * d.C * 4);
+  w.total = c.off;
+  return w;
+}
+
+// ---------------------------------------------------------------------------
+// Building blocks
+// ---------------------------------------------------------------------------
+static int qkvg(const mea_block_dims& d, const void* xn, const void* wq, const void* wk, const void* wv,
+                const void* wg, const void* f1, const void* f2, void* q, void* k, void* v, void* gs, float* rq,
+                float* rk, int* status, cudaStream_t st) {
+  const int HN = d.H * d.N;
+  GemmLaunch L{};
+  L.M = d.B * d.T;
+  L.N = 4 * HN;
+  L.K = d.C;
+  L.bn = 256;
+  L.amode = A_K;
+  L.bmode = B_SLABS;
+  L.epi = EPI_QKVG;
+  L.a = xn;
+  L.lda = d.C;
+  L.b[0] = wq;
+  L.b[1] = wk;
+  L.b[2] = wv;
+  L.b[3] = wg;
+  L.ldb = d.C;
+  L.b_rows = HN;
+  L.slab_rows = d.N;
+  L.k_splits = 1;
+  GemmParams p{};
+  p.status = status;
+  p.q = static_cast<__nv_bfloat16*>(q);
+  p.k = static_cast<__nv_bfloat16*>(k);
+  p.v = static_cast<__nv_bfloat16*>(v);
+  p.g = static_cast<__nv_bfloat16*>(gs);
+  p.f1 = static_cast<const __nv_bfloat16*>(f1);
+  p.f2 = static_cast<const __nv_bfloat16*>(f2);
+  p.ldf = d.N;
+  p.rq = rq;
+  p.rk = rk;
+  p.row_scale = nullptr;
+  p.T = d.T;
+  p.H = d.H;
+  p.hd = d.N;
+  p.eps = d.eps;
+  return run_gemm(L, p, st);
+}
+
+static int gate_bwd(const mea_block_dims& d, const void* dy, const void* wo, const void* o, const void* gs, void* dO,
+                    void* dg, long long ld_dg, float* delta, int* status, cudaStream_t st) {
+  const int HN = d.H * d.N;
+  GemmLaunch L{};
+  L.M = d.B * d.T;
+  L.N = HN;
+  L.K = d.C;
+  L.bn = pick_bn(HN);
+  L.amode = A_K;
+  L.bmode = B_MN;
+  L.epi = EPI_DGATE;
+  L.a = dy;
+  L.lda = d.C;
+  L.b[0] = wo;
+  L.ldb = HN;
+  L.k_splits = 1;
+  GemmParams p{};
+  p.status = status;
+  p.o_in = static_cast<const __nv_bfloat16*>(o);
+  p.gs_in = static_cast<const __nv_bfloat16*>(gs);
+  p.do_out = static_cast<__nv_bfloat16*>(dO);
+  p.dg_out = static_cast<__nv_bfloat16*>(dg);
+  p.ld_dg = ld_dg;
+  p.delta = delta;
+  p.T = d.T;
+  p.H = d.H;
+  p.hd = d.N;
+  return run_gemm(L, p, st);
+}
+
+// Split-K weight-gradient GEMM: out[M', N'] += A^T B over the token dim.
+static int weight_grad(int Mp, int Np, int tokens, const void* a, long long lda, const void* b, long long ldb,
+                       float* out, int* status, cudaStream_t st) {
+  GemmLaunch L{};
+  L.M = Mp;
+  L.N = Np;
+  L.K = tokens;
+  L.bn = pick_bn(Np);
+  L.amode = A_MN;
+  L.bmode = B_MN;
+  L.epi = EPI_RED_F32;
+  L.a = a;
+  L.lda = lda;
+  L.b[0] = b;
+  L.ldb = ldb;
+  L.k_splits = auto_splits(Mp / GEMM_BM, Np / L.bn, tokens / GEMM_BK, 8);
+  GemmParams p{};
+  p.status = status;
+  p.out = out;
+  p.ldo = Np;
+  return run_gemm(L, p, st);
+}
+
+#define MEA_TRY(expr)            \
+  do {                           \
+    const int rc_ = (expr);      \
+    if (rc_ != MEA_OK) return rc_; \
+  } while (0)
+
+static int memset_async(void* p, size_t bytes, cudaStream_t st) {
+  if (!p || !bytes) return MEA_OK;
+  if (cudaMemsetAsync(p, 0, bytes, st) != cudaSuccess) return set_error(MEA_ERR_CUDA, "cudaMemsetAsync failed");
+  return MEA_OK;
+}
+
+}  // namespace mea
+
+using namespace mea;
+
+extern "C" {
+
+int mea_version(void) { return 100; }
+
+const char* mea_last_error_string(void) { return g_err; }
+
+int mea_device_check(void) {
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, current_device()) != cudaSuccess)
+    return set_error(MEA_ERR_CUDA, "cudaGetDeviceProperties failed");
+  if (prop.major != 10 || prop.minor != 0)
+    return set_error(MEA_ERR_UNSUPPORTED_DEVICE, "device is sm_%d%d; libmea is built for sm_100a only", prop.major,
+                     prop.minor);
+  return MEA_OK;
+}
+
+int mea_read_status(const int* status_dev, int* out, void* stream) {
+  if (!status_dev || !out) return set_error(MEA_ERR_INVALID_ARGUMENT, "status pointers are NULL");
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return set_error(MEA_ERR_CUDA, "stream sync: %s", cudaGetErrorString(cudaGetLastError()));
+  if (cudaMemcpy(out, status_dev, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return set_error(MEA_ERR_CUDA, "status copy failed");
+  if (*out != 0)
+    return set_error(MEA_ERR_DEVICE_TIMEOUT, "device wait timed out (kernel %d, site %d)", (*out >> 8) & 0xFF,
+                     (*out >> 16) & 0xFFFF);
+  return MEA_OK;
+}
+
+size_t mea_forward_workspace_size(const mea_block_dims* d) {
+  if (validate(d) != MEA_OK) return 0;
+  return fwd_layout(*d).total;
+}
+
+size_t mea_backward_workspace_size(const mea_block_dims* d) {
+  if (validate(d) != MEA_OK) return 0;
+  return bwd_layout(*d).total;
+}
+
+int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                      const void* wg, const void* wo, const void* factor1, const void* factor2, void* y, float* lse2,
+                      void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  MEA_TRY(validate(d));
+  const FwdWs w = fwd_layout(*d);
+  if (!workspace || workspace_bytes < w.total)
+    return set_error(MEA_ERR_WORKSPACE, "forward workspace needs %zu bytes, got %zu", w.total, workspace_bytes);
+  auto st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  const int M = d->B * d->T, HN = d->H * d->N;
+  MEA_TRY(run_rmsnorm_fwd(M, d->C, d->eps, x, ws + w.xn, reinterpret_cast<float*>(ws + w.rx), st));
+  MEA_TRY(qkvg(*d, ws + w.xn, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, nullptr,
+               nullptr, status, st));
+  MEA_TRY(run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated, lse2, nullptr,
+                       status, st));
+  GemmLaunch L{};
+  L.M = M;
+  L.N = d->C;
+  L.K = HN;
+  L.bn = pick_bn(d->C);
+  L.amode = A_K;
+  L.bmode = B_K;
+  L.epi = EPI_BF16;
+  L.a = ws + w.gated;
+  L.lda = HN;
+  L.b[0] = wo;
+  L.ldb = HN;
+  L.k_splits = 1;
+  GemmParams p{};
+  p.status = status;
+  p.out = y;
+  p.ldo = d->C;
+  return run_gemm(L, p, st);
+}
+
+int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                       const void* wg, const void* wo, const void* factor1, const void* factor2, const float* lse2,
+                       const void* dy, void* dx, void* dwq, void* dwk, void* dwv, void* dwg, void* dwo,
+                       float* dfactor1, float* dfactor2, float* dweights_f32, void* workspace,
+                       size_t workspace_bytes, int* status, void* stream) {
+  MEA_TRY(validate(d));
+  const BwdWs w = bwd_layout(*d);
+  if (!workspace || workspace_bytes < w.total)
+    return set_error(MEA_ERR_WORKSPACE, "backward workspace needs %zu bytes, got %zu", w.total, workspace_bytes);
+  auto st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  const int M = d->B * d->T, HN = d->H * d->N, C = d->C;
+  const size_t BHTN = size_t(M) * HN;
+  float* rx = reinterpret_cast<float*>(ws + w.rx);
+  float* rq = reinterpret_cast<float*>(ws + w.rq);
+  float* rk = reinterpret_cast<float*>(ws + w.rk);
+  float* delta = reinterpret_cast<float*>(ws + w.delta);
+  float* dqacc = reinterpret_cast<float*>(ws + w.dqacc);
+  float* dw32 = dweights_f32 ? dweights_f32 : reinterpret_cast<float*>(ws + w.dw32);
+  float* dwo32 = dw32 + size_t(4) * HN * C;
+  char* dacc = ws + w.dacc;
+  const long long ld_dacc = 4LL * HN;
+
+  // Recompute: input norm, projections (+ inverse RMS of q/k), attention (+ O).
+  MEA_TRY(run_rmsnorm_fwd(M, C, d->eps, x, ws + w.xn, rx, st));
+  MEA_TRY(qkvg(*d, ws + w.xn, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, rq, rk,
+               status, st));
+  MEA_TRY(run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated,
+                       reinterpret_cast<float*>(ws + w.lse), ws + w.o, status, st));
+  MEA_TRY(memset_async(dw32, size_t(5) * HN * C * 4, st));
+  MEA_TRY(memset_async(dqacc, BHTN * 4, st));
+  MEA_TRY(memset_async(dfactor1, size_t(d->T_max) * d->N * 4, st));
+  MEA_TRY(memset_async(dfactor2, size_t(d->T_max) * d->N * 4, st));
+  // o_proj backward: dWo = dY^T gated; dGated = dY Wo with the gate backward fused.
+  MEA_TRY(weight_grad(C, HN, M, dy, C, ws + w.gated, HN, dwo32, status, st));
+  MEA_TRY(gate_bwd(*d, dy, wo, ws + w.o, ws + w.gs, ws + w.dO, dacc + size_t(3) * HN * 2, ld_dacc, delta, status,
+                   st));
+  // Attention backward: dq (fp32 accumulate), dk, dv -> v slot of dacc.
+  MEA_TRY(run_attn_bwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.dO, lse2, delta, dqacc, ws + w.dk,
+                       dacc + size_t(2) * HN * 2, ld_dacc, status, st));
+  // q/k norm + rotary backward -> q, k slots of dacc; rotary-table gradients.
+  MEA_TRY(run_qk_norm_rope_bwd(d->B, d->H, d->T, d->N, dqacc, ws + w.dk, ws + w.q, ws + w.k, rq, rk, factor1, factor2,
+                               d->N, dacc, ld_dacc, dfactor1, dfactor2, st));
+  // Projection weight gradients: [4HN, C] = dacc^T xn.
+  MEA_TRY(weight_grad(4 * HN, C, M, dacc, ld_dacc, ws + w.xn, C, dw32, status, st));
+  // dx_normed = dacc [Wq; Wk; Wv; Wg]
+  {
+    GemmLaunch L{};
+    L.M = M;
+    L.N = C;
+    L.K = 4 * HN;
+    L.bn = pick_bn(C);
+    L.amode = A_K;
+    L.bmode = B_MN_KSPLIT4;
+    L.epi = EPI_BF16;
+    L.a = dacc;
+    L.lda = ld_dacc;
+    L.b[0] = wq;
+    L.b[1] = wk;
+    L.b[2] = wv;
+    L.b[3] = wg;
+    L.ldb = C;
+    L.b_rows = HN;
+    L.k_splits = 1;
+    GemmParams p{};
+    p.status = status;
+    p.out = ws + w.dxn;
+    p.ldo = C;
+    MEA_TRY(run_gemm(L, p, st));
+  }
+  MEA_TRY(run_rmsnorm_bwd(M, C, ws + w.dxn, x, rx, dx, st));
+  const size_t wsz = size_t(HN) * C;
+  MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32, dwq, st));
+  MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32 + wsz, dwk, st));
+  MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32 + 2 * wsz, dwv, st));
+  MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32 + 3 * wsz, dwg, st));
+  MEA_TRY(run_cast_f32_bf16((long long)wsz, dwo32, dwo, st));
+  return MEA_OK;
+}
+
+int mea_rmsnorm_forward(int rows, int C, float eps, const void* x, void* xn, float* r, void* stream) {
+  return run_rmsnorm_fwd(rows, C, eps, x, xn, r, static_cast<cudaStream_t>(stream));
+}
+
+int mea_qkvg_forward(const mea_block_dims* d, const void* xn, const void* wq, const void* wk, const void* wv,
+                     const void* wg, const void* factor1, const void* factor2, void* q, void* k, void* v, void* gs,
+                     float* rq, float* rk, int* status, void* stream) {
+  MEA_TRY(validate(d));
+  return qkvg(*d, xn, wq, wk, wv, wg, factor1, factor2, q, k, v, gs, rq, rk, status, static_cast<cudaStream_t>(stream));
+}
+
+int mea_attention_forward(int B, int H, int T, int N, const void* q, const void* k, const void* v, const void* gs,
+                          void* gated, float* lse2, void* o, int* status, void* stream) {
+  return run_attn_fwd(B, H, T, N, q, k, v, gs, gated, lse2, o, status, static_cast<cudaStream_t>(stream));
+}
+
+int mea_gemm(int M, int N, int K, const void* a, long long lda, int a_mn, const void* b, long long ldb, int b_mn,
+             float* out, long long ldo, int accumulate, int* status, void* stream) {
+  GemmLaunch L{};
+  L.M = M;
+  L.N = N;
+  L.K = K;
+  L.bn = pick_bn(N);
+  L.amode = a_mn ? A_MN : A_K;
+  L.bmode = b_mn ? B_MN : B_K;
+  L.epi = accumulate ? EPI_RED_F32 : EPI_F32;
+  L.a = a;
+  L.lda = lda;
+  L.b[0] = b;
+  L.ldb = ldb;
+  L.k_splits = 1;
+  if (accumulate && M % GEMM_BM == 0 && N % L.bn == 0 && K % GEMM_BK == 0)
+    L.k_splits = auto_splits(M / GEMM_BM, N / L.bn, K / GEMM_BK, 8);
+  if (accumulate && L.amode != A_MN) L.k_splits = 1;  // the reducing epilogue is built for A_MN x B_MN only
+  if (accumulate && (L.amode != A_MN || L.bmode != B_MN))
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "mea_gemm: accumulate needs a_mn = b_mn = 1");
+  GemmParams p{};
+  p.status = status;
+  p.out = out;
+  p.ldo = ldo;
+  return run_gemm(L, p, static_cast<cudaStream_t>(stream));
+}
+
+int mea_gate_backward(const mea_block_dims* d, const void* dy, const void* wo, const void* o, const void* gs,
+                      void* dO, void* dg, long long ld_dg, float* delta, int* status, void* stream) {
+  MEA_TRY(validate(d));
+  return gate_bwd(*d, dy, wo, o, gs, dO, dg, ld_dg, delta, status, static_cast<cudaStream_t>(stream));
+}
+
+int mea_attention_backward(int B, int H, int T, int N, const void* q, const void* k, const void* v, const void* dO,
+                           const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv,
+                           int* status, void* stream) {
+  return run_attn_bwd(B, H, T, N, q, k, v, dO, lse2, delta, dq_acc, dk, dv, ld_dv, status,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int mea_qk_norm_rope_backward(const mea_block_dims* d, const float* dq_acc, const void* dk, const void* q,
+                              const void* k, const float* rq, const float* rk, const void* factor1,
+                              const void* factor2, void* dacc, long long ld_dacc, float* dfactor1, float* dfactor2,
+                              void* stream) {
+  MEA_TRY(validate(d));
+  if ((dfactor1 == nullptr) != (dfactor2 == nullptr))
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "dfactor1 and dfactor2 must both be set or both be NULL");
+  return run_qk_norm_rope_bwd(d->B, d->H, d->T, d->N, dq_acc, dk, q, k, rq, rk, factor1, factor2, d->N, dacc, ld_dacc,
+                              dfactor1, dfactor2, static_cast<cudaStream_t>(stream));
+}
+
+int mea_rmsnorm_backward(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, void* stream) {
+  return run_rmsnorm_bwd(rows, C, dxn, x, r, dx, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

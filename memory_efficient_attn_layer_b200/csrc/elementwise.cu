@@ -1,0 +1,278 @@
+// Bandwidth-bound kernels of the block: the input RMSNorm forward and
+// backward, the per-head q/k RMSNorm + rotary backward (with the optional
+// rotary-table gradients), and an fp32 -> bf16 cast for the weight gradients.
+// All are one pass over HBM with 16-byte vector accesses.
+#include <cuda_bf16.h>
+
+#include "launch.h"
+#include "ptx.cuh"
+
+namespace mea {
+
+// ---------------------------------------------------------------------------
+// Input RMSNorm forward: xn = bf16(x * r), r = rsqrt(mean(x^2) + eps).
+// One warp per row (fast_triton_attn.py:12-34 and the inv_rms store of
+// :181-210).
+// ---------------------------------------------------------------------------
+__global__ void rmsnorm_fwd_kernel(int rows, int C, float eps, const __nv_bfloat16* __restrict__ x,
+                                   __nv_bfloat16* __restrict__ xn, float* __restrict__ rout) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const __nv_bfloat16* xr = x + size_t(warp) * C;
+  float ss = 0.f;
+  for (int c = lane * 8; c < C; c += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a = bf16_lo(w[e]), b = bf16_hi(w[e]);
+      ss = fmaf(a, a, fmaf(b, b, ss));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / float(C) + eps);
+  if (rout && lane == 0) rout[warp] = r;
+  if (!xn) return;
+  __nv_bfloat16* yr = xn + size_t(warp) * C;
+  for (int c = lane * 8; c < C; c += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = pack_bf16(bf16_lo(w[e]) * r, bf16_hi(w[e]) * r);
+    st_global_v4(yr + c, o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Input RMSNorm backward (fast_triton_attn.py:663-669):
+//   dx = r * (g - xn * sum(g * xn) / C),  xn = bf16(x * r), g = d xn.
+// ---------------------------------------------------------------------------
+__global__ void rmsnorm_bwd_kernel(int rows, int C, const __nv_bfloat16* __restrict__ dxn,
+                                   const __nv_bfloat16* __restrict__ x, const float* __restrict__ rin,
+                                   __nv_bfloat16* __restrict__ dx) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const size_t off = size_t(warp) * C;
+  const float r = rin[warp];
+  float dot = 0.f;
+  for (int c = lane * 8; c < C; c += 256) {
+    const uint4 gv = *reinterpret_cast<const uint4*>(dxn + off + c);
+    const uint4 xv = *reinterpret_cast<const uint4*>(x + off + c);
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      dot = fmaf(bf16_lo(gw[e]), round_bf16(bf16_lo(xw[e]) * r), dot);
+      dot = fmaf(bf16_hi(gw[e]), round_bf16(bf16_hi(xw[e]) * r), dot);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  const float k = dot / float(C);
+  for (int c = lane * 8; c < C; c += 256) {
+    const uint4 gv = *reinterpret_cast<const uint4*>(dxn + off + c);
+    const uint4 xv = *reinterpret_cast<const uint4*>(x + off + c);
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float n0 = round_bf16(bf16_lo(xw[e]) * r), n1 = round_bf16(bf16_hi(xw[e]) * r);
+      o[e] = pack_bf16(r * (bf16_lo(gw[e]) - n0 * k), r * (bf16_hi(gw[e]) - n1 * k));
+    }
+    st_global_v4(dx + off + c, o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-head q/k RMSNorm + rotary backward, exact for any rotary table.
+//
+// Forward (per pair i of row (b,h,t)): qn = acc * r, q_rot = R_t qn with
+//   R_t = [[f1[2i], f2[2i]], [f2[2i+1], f1[2i+1]]]   (fast_triton_attn.py:140).
+// Backward from d q_rot:
+//   dqn  = R_t^T dq_rot                                (inverse rotary, :614-619)
+//   dot  = sum(dqn * qn) = sum(dq_rot * q_rot)          (holds for any R_t)
+//   dacc = r * (dqn - qn * dot / N)                     (norm backward, :603-612)
+// qn is recovered from the stored bf16 q_rot through R_t^{-1}; pairs with a
+// singular 2x2 block contribute qn = 0 there.  The reference applies the norm
+// backward in the rotated frame, which equals this only for orthogonal R_t.
+// Table gradients (:622-639), exact form:
+//   df1[t,n] += dq_rot[n] * qn[n],  df2[t,n] += dq_rot[n] * qn[n^1]  over (b,h), q and k.
+//
+// Grid: x = position t, y = chunk of the B*H rows; each block loops over its
+// (b,h) rows at fixed t so the table gradients reduce in registers and leave
+// the block with one atomic per (t, n).
+// ---------------------------------------------------------------------------
+template <int HD>
+__global__ void __launch_bounds__(256) qk_bwd_kernel(int BH, int H, int T, int bh_per_block,
+                                                     const float* __restrict__ dq_acc,
+                                                     const __nv_bfloat16* __restrict__ dk,
+                                                     const __nv_bfloat16* __restrict__ q_rot,
+                                                     const __nv_bfloat16* __restrict__ k_rot,
+                                                     const float* __restrict__ rq, const float* __restrict__ rk,
+                                                     const __nv_bfloat16* __restrict__ f1,
+                                                     const __nv_bfloat16* __restrict__ f2, long long ldf,
+                                                     __nv_bfloat16* __restrict__ dacc, long long ld_dacc,
+                                                     float* __restrict__ df1, float* __restrict__ df2) {
+  constexpr int TPR = HD / 2 < 32 ? HD / 2 : 32;  // threads per row
+  constexpr int EPT = HD / TPR;                    // elements per thread (2 or 4)
+  constexpr int RPB = 256 / TPR;                   // rows in flight per block
+  const int t = blockIdx.x;
+  const int sub = threadIdx.x % TPR;
+  const int grp = threadIdx.x / TPR;
+  const int n0 = sub * EPT;
+  const int HN = H * HD;
+
+  float tf1[EPT], tf2[EPT];
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) {
+    tf1[e] = __bfloat162float(f1[size_t(t) * ldf + n0 + e]);
+    tf2[e] = __bfloat162float(f2[size_t(t) * ldf + n0 + e]);
+  }
+  float a1[EPT], a2[EPT];
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) a1[e] = a2[e] = 0.f;
+
+  const int bh_begin = blockIdx.y * bh_per_block;
+  const int bh_end = min(bh_begin + bh_per_block, BH);
+  // Trip count is uniform across the block so the row shuffles below always
+  // see every lane; lanes past the end work on zeros and store nothing.
+  for (int base = bh_begin; base < bh_end; base += RPB) {
+    const int bh = base + grp;
+    const bool valid = bh < bh_end;
+    const size_t row = size_t(valid ? bh : bh_begin) * T + t;
+    const int b = (valid ? bh : bh_begin) / H, h = (valid ? bh : bh_begin) % H;
+    __nv_bfloat16* drow = dacc + (size_t(b) * T + t) * ld_dacc + size_t(h) * HD + n0;
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      float g[EPT], y[EPT];
+      const __nv_bfloat16* src = (which == 0 ? q_rot : k_rot) + row * HD + n0;
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) {
+        g[e] = !valid ? 0.f : (which == 0 ? dq_acc[row * HD + n0 + e] : __bfloat162float(dk[row * HD + n0 + e]));
+        y[e] = !valid ? 0.f : __bfloat162float(src[e]);
+      }
+      const float r = valid ? (which == 0 ? rq : rk)[row] : 0.f;
+      float dot = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) dot = fmaf(g[e], y[e], dot);
+#pragma unroll
+      for (int o = TPR / 2; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o, TPR);
+      const float kk = dot / float(HD);
+      uint32_t out[EPT / 2];
+#pragma unroll
+      for (int e = 0; e < EPT; e += 2) {
+        const float fe1 = tf1[e], fo1 = tf1[e + 1], fe2 = tf2[e], fo2 = tf2[e + 1];
+        const float det = fe1 * fo1 - fe2 * fo2;
+        const float inv = fabsf(det) > 1e-30f ? 1.0f / det : 0.f;
+        const float qa = (fo1 * y[e] - fe2 * y[e + 1]) * inv;
+        const float qb = (fe1 * y[e + 1] - fo2 * y[e]) * inv;
+        const float da = fe1 * g[e] + fo2 * g[e + 1];
+        const float db = fe2 * g[e] + fo1 * g[e + 1];
+        out[e / 2] = pack_bf16(r * (da - qa * kk), r * (db - qb * kk));
+        a1[e] = fmaf(g[e], qa, a1[e]);
+        a1[e + 1] = fmaf(g[e + 1], qb, a1[e + 1]);
+        a2[e] = fmaf(g[e], qb, a2[e]);
+        a2[e + 1] = fmaf(g[e + 1], qa, a2[e + 1]);
+      }
+      __nv_bfloat16* d = drow + (which == 0 ? 0 : HN);
+      if (valid) {
+        if (EPT == 2)
+          *reinterpret_cast<uint32_t*>(d) = out[0];
+        else
+          *reinterpret_cast<uint2*>(d) = make_uint2(out[0], out[EPT / 2 - 1]);
+      }
+    }
+  }
+  if (!df1) return;
+  __shared__ float red[2][RPB][HD];
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) {
+    red[0][grp][n0 + e] = a1[e];
+    red[1][grp][n0 + e] = a2[e];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 2 * HD; i += blockDim.x) {
+    const int w = i / HD, n = i % HD;
+    float s = 0.f;
+    for (int gI = 0; gI < RPB; ++gI) s += red[w][gI][n];
+    atomicAdd((w == 0 ? df1 : df2) + size_t(t) * HD + n, s);
+  }
+}
+
+__global__ void cast_f32_bf16_kernel(long long n, const float* __restrict__ src, __nv_bfloat16* __restrict__ dst) {
+  const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i + 3 < n) {
+    const float4 v = *reinterpret_cast<const float4*>(src + i);
+    *reinterpret_cast<uint2*>(dst + i) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+  } else {
+    for (long long j = i; j < n; ++j) dst[j] = __float2bfloat16_rn(src[j]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+int run_rmsnorm_fwd(int rows, int C, float eps, const void* x, void* xn, float* r, cudaStream_t st) {
+  if (C % 8 || C <= 0 || rows <= 0) return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "rmsnorm: C=%d must be a multiple of 8", C);
+  const int threads = 256;
+  const int blocks = (rows * 32 + threads - 1) / threads;
+  rmsnorm_fwd_kernel<<<blocks, threads, 0, st>>>(rows, C, eps, static_cast<const __nv_bfloat16*>(x),
+                                                 static_cast<__nv_bfloat16*>(xn), r);
+  return check_launch("rmsnorm_fwd_kernel");
+}
+
+int run_rmsnorm_bwd(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, cudaStream_t st) {
+  if (C % 8 || C <= 0 || rows <= 0) return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "rmsnorm bwd: C=%d must be a multiple of 8", C);
+  const int threads = 256;
+  const int blocks = (rows * 32 + threads - 1) / threads;
+  rmsnorm_bwd_kernel<<<blocks, threads, 0, st>>>(rows, C, static_cast<const __nv_bfloat16*>(dxn),
+                                                 static_cast<const __nv_bfloat16*>(x), r,
+                                                 static_cast<__nv_bfloat16*>(dx));
+  return check_launch("rmsnorm_bwd_kernel");
+}
+
+int run_qk_norm_rope_bwd(int B, int H, int T, int HD, const float* dq_acc, const void* dk, const void* q_rot,
+                         const void* k_rot, const float* rq, const float* rk, const void* f1, const void* f2,
+                         long long ldf, void* dacc, long long ld_dacc, float* df1, float* df2, cudaStream_t st) {
+  const int BH = B * H;
+  const int bh_per_block = BH < 64 ? BH : 64;
+  dim3 grid(T, (BH + bh_per_block - 1) / bh_per_block);
+  auto f1p = static_cast<const __nv_bfloat16*>(f1);
+  auto f2p = static_cast<const __nv_bfloat16*>(f2);
+  auto dkp = static_cast<const __nv_bfloat16*>(dk);
+  auto qp = static_cast<const __nv_bfloat16*>(q_rot);
+  auto kp = static_cast<const __nv_bfloat16*>(k_rot);
+  auto dp = static_cast<__nv_bfloat16*>(dacc);
+  switch (HD) {
+    case 32:
+      qk_bwd_kernel<32><<<grid, 256, 0, st>>>(BH, H, T, bh_per_block, dq_acc, dkp, qp, kp, rq, rk, f1p, f2p, ldf, dp,
+                                              ld_dacc, df1, df2);
+      break;
+    case 64:
+      qk_bwd_kernel<64><<<grid, 256, 0, st>>>(BH, H, T, bh_per_block, dq_acc, dkp, qp, kp, rq, rk, f1p, f2p, ldf, dp,
+                                              ld_dacc, df1, df2);
+      break;
+    case 128:
+      qk_bwd_kernel<128><<<grid, 256, 0, st>>>(BH, H, T, bh_per_block, dq_acc, dkp, qp, kp, rq, rk, f1p, f2p, ldf, dp,
+                                               ld_dacc, df1, df2);
+      break;
+    default:
+      return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "qk backward: head dim %d not in {32, 64, 128}", HD);
+  }
+  return check_launch("qk_bwd_kernel");
+}
+
+int run_cast_f32_bf16(long long n, const float* src, void* dst, cudaStream_t st) {
+  if (n <= 0) return MEA_OK;
+  const long long threads = 256;
+  const long long blocks = (n / 4 + threads) / threads;
+  cast_f32_bf16_kernel<<<unsigned(blocks), unsigned(threads), 0, st>>>(n, src, static_cast<__nv_bfloat16*>(dst));
+  return check_launch("cast_f32_bf16_kernel");
+}
+
+}  // namespace mea
