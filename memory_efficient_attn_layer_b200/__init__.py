@@ -1,0 +1,11 @@
+"""B200-native (sm_100a) gated causal attention block.
+
+Drop-in for xTimeCrystal/memory_efficient_attn_layer: ``fused_attn``,
+``FusedAttentionFunction`` and ``CausalSoftmaxAttention`` keep the reference's
+names and call surface; the work runs in hand-written tcgen05/TMA kernels in
+``libmea.so`` (C ABI in ``include/mea.h``).
+"""
+from .fused_attn import FusedAttentionFunction, fused_attn
+from .module import CausalSoftmaxAttention, Yarn
+
+__all__ = ["fused_attn", "FusedAttentionFunction", "CausalSoftmaxAttention", "Yarn"]

@@ -1,0 +1,148 @@
+"""ctypes binding of libmea.so (declared in include/mea.h).
+
+The library is built in-tree (``python -m memory_efficient_attn_layer_b200.build``)
+and loaded from next to this file.  There is no fallback: if the library is
+missing or the GPU is not an sm_100 part, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import threading
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libmea.so")
+HEADER_PATH = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "mea.h")
+
+MEA_OK = 0
+ERROR_NAMES = {
+    1: "MEA_ERR_INVALID_ARGUMENT", 2: "MEA_ERR_UNSUPPORTED_SHAPE", 3: "MEA_ERR_ALIGNMENT",
+    4: "MEA_ERR_CUDA", 5: "MEA_ERR_DEVICE_TIMEOUT", 6: "MEA_ERR_UNSUPPORTED_DEVICE", 7: "MEA_ERR_WORKSPACE",
+}
+
+
+class MeaBlockDims(ctypes.Structure):
+    _fields_ = [("B", ctypes.c_int), ("T", ctypes.c_int), ("C", ctypes.c_int), ("H", ctypes.c_int),
+                ("N", ctypes.c_int), ("T_max", ctypes.c_int), ("eps", ctypes.c_float)]
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_LL = ctypes.c_longlong
+_F = ctypes.c_float
+_S = ctypes.c_size_t
+_D = ctypes.POINTER(MeaBlockDims)
+
+# name -> (restype, argtypes); mirrors include/mea.h
+SIGNATURES = {
+    "mea_version": (_I, []),
+    "mea_last_error_string": (ctypes.c_char_p, []),
+    "mea_device_check": (_I, []),
+    "mea_read_status": (_I, [_P, ctypes.POINTER(_I), _P]),
+    "mea_forward_workspace_size": (_S, [_D]),
+    "mea_block_forward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P, _P]),
+    "mea_backward_workspace_size": (_S, [_D]),
+    "mea_block_backward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                _P, _S, _P, _P]),
+    "mea_rmsnorm_forward": (_I, [_I, _I, _F, _P, _P, _P, _P]),
+    "mea_qkvg_forward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "mea_attention_forward": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "mea_gemm": (_I, [_I, _I, _I, _P, _LL, _I, _P, _LL, _I, _P, _LL, _I, _P, _P]),
+    "mea_gate_backward": (_I, [_D, _P, _P, _P, _P, _P, _P, _LL, _P, _P, _P]),
+    "mea_attention_backward": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P]),
+    "mea_qk_norm_rope_backward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P, _P]),
+    "mea_rmsnorm_backward": (_I, [_I, _I, _P, _P, _P, _P, _P]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def header_symbols() -> list:
+    """Names of the functions declared in include/mea.h."""
+    with open(HEADER_PATH) as f:
+        text = f.read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(mea_[a-z0-9_]+)\s*\(", text)))
+
+
+def lib() -> ctypes.CDLL:
+    """Load libmea.so once and declare its signatures."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"libmea.so not found at {LIB_PATH}; build it with "
+                        "`python -m memory_efficient_attn_layer_b200.build`")
+                L = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(L, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = L
+    return _lib
+
+
+class MeaError(RuntimeError):
+    """A non-zero status from libmea; ``code`` is the MEA_ERR_* value."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERROR_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+def check(rc: int) -> None:
+    if rc != MEA_OK:
+        raise MeaError(rc, lib().mea_last_error_string().decode(errors="replace"))
+
+
+def ptr(t) -> int | None:
+    """Device address of a tensor (None for None)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(device=None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+_status = {}
+_checked_devices = set()
+
+
+def status_buffer(device: torch.device) -> torch.Tensor:
+    """Per-device int32 word the kernels write when a bounded wait gives up."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _status.get(idx)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=device)
+        _status[idx] = buf
+    return buf
+
+
+def read_status(device: torch.device) -> int:
+    """Synchronises the current stream and raises MeaError if a kernel timed out."""
+    buf = status_buffer(device)
+    out = ctypes.c_int(0)
+    rc = lib().mea_read_status(ctypes.c_void_p(buf.data_ptr()), ctypes.byref(out),
+                               ctypes.c_void_p(stream_ptr(device)))
+    if rc != MEA_OK:
+        buf.zero_()
+        check(rc)
+    return out.value
+
+
+def require_device(device: torch.device) -> None:
+    """Raises unless `device` is a CUDA sm_100 device (checked once per device)."""
+    if device.type != "cuda":
+        raise RuntimeError("memory_efficient_attn_layer_b200 runs on CUDA (sm_100a) tensors only; "
+                           f"got a tensor on {device}")
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx in _checked_devices:
+        return
+    with torch.cuda.device(idx):
+        check(lib().mea_device_check())
+    _checked_devices.add(idx)

@@ -55,7 +55,9 @@ struct AttnBwdCfg {
   static constexpr uint32_t OFF_DS = OFF_DO + STAGES * TB;
   static constexpr uint32_t OFF_LSE = OFF_DS + DS_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_LSE + STAGES * 1024;
-  static constexpr size_t SMEM = 1024 + OFF_BAR + 256;
+  static constexpr size_t SMEM_USED = 1024 + OFF_BAR + 256;
+  // One CTA per SM: all 512 TMEM columns are allocated.
+  static constexpr size_t SMEM = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
 };
 
 template <int HD>

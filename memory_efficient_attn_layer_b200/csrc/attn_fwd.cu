@@ -43,7 +43,10 @@ struct AttnFwdCfg {
   static constexpr uint32_t TILE_BYTES = 128 * HD * 2;
   static constexpr uint32_t O_COL = 256;  // TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+HD)
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr size_t SMEM = 1024 + TILE_BYTES * (1 + 2 * STAGES) + 256;
+  static constexpr size_t SMEM_USED = 1024 + TILE_BYTES * (1 + 2 * STAGES) + 256;
+  // All 512 TMEM columns are taken, so ask for enough shared memory that a
+  // second CTA never lands on the same SM (it would only wait in tcgen05.alloc).
+  static constexpr size_t SMEM = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
 };
 
 template <int HD>

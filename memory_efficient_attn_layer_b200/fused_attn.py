@@ -1,0 +1,113 @@
+"""``fused_attn`` and its autograd function: the drop-in boundary.
+
+Mirrors the reference's interface (fast_triton_attn.py:373-697): same names,
+same argument order and meaning, same gradient tuple.  The work is done by
+libmea.so (sm_100a kernels) through two calls, ``mea_block_forward`` and
+``mea_block_backward``.  The forward keeps only x, the weights, the rotary
+tables and the attention row log-sum-exp for the backward; everything else is
+recomputed there (the reference additionally keeps the attention output,
+fast_triton_attn.py:463-466).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from . import _lib
+
+_CHECK_STATUS = os.environ.get("MEA_CHECK_STATUS", "0") == "1"
+
+
+def _dims(x: torch.Tensor, H: int, N: int, factor1: torch.Tensor, eps: float) -> _lib.MeaBlockDims:
+    B, T, C = x.shape
+    return _lib.MeaBlockDims(B, T, C, int(H), int(N), factor1.shape[0], float(eps))
+
+
+def _check_inputs(x, weights, factor1, factor2, H, N):
+    _lib.require_device(x.device)
+    if x.dim() != 3:
+        raise ValueError(f"x must be [B, T, C], got shape {tuple(x.shape)}")
+    B, T, C = x.shape
+    HN = H * N
+    shapes = [(HN, C)] * 4 + [(C, HN)]
+    for name, w, shp in zip(("q", "k", "v", "g", "o"), weights, shapes):
+        if tuple(w.shape) != shp:
+            raise ValueError(f"{name}_proj.weight must be {shp}, got {tuple(w.shape)}")
+    for t in (x, *weights, factor1, factor2):
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"fused_attn computes in bf16; got a {t.dtype} tensor")
+        if t.device != x.device:
+            raise ValueError("all tensors must be on the same device")
+    if factor1.dim() != 2 or factor1.shape[1] != N or factor1.shape[0] < T or factor2.shape != factor1.shape:
+        raise ValueError(f"rotary tables must be [T_max >= {T}, {N}], got {tuple(factor1.shape)} / "
+                         f"{tuple(factor2.shape)}")
+
+
+class FusedAttentionFunction(torch.autograd.Function):
+    """Autograd node of the block (fast_triton_attn.py:373)."""
+
+    @staticmethod
+    def forward(ctx, x, q_weight, k_weight, v_weight, g_weight, o_weight, factor1, factor2, H, N, eps):
+        weights = [w.contiguous() for w in (q_weight, k_weight, v_weight, g_weight, o_weight)]
+        x = x.contiguous()
+        factor1 = factor1.contiguous()
+        factor2 = factor2.contiguous()
+        _check_inputs(x, weights, factor1, factor2, H, N)
+        B, T, C = x.shape
+        L = _lib.lib()
+        dims = _dims(x, H, N, factor1, eps)
+        y = torch.empty_like(x)
+        lse = torch.empty(B, H, T, dtype=torch.float32, device=x.device)
+        ws_bytes = L.mea_forward_workspace_size(ctypes.byref(dims))
+        if ws_bytes == 0:  # invalid dims: let the library say why
+            _lib.check(L.mea_block_forward(ctypes.byref(dims), *([None] * 11), 0, None, None))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+        status = _lib.status_buffer(x.device)
+        _lib.check(L.mea_block_forward(
+            ctypes.byref(dims), _lib.ptr(x), *[_lib.ptr(w) for w in weights], _lib.ptr(factor1),
+            _lib.ptr(factor2), _lib.ptr(y), _lib.ptr(lse), _lib.ptr(ws), ws_bytes, _lib.ptr(status),
+            _lib.stream_ptr(x.device)))
+        if _CHECK_STATUS:
+            _lib.read_status(x.device)
+        ctx.save_for_backward(x, *weights, factor1, factor2, lse)
+        ctx.H, ctx.N, ctx.eps = int(H), int(N), float(eps)
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        x, wq, wk, wv, wg, wo, factor1, factor2, lse = ctx.saved_tensors
+        H, N, eps = ctx.H, ctx.N, ctx.eps
+        dy = grad_output.to(torch.bfloat16).contiguous()
+        L = _lib.lib()
+        dims = _dims(x, H, N, factor1, eps)
+        dx = torch.empty_like(x)
+        dws = [torch.empty_like(w) for w in (wq, wk, wv, wg, wo)]
+        want_df = ctx.needs_input_grad[6] or ctx.needs_input_grad[7]
+        df1 = torch.empty(factor1.shape, dtype=torch.float32, device=x.device) if want_df else None
+        df2 = torch.empty(factor2.shape, dtype=torch.float32, device=x.device) if want_df else None
+        ws_bytes = L.mea_backward_workspace_size(ctypes.byref(dims))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+        status = _lib.status_buffer(x.device)
+        _lib.check(L.mea_block_backward(
+            ctypes.byref(dims), _lib.ptr(x), _lib.ptr(wq), _lib.ptr(wk), _lib.ptr(wv), _lib.ptr(wg), _lib.ptr(wo),
+            _lib.ptr(factor1), _lib.ptr(factor2), _lib.ptr(lse), _lib.ptr(dy), _lib.ptr(dx),
+            *[_lib.ptr(d) for d in dws], _lib.ptr(df1), _lib.ptr(df2), None, _lib.ptr(ws), ws_bytes,
+            _lib.ptr(status), _lib.stream_ptr(x.device)))
+        if _CHECK_STATUS:
+            _lib.read_status(x.device)
+        gf1 = df1.to(factor1.dtype) if want_df else None
+        gf2 = df2.to(factor2.dtype) if want_df else None
+        return (dx, *dws, gf1, gf2, None, None, None)
+
+
+def fused_attn(x, q_proj, k_proj, v_proj, g_proj, o_proj, yarn_module, H, N, eps=1e-6):
+    """Gated causal attention block (fast_triton_attn.py:681-697).
+
+    Reads ``.weight`` of the five bias-free ``nn.Linear`` projections and
+    ``.factor1`` / ``.factor2`` of the rotary object, exactly as the reference.
+    """
+    return FusedAttentionFunction.apply(
+        x, q_proj.weight, k_proj.weight, v_proj.weight, g_proj.weight, o_proj.weight,
+        yarn_module.factor1, yarn_module.factor2, H, N, eps)
