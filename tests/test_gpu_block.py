@@ -1,0 +1,106 @@
+"""GPU: the whole block (forward + memory-saving backward) through the public
+API against the CPU oracle and the reference's golden vectors.
+
+Tolerances: outputs max|a-b|/max|b| <= 2e-2 against the
+fp32 oracle; every gradient cosine similarity > 0.999."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import DEV, cos, maxrel
+from memory_efficient_attn_layer_b200 import FusedAttentionFunction
+from oracle.eager import GRAD_NAMES, block_fwd_bwd, make_inputs
+
+pytestmark = pytest.mark.gpu
+Y_TOL = 2e-2
+COS_TOL = 0.999
+
+
+def run_block(inp, H, N, factor_grads=True):
+    leaves = []
+    for k in ("x", "wq", "wk", "wv", "wg", "wo", "f1", "f2"):
+        t = inp[k].to(device=DEV, dtype=torch.bfloat16).contiguous()
+        t.requires_grad_(k not in ("f1", "f2") or factor_grads)
+        leaves.append(t)
+    y = FusedAttentionFunction.apply(*leaves, H, N, 1e-6)
+    y.backward(inp["dy"].to(device=DEV, dtype=torch.bfloat16))
+    torch.cuda.synchronize()
+    out = {"y": y.detach().float().cpu()}
+    for name, leaf in zip(GRAD_NAMES, leaves):
+        if leaf.grad is not None:
+            out[name] = leaf.grad.float().cpu()
+    return out
+
+
+def check(got, want, names, y_tol=Y_TOL, cos_tol=COS_TOL):
+    assert maxrel(got["y"], want["y"]) <= y_tol, ("y", maxrel(got["y"], want["y"]))
+    for n in names:
+        if n == "y":
+            continue
+        c = cos(got[n], want[n])
+        assert c > cos_tol, (n, c)
+
+
+def load_golden(name):
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", f"golden_{name}.npz"))
+    B, T, C, H, N, seed, T_max = (int(v) for v in z["shape"])
+    inp = {k[3:]: torch.from_numpy(z[k].view(np.int16)).view(torch.bfloat16).float()
+           for k in z.files if k.startswith("in_")}
+    want = {k: torch.from_numpy(z[k]) for k in ["y", *GRAD_NAMES]}
+    return (H, N), inp, want
+
+
+@pytest.mark.parametrize("case", ["c1", "n64", "n128"])
+def test_block_matches_oracle_and_reference(case):
+    (H, N), inp, ref = load_golden(case)
+    got = run_block(inp, H, N)
+    oracle = block_fwd_bwd(inp, H, N)
+    check(got, oracle, ["y", *GRAD_NAMES])
+    # against the reference's own outputs (both sides round to bf16 along the way)
+    check(got, ref, ["y", *GRAD_NAMES], y_tol=3e-2)
+    # factor-table gradient rows beyond T are zero, as in the reference (fast_triton_attn.py:636-639)
+    T = inp["x"].shape[1]
+    assert torch.count_nonzero(got["df1"][T:]) == 0 and torch.count_nonzero(got["df2"][T:]) == 0
+
+
+def test_block_nonorthogonal_table_is_exact():
+    """A rotary table with magnitude 1.3: the reference's rotated-frame backward is
+    inexact here (cos ~0.99 for dWk); this path stays at the oracle's bar."""
+    inp = make_inputs(2, 256, 128, 2, 64, seed=7, mscale=1.3)
+    check(run_block(inp, 2, 64), block_fwd_bwd(inp, 2, 64), ["y", *GRAD_NAMES])
+
+
+def test_block_without_factor_grads():
+    inp = make_inputs(1, 256, 256, 4, 64, seed=8)
+    got = run_block(inp, 4, 64, factor_grads=False)
+    assert "df1" not in got
+    check(got, block_fwd_bwd(inp, 4, 64, factor_grads=False), ["y", *GRAD_NAMES[:6]])
+
+
+def test_block_forward_is_deterministic():
+    inp = make_inputs(2, 256, 128, 4, 32, seed=9)
+    a = run_block(inp, 4, 32)["y"]
+    b = run_block(inp, 4, 32)["y"]
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("B,T,C,H,N", [(128, 2048, 512, 8, 64), (32, 4096, 1024, 8, 128)])
+def test_block_full_size_single_sequence_gradient(B, T, C, H, N):
+    """Baseline-size shapes (configs 2 and 3).  The upstream gradient is non-zero
+    for sequence 0 only, so (a) y[0], dx[0] and every weight gradient must equal
+    the oracle run on sequence 0 alone, and (b) dx of every other sequence must
+    be exactly zero: a size-independent check of the batch independence."""
+    g = torch.Generator().manual_seed(11)
+    inp0 = make_inputs(1, T, C, H, N, seed=11)
+    x = torch.randn(B, T, C, generator=g).to(torch.bfloat16).float()
+    x[0] = inp0["x"][0]
+    dy = torch.zeros(B, T, C)
+    dy[0] = inp0["dy"][0]
+    full = dict(inp0, x=x, dy=dy)
+    got = run_block(full, H, N, factor_grads=False)
+    want = block_fwd_bwd(inp0, H, N, factor_grads=False)
+    assert torch.count_nonzero(got["dx"][1:]) == 0
+    got0 = {k: (v[:1] if k in ("y", "dx") else v) for k, v in got.items()}
+    check(got0, want, ["y", *GRAD_NAMES[:6]])
