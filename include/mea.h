@@ -130,6 +130,20 @@ int mea_qk_norm_rope_backward(const mea_block_dims* d, const float* dq_acc, cons
 /* rms_norm_backward_new (fast_triton_attn.py:663-669): dx from d(xn), x and r. */
 int mea_rmsnorm_backward(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, void* stream);
 
+/* ---------------------------------------------------------------- profiling
+ * No counterpart in the reference (it has no timing hooks).  When enabled,
+ * mea_block_forward / mea_block_backward record CUDA events on the caller's
+ * stream around each of their kernels. */
+
+/* Enables (on != 0) or disables recording and drops recorded events. */
+int mea_profile_enable(int on);
+/* Synchronises the recorded events, writes per-stage total milliseconds and
+ * launch counts (arrays of max_stages), clears the record; returns the number
+ * of stages the library knows (or a negative error). */
+int mea_profile_read(int max_stages, float* total_ms, int* counts);
+/* Name of a profiling stage ("" when out of range). */
+const char* mea_profile_stage_name(int stage);
+
 #ifdef __cplusplus
 }
 #endif

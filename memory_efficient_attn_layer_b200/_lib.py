@@ -54,6 +54,9 @@ SIGNATURES = {
     "mea_attention_backward": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P]),
     "mea_qk_norm_rope_backward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P, _P]),
     "mea_rmsnorm_backward": (_I, [_I, _I, _P, _P, _P, _P, _P]),
+    "mea_profile_enable": (_I, [_I]),
+    "mea_profile_read": (_I, [_I, ctypes.POINTER(_F), ctypes.POINTER(_I)]),
+    "mea_profile_stage_name": (ctypes.c_char_p, [_I]),
 }
 
 _lib = None
@@ -146,3 +149,19 @@ def require_device(device: torch.device) -> None:
     with torch.cuda.device(idx):
         check(lib().mea_device_check())
     _checked_devices.add(idx)
+
+
+def profile_enable(on: bool = True) -> None:
+    """Start (or stop) per-stage CUDA-event timing inside the block calls."""
+    check(lib().mea_profile_enable(1 if on else 0))
+
+
+def profile_read() -> dict:
+    """{stage name: (total ms, launches)} since the last enable/read; syncs."""
+    n = 32
+    ms = (_F * n)()
+    cnt = (_I * n)()
+    k = lib().mea_profile_read(n, ms, cnt)
+    if k < 0:
+        check(k)
+    return {lib().mea_profile_stage_name(i).decode(): (ms[i], cnt[i]) for i in range(k) if cnt[i]}

@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
+#include <vector>
 
 #include "gemm.cuh"
 #include "launch.h"
@@ -236,10 +237,63 @@ static int weight_grad(int Mp, int Np, int tokens, const void* a, long long lda,
   return run_gemm(L, p, st);
 }
 
+
+// ---------------------------------------------------------------------------
+// Optional per-stage timing: CUDA events recorded on the caller's stream around
+// every kernel of the block calls (mea_profile_enable / mea_profile_read).
+// ---------------------------------------------------------------------------
+enum Stage : int {
+  ST_FWD_NORM = 0, ST_FWD_QKVG, ST_FWD_ATTN, ST_FWD_OPROJ,
+  ST_BWD_NORM, ST_BWD_QKVG, ST_BWD_ATTN_FWD, ST_BWD_MEMSET, ST_BWD_DWO, ST_BWD_DGATE, ST_BWD_ATTN, ST_BWD_QK,
+  ST_BWD_DW, ST_BWD_DX, ST_BWD_NORM_BWD, ST_BWD_CAST, ST_COUNT
+};
+static const char* kStageNames[ST_COUNT] = {
+  "fwd.rmsnorm", "fwd.qkvg_gemm", "fwd.attention", "fwd.o_proj_gemm",
+  "bwd.rmsnorm", "bwd.qkvg_gemm", "bwd.attention_recompute", "bwd.memset", "bwd.dWo_gemm", "bwd.dgate_gemm",
+  "bwd.attention_bwd", "bwd.qk_norm_rope_bwd", "bwd.dW_gemm", "bwd.dx_gemm", "bwd.rmsnorm_bwd", "bwd.cast"};
+
+struct Profiler {
+  std::mutex mu;
+  bool on = false;
+  struct Rec { int stage; cudaEvent_t a, b; };
+  std::vector<Rec> recs;
+  std::vector<cudaEvent_t> pool;
+  cudaEvent_t get() {
+    if (!pool.empty()) { cudaEvent_t e = pool.back(); pool.pop_back(); return e; }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+};
+static Profiler g_prof;
+
+struct StageScope {
+  int stage;
+  cudaStream_t st;
+  cudaEvent_t b = nullptr;
+  StageScope(int s, cudaStream_t stream) : stage(s), st(stream) {
+    if (!g_prof.on) return;
+    std::lock_guard<std::mutex> lock(g_prof.mu);
+    cudaEvent_t a = g_prof.get();
+    b = g_prof.get();
+    cudaEventRecord(a, st);
+    g_prof.recs.push_back({stage, a, b});
+  }
+  ~StageScope() {
+    if (b) cudaEventRecord(b, st);
+  }
+};
+
 #define MEA_TRY(expr)            \
   do {                           \
     const int rc_ = (expr);      \
     if (rc_ != MEA_OK) return rc_; \
+  } while (0)
+
+#define MEA_STAGE(id, expr)        \
+  do {                             \
+    StageScope scope_(id, st);     \
+    MEA_TRY(expr);                 \
   } while (0)
 
 static int memset_async(void* p, size_t bytes, cudaStream_t st) {
@@ -300,10 +354,10 @@ int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, co
   auto st = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
   const int M = d->B * d->T, HN = d->H * d->N;
-  MEA_TRY(run_rmsnorm_fwd(M, d->C, d->eps, x, ws + w.xn, reinterpret_cast<float*>(ws + w.rx), st));
-  MEA_TRY(qkvg(*d, ws + w.xn, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, nullptr,
+  MEA_STAGE(ST_FWD_NORM, run_rmsnorm_fwd(M, d->C, d->eps, x, ws + w.xn, reinterpret_cast<float*>(ws + w.rx), st));
+  MEA_STAGE(ST_FWD_QKVG, qkvg(*d, ws + w.xn, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, nullptr,
                nullptr, status, st));
-  MEA_TRY(run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated, lse2, nullptr,
+  MEA_STAGE(ST_FWD_ATTN, run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated, lse2, nullptr,
                        status, st));
   GemmLaunch L{};
   L.M = M;
@@ -322,6 +376,7 @@ int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, co
   p.status = status;
   p.out = y;
   p.ldo = d->C;
+  StageScope scope_(ST_FWD_OPROJ, st);
   return run_gemm(L, p, st);
 }
 
@@ -349,27 +404,30 @@ int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, c
   const long long ld_dacc = 4LL * HN;
 
   // Recompute: input norm, projections (+ inverse RMS of q/k), attention (+ O).
-  MEA_TRY(run_rmsnorm_fwd(M, C, d->eps, x, ws + w.xn, rx, st));
-  MEA_TRY(qkvg(*d, ws + w.xn, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, rq, rk,
+  MEA_STAGE(ST_BWD_NORM, run_rmsnorm_fwd(M, C, d->eps, x, ws + w.xn, rx, st));
+  MEA_STAGE(ST_BWD_QKVG, qkvg(*d, ws + w.xn, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, rq, rk,
                status, st));
-  MEA_TRY(run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated,
+  MEA_STAGE(ST_BWD_ATTN_FWD, run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated,
                        reinterpret_cast<float*>(ws + w.lse), ws + w.o, status, st));
-  MEA_TRY(memset_async(dw32, size_t(5) * HN * C * 4, st));
-  MEA_TRY(memset_async(dqacc, BHTN * 4, st));
-  MEA_TRY(memset_async(dfactor1, size_t(d->T_max) * d->N * 4, st));
-  MEA_TRY(memset_async(dfactor2, size_t(d->T_max) * d->N * 4, st));
+  {
+    StageScope scope_(ST_BWD_MEMSET, st);
+    MEA_TRY(memset_async(dw32, size_t(5) * HN * C * 4, st));
+    MEA_TRY(memset_async(dqacc, BHTN * 4, st));
+    MEA_TRY(memset_async(dfactor1, size_t(d->T_max) * d->N * 4, st));
+    MEA_TRY(memset_async(dfactor2, size_t(d->T_max) * d->N * 4, st));
+  }
   // o_proj backward: dWo = dY^T gated; dGated = dY Wo with the gate backward fused.
-  MEA_TRY(weight_grad(C, HN, M, dy, C, ws + w.gated, HN, dwo32, status, st));
-  MEA_TRY(gate_bwd(*d, dy, wo, ws + w.o, ws + w.gs, ws + w.dO, dacc + size_t(3) * HN * 2, ld_dacc, delta, status,
+  MEA_STAGE(ST_BWD_DWO, weight_grad(C, HN, M, dy, C, ws + w.gated, HN, dwo32, status, st));
+  MEA_STAGE(ST_BWD_DGATE, gate_bwd(*d, dy, wo, ws + w.o, ws + w.gs, ws + w.dO, dacc + size_t(3) * HN * 2, ld_dacc, delta, status,
                    st));
   // Attention backward: dq (fp32 accumulate), dk, dv -> v slot of dacc.
-  MEA_TRY(run_attn_bwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.dO, lse2, delta, dqacc, ws + w.dk,
+  MEA_STAGE(ST_BWD_ATTN, run_attn_bwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.dO, lse2, delta, dqacc, ws + w.dk,
                        dacc + size_t(2) * HN * 2, ld_dacc, status, st));
   // q/k norm + rotary backward -> q, k slots of dacc; rotary-table gradients.
-  MEA_TRY(run_qk_norm_rope_bwd(d->B, d->H, d->T, d->N, dqacc, ws + w.dk, ws + w.q, ws + w.k, rq, rk, factor1, factor2,
+  MEA_STAGE(ST_BWD_QK, run_qk_norm_rope_bwd(d->B, d->H, d->T, d->N, dqacc, ws + w.dk, ws + w.q, ws + w.k, rq, rk, factor1, factor2,
                                d->N, dacc, ld_dacc, dfactor1, dfactor2, st));
   // Projection weight gradients: [4HN, C] = dacc^T xn.
-  MEA_TRY(weight_grad(4 * HN, C, M, dacc, ld_dacc, ws + w.xn, C, dw32, status, st));
+  MEA_STAGE(ST_BWD_DW, weight_grad(4 * HN, C, M, dacc, ld_dacc, ws + w.xn, C, dw32, status, st));
   // dx_normed = dacc [Wq; Wk; Wv; Wg]
   {
     GemmLaunch L{};
@@ -393,10 +451,11 @@ int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, c
     p.status = status;
     p.out = ws + w.dxn;
     p.ldo = C;
-    MEA_TRY(run_gemm(L, p, st));
+    MEA_STAGE(ST_BWD_DX, run_gemm(L, p, st));
   }
-  MEA_TRY(run_rmsnorm_bwd(M, C, ws + w.dxn, x, rx, dx, st));
+  MEA_STAGE(ST_BWD_NORM_BWD, run_rmsnorm_bwd(M, C, ws + w.dxn, x, rx, dx, st));
   const size_t wsz = size_t(HN) * C;
+  StageScope cast_scope(ST_BWD_CAST, st);
   MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32, dwq, st));
   MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32 + wsz, dwk, st));
   MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32 + 2 * wsz, dwv, st));
@@ -474,6 +533,43 @@ int mea_qk_norm_rope_backward(const mea_block_dims* d, const float* dq_acc, cons
 
 int mea_rmsnorm_backward(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, void* stream) {
   return run_rmsnorm_bwd(rows, C, dxn, x, r, dx, static_cast<cudaStream_t>(stream));
+}
+
+int mea_profile_enable(int on) {
+  std::lock_guard<std::mutex> lock(g_prof.mu);
+  for (auto& r : g_prof.recs) {
+    g_prof.pool.push_back(r.a);
+    g_prof.pool.push_back(r.b);
+  }
+  g_prof.recs.clear();
+  g_prof.on = on != 0;
+  return MEA_OK;
+}
+
+int mea_profile_read(int max_stages, float* total_ms, int* counts) {
+  if (!total_ms || !counts || max_stages <= 0) return set_error(MEA_ERR_INVALID_ARGUMENT, "profile buffers are NULL");
+  std::lock_guard<std::mutex> lock(g_prof.mu);
+  for (int i = 0; i < max_stages; ++i) {
+    total_ms[i] = 0.f;
+    counts[i] = 0;
+  }
+  for (auto& r : g_prof.recs) {
+    if (cudaEventSynchronize(r.b) != cudaSuccess) return set_error(MEA_ERR_CUDA, "profile event sync failed");
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, r.a, r.b);
+    if (r.stage < max_stages) {
+      total_ms[r.stage] += ms;
+      counts[r.stage] += 1;
+    }
+    g_prof.pool.push_back(r.a);
+    g_prof.pool.push_back(r.b);
+  }
+  g_prof.recs.clear();
+  return ST_COUNT;
+}
+
+const char* mea_profile_stage_name(int stage) {
+  return (stage >= 0 && stage < ST_COUNT) ? kStageNames[stage] : "";
 }
 
 }  // extern "C"
