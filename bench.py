@@ -1,0 +1,417 @@
+#!/usr/bin/env python
+"""Forward + backward throughput of one gated causal attention block on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|eager]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N
+
+One step = forward + backward of the block (fast_triton_attn.py:374-675) over
+one batch of synthetic input already resident in HBM, through the public
+autograd API; with N > 1 ranks the batch is sharded by sequence (B per rank
+fixed: weak scaling) and the five weight gradients are all-reduced over NCCL.
+
+--impl reference : the reference path's CPU implementation timed on the host
+                   cores (the eager block restated in oracle/eager.py), on a
+                   bounded sample (one sequence of the workload per step).
+--impl eager     : the reference's eager GPU equivalent (README.md:42-64:
+                   checkpointed norm/projections/rotary + SDPA flash + gated
+                   o_proj) in plain PyTorch, as an informative comparator.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fwd+bwd tokens/s per attn block"
+# BASELINE.json configs (per GPU)
+CONFIGS = {
+    "c2": dict(B=128, T=2048, C=512, H=8, N=64, name="c2: 50M-class block B=128 T=2048 C=512 H=8 N=64"),
+    "c3": dict(B=32, T=4096, C=1024, H=8, N=128, name="c3: wide block B=32 T=4096 C=1024 H=8 N=128"),
+    "c4": dict(B=4, T=16384, C=2048, H=16, N=128, name="c4: long-context block B=4 T=16384 C=2048 H=16 N=128"),
+    "c5": dict(B=128, T=2048, C=768, H=12, N=64, name="c5: DP block, global B=1024 T=2048 C=768 H=12 N=64 (B=128 per GPU at 8 GPUs)"),
+}
+LAUNCHES_PER_STAGE = {"bwd.cast": 5, "bwd.memset": 0}
+
+
+def model_flops(B, T, C, H, N):
+    """Algorithmic fwd+bwd flops: 5 projections x (fwd, dgrad, wgrad) + causal attention (fwd 2, bwd 5)."""
+    M = B * T
+    return 30 * M * C * H * N + 7 * B * H * T * T * N
+
+
+def stage_flops(B, T, C, H, N):
+    M, HN = B * T, H * N
+    attn_fwd = 2 * B * H * T * T * N
+    return {
+        "fwd.qkvg_gemm": 2 * M * C * 4 * HN, "fwd.attention": attn_fwd, "fwd.o_proj_gemm": 2 * M * HN * C,
+        "bwd.qkvg_gemm": 2 * M * C * 4 * HN, "bwd.attention_recompute": attn_fwd, "bwd.dWo_gemm": 2 * M * C * HN,
+        "bwd.dgate_gemm": 2 * M * C * HN, "bwd.attention_bwd": 5 * B * H * T * T * N,
+        "bwd.dW_gemm": 2 * M * 4 * HN * C, "bwd.dx_gemm": 2 * M * 4 * HN * C,
+    }
+
+
+def stage_bytes(B, T, C, H, N):
+    """Algorithmic HBM bytes of the bandwidth-bound stages."""
+    M, HN = B * T, H * N
+    return {
+        "fwd.rmsnorm": M * C * 2 * 2 + M * 4, "bwd.rmsnorm": M * C * 2 * 2 + M * 4,
+        "bwd.qk_norm_rope_bwd": M * HN * (4 + 2 + 2 + 2 + 2 * 2) + 2 * B * H * T * 4,
+        "bwd.rmsnorm_bwd": M * C * 2 * 3 + M * 4, "bwd.cast": 5 * HN * C * 6,
+    }
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        load = sorted(sm)[len(sm) // 4:] if sm else []  # drop ramp-up samples
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- inputs
+def make_block_inputs(cfg, device, rank, requires_grad=True):
+    from memory_efficient_attn_layer_b200 import Yarn
+
+    B, T, C, H, N = (cfg[k] for k in ("B", "T", "C", "H", "N"))
+    g = torch.Generator(device=device).manual_seed(0)  # weights replicated on every rank
+    bound = 0.5 / math.sqrt(C)
+    ws = [(torch.rand(H * N, C, device=device, generator=g) * 2 - 1) * bound for _ in range(4)]
+    ws.append((torch.rand(C, H * N, device=device, generator=g) * 2 - 1) * bound)
+    ws = [w.to(torch.bfloat16).requires_grad_(requires_grad) for w in ws]
+    gx = torch.Generator(device=device).manual_seed(1000 + rank)  # this rank's shard of the batch
+    x = torch.randn(B, T, C, device=device, generator=gx).to(torch.bfloat16)
+    dy = torch.randn(B, T, C, device=device, generator=gx).to(torch.bfloat16)
+    yarn = Yarn(N, T, device=device)
+    return x, ws, yarn, dy
+
+
+# --------------------------------------------------------------------------- CPU baseline
+def cpu_sample(cfg, budget_s=12.0, min_reps=2):
+    """Eager fp32 block on the host cores, one sequence of the workload per rep."""
+    from oracle.eager import block_fwd_bwd, make_inputs
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    inp = make_inputs(1, cfg["T"], cfg["C"], cfg["H"], cfg["N"], seed=0)
+    block_fwd_bwd(inp, cfg["H"], cfg["N"])  # warm-up
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < min_reps or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        block_fwd_bwd(inp, cfg["H"], cfg["N"])
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": cfg["T"] / t, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"eager fp32 block fwd+bwd (oracle/eager.py) on 1 sequence of {cfg['T']} tokens "
+                      f"(C={cfg['C']} H={cfg['H']} N={cfg['N']}), median of {len(times)} reps",
+            "s_per_sequence": t}
+
+
+# --------------------------------------------------------------------------- arms
+def run_reference(args, cfg, rank, world):
+    """CPU implementation of the path (oracle port) on the host cores; rank 0 only."""
+    if rank != 0:
+        return
+    from oracle.eager import block_fwd_bwd, make_inputs
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    inp = make_inputs(1, cfg["T"], cfg["C"], cfg["H"], cfg["N"], seed=0)
+    for _ in range(args.warmup):
+        block_fwd_bwd(inp, cfg["H"], cfg["N"])
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        block_fwd_bwd(inp, cfg["H"], cfg["N"])
+    dt = time.perf_counter() - t0
+    value = args.steps * cfg["T"] / dt
+    sample = (f"eager fp32 block fwd+bwd (oracle/eager.py, the reference's eager equivalent README.md:42-64) on one "
+              f"sequence of {cfg['T']} tokens per step")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg["name"], "sample": "1 sequence per step", "B": 1, "T": cfg["T"], "C": cfg["C"],
+                   "H": cfg["H"], "N": cfg["N"]},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def eager_block(x, ws, yarn, H, N, eps=1e-6):
+    """README.md:42-64 in plain PyTorch on the GPU (comparator only)."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    B, T, C = x.shape
+    wq, wk, wv, wg, wo = ws
+
+    def norm(t):
+        return F.rms_norm(t, (t.shape[-1],), eps=eps)
+
+    def forward1(x):
+        x = norm(x)
+        q = F.linear(x, wq).view(B, T, H, N)
+        k = F.linear(x, wk).view(B, T, H, N)
+        v = F.linear(x, wv).view(B, T, H, N)
+        g = F.linear(x, wg)
+        return yarn.rotary(norm(q)), yarn.rotary(norm(k)), v, g
+
+    q, k, v, g = torch.utils.checkpoint.checkpoint(forward1, x, use_reentrant=False)
+    with sdpa_kernel(SDPBackend.FLASH_ATTENTION):
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True)
+    o = o.transpose(1, 2).contiguous().view(B, T, H * N)
+    return F.linear(o * torch.sigmoid(g), wo)
+
+
+def run_gpu(args, cfg, rank, world, device):
+    import torch.distributed as dist
+
+    from memory_efficient_attn_layer_b200 import FusedAttentionFunction, _lib
+
+    B, T, C, H, N = (cfg[k] for k in ("B", "T", "C", "H", "N"))
+    tokens_rank = B * T
+    x, ws, yarn, dy = make_block_inputs(cfg, device, rank)
+    eager = args.impl == "eager"
+
+    def fwd(inp):
+        if eager:
+            return eager_block(inp, ws, yarn, H, N)
+        return FusedAttentionFunction.apply(inp, *ws, yarn.factor1, yarn.factor2, H, N, 1e-6)
+
+    def step(inp, grad):
+        y = fwd(inp)
+        y.backward(grad)
+        if world > 1:
+            for w in ws:
+                dist.all_reduce(w.grad)
+        for w in ws:
+            w.grad = None
+        return y
+
+    # ---- activation memory: what the forward keeps for the backward, and the fwd+bwd peak
+    torch.cuda.synchronize(device)
+    torch.cuda.reset_peak_memory_stats(device)
+    m0 = torch.cuda.memory_allocated(device)
+    xa = x.detach().requires_grad_(True)
+    y = fwd(xa)
+    torch.cuda.synchronize(device)
+    saved = torch.cuda.memory_allocated(device) - m0 - y.numel() * y.element_size()
+    y.backward(dy)
+    torch.cuda.synchronize(device)
+    peak = torch.cuda.max_memory_allocated(device) - m0
+    del y, xa
+    for w in ws:
+        w.grad = None
+
+    # ---- device-timed steps (inputs resident in HBM; x is 2*B*T*C bytes > L2)
+    for _ in range(args.warmup):
+        step(x, dy)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    if not eager:
+        _lib.profile_enable(True)
+    clocks = ClockSampler(device.index if device.index is not None else 0)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step(x, dy)
+    ev1.record()
+    torch.cuda.synchronize(device)
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    stages = {}
+    if not eager:
+        stages = _lib.profile_read()
+        _lib.profile_enable(False)
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * tokens_rank * args.steps / (ms / 1e3)
+
+    # ---- end to end through the public API: pinned host input -> device, fwd+bwd, loss back to host
+    xh = x.detach().cpu().pin_memory()
+    dyh = dy.detach().cpu().pin_memory()
+    loss_h = torch.empty(1, dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, args.steps // 10)
+
+    def e2e_step():
+        xd = xh.to(device, non_blocking=True)
+        dyd = dyh.to(device, non_blocking=True)
+        y = fwd(xd)
+        loss = (y * dyd).sum(dtype=torch.float32)
+        loss.backward()
+        if world > 1:
+            for w in ws:
+                dist.all_reduce(w.grad)
+        for w in ws:
+            w.grad = None
+        loss_h.copy_(loss.detach().view(1), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    ems = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ems], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e_value = world * tokens_rank * e2e_steps / (ems / 1e3)
+
+    if rank != 0:
+        return
+    peaks = load_peaks()
+    F_step = model_flops(B, T, C, H, N)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: x, dy ~ N(0,1); weights ~ U(+-0.5/sqrt(C)) replicated; rotary tables for N, T",
+        "config": {"workload": cfg["name"], "B_per_gpu": B, "global_batch": B * world, "T": T, "C": C, "H": H,
+                   "N": N, "parallelism": f"dp{world}" if world > 1 else "single",
+                   "l2": f"inputs larger than L2 (x is {2 * B * T * C / 1e6:.0f} MB per GPU), no flush"},
+    }
+    if eager:
+        line["impl"] = "eager"
+    line["tensor_pipe_frac_step"] = {
+        "achieved_tflops": F_step / (ms_step / 1e3) / 1e12, "peak_tflops": peaks["bf16_tflops_sustained"],
+        "frac": F_step / (ms_step / 1e3) / 1e12 / peaks["bf16_tflops_sustained"],
+        "flops_per_step": F_step, "peak_source": peaks["source"] + " sustained"}
+    line["activation_gb"] = {"saved_for_backward": saved / 1e9, "peak_fwd_bwd": peak / 1e9}
+    if stages:
+        sf, sb = stage_flops(B, T, C, H, N), stage_bytes(B, T, C, H, N)
+        table = {}
+        for name, (tot, cnt) in stages.items():
+            avg = tot / cnt
+            row = {"ms": avg, "share": tot / sum(v[0] for v in stages.values())}
+            if name in sf:
+                row["tflops"] = sf[name] / (avg / 1e3) / 1e12
+            if name in sb:
+                row["gbs"] = sb[name] / (avg / 1e3) / 1e9
+            table[name] = row
+        line["stages"] = table
+        top = max(stages, key=lambda k: stages[k][0])
+        avg = stages[top][0] / stages[top][1]
+        if top in sf:
+            ach = sf[top] / (avg / 1e3) / 1e12
+            line["roofline"] = {"kernel": top, "bound": "tensor", "achieved": ach,
+                                "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                                "frac": ach / peaks["bf16_tflops_sustained"], "traffic": None,
+                                "peak_source": peaks["source"] + " sustained",
+                                "algorithmic": f"{sf[top]:.4g} flop per launch"}
+        else:
+            ach = sb[top] / (avg / 1e3) / 1e9
+            line["roofline"] = {"kernel": top, "bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"],
+                                "unit": "GB/s", "frac": ach / peaks["hbm_gbs"], "traffic": None,
+                                "peak_source": peaks["source"]}
+        line["gpu_launches"] = sum(cnt * LAUNCHES_PER_STAGE.get(n, 1) for n, (_, cnt) in stages.items())
+    line["e2e"] = {"value": e2e_value, "unit": "tokens/s",
+                   "h2d_bytes_per_step": world * (x.numel() * x.element_size() + dy.numel() * dy.element_size()),
+                   "d2h_bytes_per_step": world * 4,
+                   "path": "FusedAttentionFunction.apply + loss=(y*dy).sum() + backward, pinned host x/dy copied in, "
+                           "loss copied out, every step"}
+    line["clocks"] = clk
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_sample(cfg)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference", "eager"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    cfg = CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, rank, world)
+        return
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    try:
+        run_gpu(args, cfg, rank, world, device)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
