@@ -130,6 +130,20 @@ int mea_qk_norm_rope_backward(const mea_block_dims* d, const float* dq_acc, cons
 /* rms_norm_backward_new (fast_triton_attn.py:663-669): dx from d(xn), x and r. */
 int mea_rmsnorm_backward(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, void* stream);
 
+/* ---------------------------------------------------------------- no allocation
+ * No counterpart in the reference.  mea_attention_backward for callers that
+ * cannot allocate device memory (for example a plugin whose execute callback
+ * may not call cudaMalloc, or code handed only its input and output buffers):
+ * the fp32 dQ accumulator lives in a 16 MiB array inside the library (held by
+ * every GPU that loads it), so B*H*T*N must not exceed 4,194,304; larger
+ * problems return MEA_ERR_UNSUPPORTED_SHAPE.  dq is written as bf16
+ * [B,H,T,N]; dk, dv as in mea_attention_backward.  All calls share that array:
+ * calls that overlap on the GPU race.  The first call on a device looks up the
+ * array's address; make it before any stream capture. */
+int mea_attention_backward_noalloc(int B, int H, int T, int N, const void* q, const void* k, const void* v,
+                                   const void* dO, const float* lse2, const float* delta, void* dq, void* dk,
+                                   void* dv, long long ld_dv, int* status, void* stream);
+
 /* ---------------------------------------------------------------- profiling
  * No counterpart in the reference (it has no timing hooks).  When enabled,
  * mea_block_forward / mea_block_backward record CUDA events on the caller's

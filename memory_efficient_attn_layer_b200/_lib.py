@@ -54,6 +54,7 @@ SIGNATURES = {
     "mea_attention_backward": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P]),
     "mea_qk_norm_rope_backward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P, _P]),
     "mea_rmsnorm_backward": (_I, [_I, _I, _P, _P, _P, _P, _P]),
+    "mea_attention_backward_noalloc": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P]),
     "mea_profile_enable": (_I, [_I]),
     "mea_profile_read": (_I, [_I, ctypes.POINTER(_F), ctypes.POINTER(_I)]),
     "mea_profile_stage_name": (ctypes.c_char_p, [_I]),
