@@ -5,14 +5,18 @@
 // (fast_triton_attn.py:425-457) and, in the backward, the recompute gate
 // (fast_triton_attn.py:559-570).
 //
-// One CTA = one (b, h, 128-row query tile).  Warp 0 loads Q once and streams
-// K/V tiles through a ring with TMA; warp 1 issues S_j = Q K_j^T into one of
-// two TMEM score buffers and O += P_j V_j with P read straight from TMEM (the
-// softmax warps overwrite S_j with bf16 P_j in place); warps 2..5 run the
-// online softmax, one query row per thread.  The running max is refreshed
-// lazily: O and the row sum are rescaled only when a row's max grows by more
-// than 2^8, which keeps every P value <= 256.  Key tiles above the diagonal
-// are never loaded (causal skipping); the diagonal tile is masked.
+// One CTA = one (b, h, 128-row query tile), two CTAs per SM: each holds 256
+// TMEM columns (score tile S [0,128) and output O [128, 128+N)), so while one
+// CTA's softmax warps work on exponentials the other CTA's MMAs keep the
+// tensor core busy, and one CTA's prologue/epilogue overlaps the other's
+// main loop.  Warp 0 loads Q once and streams K and V through separate TMA
+// rings; warp 1 issues S_j = Q K_j^T and then O += P_j V_j with P read straight
+// from TMEM (the softmax warps overwrite S_j with bf16 P_j in place; S_{j+1}
+// is issued after PV_j, and tcgen05 MMAs of one thread run in issue order);
+// warps 2..5 run the online softmax, one query row per thread.  The running
+// max is refreshed lazily: O and the row sum are rescaled only when a row's max
+// grows by more than 2^8 (every P value stays <= 256).  Key tiles above the
+// diagonal are never loaded (causal skipping); the diagonal tile is masked.
 //
 // Outputs: gated[b, t, h*N + n] = (O/l)[n] * gs[b,h,t,n] (bf16), the row
 // log-sum-exp in log2 units lse2 = m + log2(l) (fp32, [B,H,T]), and
@@ -39,21 +43,19 @@ struct AttnFwdMaps {
 
 template <int HD>
 struct AttnFwdCfg {
-  static constexpr int STAGES = HD <= 64 ? 3 : 2;
+  static constexpr int KS = HD <= 64 ? 2 : 1;  // K ring depth
+  static constexpr int VS = HD <= 64 ? 2 : 1;  // V ring depth
   static constexpr uint32_t TILE_BYTES = 128 * HD * 2;
-  static constexpr uint32_t O_COL = 256;  // TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+HD)
-  static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr size_t SMEM_USED = 1024 + TILE_BYTES * (1 + 2 * STAGES) + 256;
-  // All 512 TMEM columns are taken, so ask for enough shared memory that a
-  // second CTA never lands on the same SM (it would only wait in tcgen05.alloc).
-  static constexpr size_t SMEM = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
+  static constexpr uint32_t S_COL = 0, O_COL = 128;
+  static constexpr uint32_t TMEM_COLS = 256;
+  static constexpr size_t SMEM = 1024 + TILE_BYTES * (1 + KS + VS) + 256;
 };
 
 template <int HD>
-__global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant__ AttnFwdMaps maps, const AttnFwdParams p) {
+__global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ AttnFwdMaps maps, const AttnFwdParams p) {
   using Cfg = AttnFwdCfg<HD>;
   using Tile = HeadTile<HD>;
-  constexpr int STAGES = Cfg::STAGES;
+  constexpr int KS = Cfg::KS, VS = Cfg::VS;
   constexpr uint32_t TB = Cfg::TILE_BYTES;
   constexpr uint32_t IDESC_S = idesc_bf16(128, 128, 0, 0);
   constexpr uint32_t IDESC_O = idesc_bf16(128, HD, 0, 1);
@@ -61,19 +63,20 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sQ = smem_u32(smem);
-  const uint32_t sK = sQ + TB;           // STAGES K tiles
-  const uint32_t sV = sK + STAGES * TB;  // STAGES V tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TB * (1 + 2 * STAGES));
+  const uint32_t sK = sQ + TB;       // KS K tiles
+  const uint32_t sV = sK + KS * TB;  // VS V tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TB * (1 + KS + VS));
   const uint32_t b0 = smem_u32(bars);
   const uint32_t q_full = b0;
   auto k_full = [&](int s) { return b0 + 8u * (1 + s); };
-  auto v_full = [&](int s) { return b0 + 8u * (1 + STAGES + s); };
-  auto kv_empty = [&](int s) { return b0 + 8u * (1 + 2 * STAGES + s); };
-  auto s_full = [&](int i) { return b0 + 8u * (1 + 3 * STAGES + i); };
-  auto p_full = [&](int i) { return b0 + 8u * (3 + 3 * STAGES + i); };
-  const uint32_t o_bar = b0 + 8u * (5 + 3 * STAGES);
-  const uint32_t drain_bar = b0 + 8u * (6 + 3 * STAGES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7 + 3 * STAGES);
+  auto k_empty = [&](int s) { return b0 + 8u * (1 + KS + s); };
+  auto v_full = [&](int s) { return b0 + 8u * (1 + 2 * KS + s); };
+  auto v_empty = [&](int s) { return b0 + 8u * (1 + 2 * KS + VS + s); };
+  const uint32_t s_full = b0 + 8u * (1 + 2 * KS + 2 * VS);
+  const uint32_t p_full = s_full + 8;
+  const uint32_t o_bar = s_full + 16;
+  const uint32_t drain_bar = s_full + 24;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5 + 2 * KS + 2 * VS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -86,15 +89,16 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < KS; ++s) {
       mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+    }
+    for (int s = 0; s < VS; ++s) {
       mbar_init(v_full(s), 1);
-      mbar_init(kv_empty(s), 1);
+      mbar_init(v_empty(s), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(s_full(i), 1);
-      mbar_init(p_full(i), 128);
-    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
     mbar_init(o_bar, 1);
     mbar_init(drain_bar, 1);
     fence_mbar_init();
@@ -119,63 +123,59 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
 #pragma unroll
       for (int c = 0; c < Tile::NCHUNK; ++c)
         tma_load_2d(sQ + c * 128 * Tile::SWB, &maps.q, q_full, c * Tile::CHUNK_ELEMS, row0 + qt * 128);
-      int last_par[STAGES];
-      for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
+      int kpar[KS], vpar[VS];
+      for (int s = 0; s < KS; ++s) kpar[s] = -1;
+      for (int s = 0; s < VS; ++s) vpar[s] = -1;
       for (int j = 0; j < nkv; ++j) {
-        const int s = j % STAGES;
-        const uint32_t ph = (j / STAGES) & 1;
-        if (!mbar_wait(kv_empty(s), ph ^ 1, g, 1)) break;
-        mbar_expect_tx(k_full(s), TB);
+        const int sk = j % KS, sv = j % VS;
+        const uint32_t pk = (j / KS) & 1, pv = (j / VS) & 1;
+        if (!mbar_wait(k_empty(sk), pk ^ 1, g, 1)) break;
+        mbar_expect_tx(k_full(sk), TB);
 #pragma unroll
         for (int c = 0; c < Tile::NCHUNK; ++c)
-          tma_load_2d(sK + s * TB + c * 128 * Tile::SWB, &maps.k, k_full(s), c * Tile::CHUNK_ELEMS, row0 + j * 128);
-        mbar_expect_tx(v_full(s), TB);
+          tma_load_2d(sK + sk * TB + c * 128 * Tile::SWB, &maps.k, k_full(sk), c * Tile::CHUNK_ELEMS, row0 + j * 128);
+        kpar[sk] = int(pk);
+        if (!mbar_wait(v_empty(sv), pv ^ 1, g, 9)) break;
+        mbar_expect_tx(v_full(sv), TB);
 #pragma unroll
         for (int c = 0; c < Tile::NCHUNK; ++c)
-          tma_load_2d(sV + s * TB + c * 128 * Tile::SWB, &maps.v, v_full(s), c * Tile::CHUNK_ELEMS, row0 + j * 128);
-        last_par[s] = int(ph);
+          tma_load_2d(sV + sv * TB + c * 128 * Tile::SWB, &maps.v, v_full(sv), c * Tile::CHUNK_ELEMS, row0 + j * 128);
+        vpar[sv] = int(pv);
       }
       if (!g.ok) {
         mbar_drain(q_full, 0);
-        for (int s = 0; s < STAGES; ++s)
-          if (last_par[s] >= 0) {
-            mbar_drain(k_full(s), uint32_t(last_par[s]));
-            mbar_drain(v_full(s), uint32_t(last_par[s]));
-          }
+        for (int s = 0; s < KS; ++s)
+          if (kpar[s] >= 0) mbar_drain(k_full(s), uint32_t(kpar[s]));
+        for (int s = 0; s < VS; ++s)
+          if (vpar[s] >= 0) mbar_drain(v_full(s), uint32_t(vpar[s]));
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (elect_one()) {
       bool any = false;
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i % STAGES;
-        if (!mbar_wait(p_full(i & 1), (i >> 1) & 1, g, 3)) return false;
-        if (!mbar_wait(v_full(s), (i / STAGES) & 1, g, 4)) return false;
-        tc_fence_after();
-        const uint32_t p_tmem = tmem + (i & 1) * 128;
-#pragma unroll
-        for (int kc = 0; kc < 8; ++kc)
-          mma_ts(tmem + Cfg::O_COL, p_tmem + kc * 8, Tile::mnmajor(sV + s * TB, 128, kc), IDESC_O,
-                 (i > 0 || kc > 0) ? 1u : 0u);
-        mma_commit(kv_empty(s));
-        mma_commit(o_bar);
-        return true;
-      };
       if (mbar_wait(q_full, 0, g, 5)) {
         for (int j = 0; j < nkv; ++j) {
-          const int s = j % STAGES;
-          if (!mbar_wait(k_full(s), (j / STAGES) & 1, g, 2)) break;
+          const int sk = j % KS, sv = j % VS;
+          if (!mbar_wait(k_full(sk), (j / KS) & 1, g, 2)) break;
           tc_fence_after();
-          const uint32_t s_tmem = tmem + (j & 1) * 128;
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk)
-            mma_ss(s_tmem, Tile::kmajor(sQ, 128, kk), Tile::kmajor(sK + s * TB, 128, kk), IDESC_S, kk > 0 ? 1u : 0u);
-          mma_commit(s_full(j & 1));
+            mma_ss(tmem + Cfg::S_COL, Tile::kmajor(sQ, 128, kk), Tile::kmajor(sK + sk * TB, 128, kk), IDESC_S,
+                   kk > 0 ? 1u : 0u);
+          mma_commit(k_empty(sk));
+          mma_commit(s_full);
           any = true;
-          if (j > 0 && !issue_pv(j - 1)) break;
+          if (!mbar_wait(p_full, j & 1, g, 3)) break;
+          if (!mbar_wait(v_full(sv), (j / VS) & 1, g, 4)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kc = 0; kc < 8; ++kc)
+            mma_ts(tmem + Cfg::O_COL, tmem + Cfg::S_COL + kc * 8, Tile::mnmajor(sV + sv * TB, 128, kc), IDESC_O,
+                   (j > 0 || kc > 0) ? 1u : 0u);
+          mma_commit(v_empty(sv));
         }
-        if (g.ok) issue_pv(nkv - 1);
+        if (g.ok) mma_commit(o_bar);
       }
       if (!g.ok && any) {
         mma_commit(drain_bar);
@@ -187,44 +187,37 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
-    float m_run = -INFINITY, l_run = 0.f;
+    const float sl2 = p.scale_log2;
+    float m_run = -INFINITY, l_run = 0.f;  // m_run in scaled log2 units
     bool ok = true;
     for (int j = 0; j < nkv && ok; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full(j & 1), (j >> 1) & 1, g, 6));
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, g, 6));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t sb = lane_base + (j & 1) * 128;
-      uint32_t sv[128];
+      const uint32_t sb = lane_base + Cfg::S_COL;
+      const bool diag = (j == qt);
+      // Pass 1: row max of the raw scores (S streamed from TMEM in 32-column chunks,
+      // four independent max chains).
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(sb + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sv[32 * c]));
-      tmem_ld_wait();
-      float mx = -INFINITY;
-      if (j == qt) {
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(sb + 32 * c, v);
+        tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          float x = __uint_as_float(sv[c]) * p.scale_log2;
-          x = c > r ? -INFINITY : x;
-          sv[c] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const float x = __uint_as_float(sv[c]) * p.scale_log2;
-          sv[c] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+        for (int e = 0; e < 32; ++e) {
+          const float x = (diag && 32 * c + e > r) ? -INFINITY : __uint_as_float(v[e]);
+          mx4[e & 3] = fmaxf(mx4[e & 3], x);
         }
       }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
       // Lazy rescale: refresh the reference max only when it grows by > 8 (log2 units).
       const bool need = mx > m_run + 8.0f;
       if (__any_sync(0xffffffffu, need)) {
         const float m_new = need ? mx : m_run;
         const float alpha = ex2(m_run - m_new);  // 0 when m_run = -inf
         if (j > 0) {
-          // O holds sum_{i<j} P_i V_i: wait for PV_{j-1}, then rescale this warp's rows.
-          ok = __all_sync(0xffffffffu, mbar_wait(o_bar, (j - 1) & 1, g, 7));
-          if (!ok) break;
-          tc_fence_after();
+          // s_full(j) completing means PV_{j-1} (issued before S_j) completed: O is stable.
 #pragma unroll
           for (int c = 0; c < HD; c += 16) {
             uint32_t ov[16];
@@ -238,27 +231,37 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
         l_run *= alpha;
         m_run = m_new;
       }
-      // P = exp2(s - m), row sum, pack to bf16 pairs and store into the S buffer.
-      float lsum = 0.f;
+      // Pass 2: P = exp2(s*c - m), row sum (four chains), pack to bf16 pairs, store over S.
+      const float neg_m = -m_run;
+      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(sb + 32 * c, v);
+        tmem_ld_wait();
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = ex2(__uint_as_float(sv[32 * c + 2 * e]) - m_run);
-          const float p1 = ex2(__uint_as_float(sv[32 * c + 2 * e + 1]) - m_run);
-          lsum += p0 + p1;
+          const int c0 = 32 * c + 2 * e;
+          float p0 = ex2(fmaf(__uint_as_float(v[2 * e]), sl2, neg_m));
+          float p1 = ex2(fmaf(__uint_as_float(v[2 * e + 1]), sl2, neg_m));
+          if (diag) {
+            p0 = c0 > r ? 0.f : p0;
+            p1 = c0 + 1 > r ? 0.f : p1;
+          }
+          ls4[(2 * e) & 3] += p0;
+          ls4[(2 * e + 1) & 3] += p1;
           pk[e] = pack_bf16(p0, p1);
         }
         tmem_st16(sb + 16 * c, pk);
       }
-      l_run += lsum;
+      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full(j & 1));
+      mbar_arrive(p_full);
     }
     // ---- epilogue: O / l, gate, repack ----
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_bar, (nkv - 1) & 1, g, 8));
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_bar, 0, g, 8));
     if (ok) {
       tc_fence_after();
       const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
