@@ -94,8 +94,12 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_kernel(const __grid_constant_
   const int lane = threadIdx.x & 31;
   const int BH = p.B * p.H;
   const int nq = p.T / 128;
-  const int jt = int(blockIdx.x) / BH;  // key tile; the longest walks (small jt) launch first
-  const int bh = int(blockIdx.x) % BH;
+  // Head-major order: the key tiles of one (b,h) run side by side, so their dQ
+  // reductions land in the same L2-resident rows; the longest walks (small jt)
+  // start first within a head.
+  const int bh = int(blockIdx.x) / nq;
+  const int jt = int(blockIdx.x) % nq;
+  (void)BH;
   const int nsteps = nq - jt;
   const int row0 = bh * p.T;
 

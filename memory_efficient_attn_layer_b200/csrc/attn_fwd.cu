@@ -51,6 +51,62 @@ struct AttnFwdCfg {
   static constexpr size_t SMEM = 1024 + TILE_BYTES * (1 + KS + VS) + 256;
 };
 
+// Row max of one 128-column score row held in TMEM (raw, unscaled scores).
+// DIAG: the diagonal tile, where key column c > query row r is masked out.
+template <bool DIAG>
+__device__ __forceinline__ float score_row_max(uint32_t sb, int r) {
+  float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t v[32];
+    tmem_ld32(sb + 32 * c, v);
+    tmem_ld_wait();
+    float x[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) x[e] = (DIAG && 32 * c + e > r) ? -INFINITY : __uint_as_float(v[e]);
+#pragma unroll
+    for (int e = 0; e < 32; e += 8) {
+      m0 = max3f(m0, x[e], x[e + 1]);
+      m1 = max3f(m1, x[e + 2], x[e + 3]);
+      m2 = max3f(m2, x[e + 4], x[e + 5]);
+      m3 = max3f(m3, x[e + 6], x[e + 7]);
+    }
+  }
+  return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+}
+
+// P = exp2(s * sl2 - m) for one row: written back over the scores as packed
+// bf16 pairs (columns [0, 64) of the S buffer); returns the row sum of P.
+template <bool DIAG>
+__device__ __forceinline__ float exp_pack_row(uint32_t sb, int r, float sl2, float neg_m) {
+  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+  const float2 scale2 = make_float2(sl2, sl2), bias2 = make_float2(neg_m, neg_m);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t v[32];
+    tmem_ld32(sb + 32 * c, v);
+    tmem_ld_wait();
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float2 t = ffma2(make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), scale2, bias2);
+      float p0 = ex2(t.x), p1 = ex2(t.y);
+      if (DIAG) {
+        const int c0 = 32 * c + 2 * e;
+        p0 = c0 > r ? 0.f : p0;
+        p1 = c0 + 1 > r ? 0.f : p1;
+      }
+      if (e & 1)
+        acc1 = fadd2(acc1, make_float2(p0, p1));
+      else
+        acc0 = fadd2(acc0, make_float2(p0, p1));
+      pk[e] = pack_bf16(p0, p1);
+    }
+    tmem_st16(sb + 16 * c, pk);
+  }
+  return (acc0.x + acc0.y) + (acc1.x + acc1.y);
+}
+
 template <int HD>
 __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ AttnFwdMaps maps, const AttnFwdParams p) {
   using Cfg = AttnFwdCfg<HD>;
@@ -82,8 +138,11 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
   const int lane = threadIdx.x & 31;
   const int BH = p.B * p.H;
   const int nq = p.T / 128;
-  const int qt = nq - 1 - int(blockIdx.x) / BH;  // heaviest query tiles first
-  const int bh = int(blockIdx.x) % BH;
+  // Head-major order: the query tiles of one (b,h) run side by side and share its
+  // K/V in L2; within a head the longest (diagonal-most) tiles start first.
+  const int bh = int(blockIdx.x) / nq;
+  const int qt = nq - 1 - int(blockIdx.x) % nq;
+  (void)BH;
   const int nkv = qt + 1;
   const int row0 = bh * p.T;  // first row of this (b,h) in the [B*H*T, HD] view
 
@@ -196,21 +255,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       tc_fence_after();
       const uint32_t sb = lane_base + Cfg::S_COL;
       const bool diag = (j == qt);
-      // Pass 1: row max of the raw scores (S streamed from TMEM in 32-column chunks,
-      // four independent max chains).
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(sb + 32 * c, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float x = (diag && 32 * c + e > r) ? -INFINITY : __uint_as_float(v[e]);
-          mx4[e & 3] = fmaxf(mx4[e & 3], x);
-        }
-      }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+      const float mx = (diag ? score_row_max<true>(sb, r) : score_row_max<false>(sb, r)) * sl2;
       // Lazy rescale: refresh the reference max only when it grows by > 8 (log2 units).
       const bool need = mx > m_run + 8.0f;
       if (__any_sync(0xffffffffu, need)) {
@@ -231,31 +276,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         l_run *= alpha;
         m_run = m_new;
       }
-      // Pass 2: P = exp2(s*c - m), row sum (four chains), pack to bf16 pairs, store over S.
-      const float neg_m = -m_run;
-      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(sb + 32 * c, v);
-        tmem_ld_wait();
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int c0 = 32 * c + 2 * e;
-          float p0 = ex2(fmaf(__uint_as_float(v[2 * e]), sl2, neg_m));
-          float p1 = ex2(fmaf(__uint_as_float(v[2 * e + 1]), sl2, neg_m));
-          if (diag) {
-            p0 = c0 > r ? 0.f : p0;
-            p1 = c0 + 1 > r ? 0.f : p1;
-          }
-          ls4[(2 * e) & 3] += p0;
-          ls4[(2 * e + 1) & 3] += p1;
-          pk[e] = pack_bf16(p0, p1);
-        }
-        tmem_st16(sb + 16 * c, pk);
-      }
-      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+      // P = exp2(s*c - m), its row sum, and bf16 P written over S for the PV MMA.
+      l_run += diag ? exp_pack_row<true>(sb, r, sl2, -m_run) : exp_pack_row<false>(sb, r, sl2, -m_run);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full);
