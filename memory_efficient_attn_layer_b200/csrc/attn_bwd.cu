@@ -5,19 +5,28 @@
 // saved row log-sum-exp (log2 units) and delta = rowsum(dO * O).
 //
 // One CTA = one (b, h, 128-row key tile); it walks the query tiles from the
-// diagonal to the end (causal skipping).  Per query tile:
-//   S^T  = K Q^T,  dP^T = V dO^T                     (tcgen05, TMEM)
-//   P^T  = exp2(S^T*c - lse2),  dS^T = P^T (dP^T - delta)   (compute warps)
-//   dV  += P^T dO      (P^T read from TMEM, written there over S^T)
-//   dK  += dS^T Q      (dS^T staged once in swizzled shared memory ...)
-//   dQ   = dS K        (... and read back as an MN-major operand)
-// dK and dV stay in TMEM for the whole walk; each dQ tile is added into an
-// fp32 accumulator in global memory ([B,H,T,N], zeroed by the caller).
+// diagonal to the end (causal skipping).  Per query tile i:
+//   S  = Q_i K^T,  dP = dO_i V^T         (tcgen05 into TMEM, one query row per lane)
+//   P  = exp2(S*c - lse2),  dS = P (dP - delta)     (softmax warps; lse2 and delta
+//                                                     are per-thread scalars)
+//   dV += P^T dO_i   (P staged in swizzled shared memory, read MN-major)
+//   dK += dS^T Q_i   (dS staged in shared memory, read MN-major)
+//   dQ_i = dS K      (dS also written to TMEM as packed bf16: A operand from TMEM)
+// dK and dV stay in TMEM for the whole walk.  A separate read-out warpgroup
+// adds each dQ_i tile (fp32) into the accumulator in global memory ([B,H,T,N],
+// zeroed by the caller) and finally writes dK and dV.
 //
-// TMEM columns: S^T [0,128), dP^T [128,256), dK [256,256+N), dV [256+N,256+2N),
-// dQ [256+2N, 256+3N) for N <= 64; for N = 128 dQ reuses the dP^T columns
-// (dP^T is fully read before dQ is written; the next dP^T waits for the dQ
-// read-out).
+// Warps: 0 TMA, 1 MMA issue, 2..5 softmax (query row = TMEM lane), 6..9 dQ
+// read-out + epilogue.
+//
+// Schedules (TMEM has 512 columns):
+//  * N <= 64 ("overlapped"): S [0,128), dP [128,256), dS [256,320), dV, dK, dQ
+//    after it.  As soon as the softmax warps have read S_i and dP_i, the MMA
+//    warp issues S_{i+1}, dP_{i+1} and only then dV_i, dK_i, dQ_i, so the next
+//    tile's exponentials overlap this tile's gradient MMAs.
+//  * N = 128 ("serial"): S [0,128) (dS written over it), dP [128,256) (dQ written
+//    over it after dP is read), dV [256,384), dK [384,512); S_{i+1} is issued
+//    after dQ_i, and dP_{i+1} after the read-out of dQ_i.
 #include "attn_common.cuh"
 #include "launch.h"
 #include "tma.h"
@@ -30,9 +39,9 @@ struct AttnBwdParams {
   float scale_log2;  // scale * log2(e)
   const float* lse2;
   const float* delta;
-  float* dq_acc;           // [B,H,T,N] fp32, accumulated
-  __nv_bfloat16* dk;       // [B,H,T,N]
-  __nv_bfloat16* dv;       // dv[(b*T + t)*ld_dv + h*N + n]
+  float* dq_acc;      // [B,H,T,N] fp32, accumulated
+  __nv_bfloat16* dk;  // [B,H,T,N]
+  __nv_bfloat16* dv;  // dv[(b*T + t)*ld_dv + h*N + n]
   long long ld_dv;
   int* status;
 };
@@ -43,32 +52,54 @@ struct AttnBwdMaps {
 
 template <int HD>
 struct AttnBwdCfg {
-  static constexpr int STAGES = HD <= 64 ? 2 : 1;
-  static constexpr bool DQ_ALIAS = HD > 64;
+  static constexpr bool OVERLAP = HD <= 64;
+  static constexpr int STAGES = HD <= 64 ? 2 : 1;  // Q/dO ring depth
   static constexpr uint32_t TB = 128 * HD * 2;
-  static constexpr uint32_t DS_BYTES = 128 * 128 * 2;
-  static constexpr uint32_t DK_COL = 256, DV_COL = 256 + HD;
-  static constexpr uint32_t DQ_COL = DQ_ALIAS ? 128 : 256 + 2 * HD;
+  static constexpr uint32_t PT = 128 * 128 * 2;  // one bf16 [128 x 128] P or dS tile
+  static constexpr uint32_t S_COL = 0, DP_COL = 128;
+  static constexpr uint32_t DS_COL = OVERLAP ? 256 : 0;
+  static constexpr uint32_t DV_COL = OVERLAP ? 320 : 256;
+  static constexpr uint32_t DK_COL = DV_COL + HD;
+  static constexpr uint32_t DQ_COL = OVERLAP ? DK_COL + HD : DP_COL;
   static constexpr uint32_t TMEM_COLS = 512;
-  // K, V, STAGES x (Q, dO), dS^T, then STAGES x (lse, delta), barriers
+  static_assert(!OVERLAP || DQ_COL + HD <= 512, "TMEM budget");
   static constexpr uint32_t OFF_K = 0, OFF_V = TB, OFF_Q = 2 * TB, OFF_DO = OFF_Q + STAGES * TB;
-  static constexpr uint32_t OFF_DS = OFF_DO + STAGES * TB;
-  static constexpr uint32_t OFF_LSE = OFF_DS + DS_BYTES;
+  static constexpr uint32_t OFF_P = OFF_DO + STAGES * TB, OFF_DS = OFF_P + PT;
+  static constexpr uint32_t OFF_LSE = OFF_DS + PT;
   static constexpr uint32_t OFF_BAR = OFF_LSE + STAGES * 1024;
-  static constexpr size_t SMEM_USED = 1024 + OFF_BAR + 256;
-  // One CTA per SM: all 512 TMEM columns are allocated.
-  static constexpr size_t SMEM = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
+  static constexpr size_t SMEM = 1024 + OFF_BAR + 256;
 };
 
+// MN-major descriptor of a [128 q rows x 128 kv] bf16 tile stored as two
+// 64-column chunks (16 KB apart) of 128-byte swizzled rows; k-step of 16 rows.
+__device__ __forceinline__ uint64_t ptile_mn(uint32_t base, int kc) {
+  return smem_desc(base + kc * 2048, 16384, 1024, SW_128B);
+}
+
+// Store 16 packed bf16 pairs of row r, key columns [32c, 32c+32), into a
+// [128 x 128] tile with the swizzle the MN-major descriptor expects.
+__device__ __forceinline__ void st_tile_row(uint32_t tile, int r, int c, const uint32_t (&w)[16]) {
+  const uint32_t row_addr = tile + (c >> 1) * 16384 + r * 128;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int lu = (c & 1) * 4 + u;
+    const uint32_t addr = row_addr + ((lu ^ (r & 7)) << 4);
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(w[4 * u]), "r"(w[4 * u + 1]),
+                 "r"(w[4 * u + 2]), "r"(w[4 * u + 3])
+                 : "memory");
+  }
+}
+
 template <int HD>
-__global__ void __launch_bounds__(192, 1) attn_bwd_kernel(const __grid_constant__ AttnBwdMaps maps, const AttnBwdParams p) {
+__global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant__ AttnBwdMaps maps, const AttnBwdParams p) {
   using Cfg = AttnBwdCfg<HD>;
   using Tile = HeadTile<HD>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t TB = Cfg::TB;
-  constexpr uint32_t IDESC_SS = idesc_bf16(128, 128, 0, 0);   // S^T, dP^T
-  constexpr uint32_t IDESC_KV = idesc_bf16(128, HD, 0, 1);    // dV (A from TMEM), dK (A K-major)
-  constexpr uint32_t IDESC_DQ = idesc_bf16(128, HD, 1, 1);    // dQ (A = dS, MN-major)
+  constexpr bool OVERLAP = Cfg::OVERLAP;
+  constexpr uint32_t IDESC_SS = idesc_bf16(128, 128, 0, 0);  // S, dP
+  constexpr uint32_t IDESC_KV = idesc_bf16(128, HD, 1, 1);   // dV, dK: A (P^T / dS^T) and B MN-major
+  constexpr uint32_t IDESC_DQ = idesc_bf16(128, HD, 0, 1);   // dQ: A = dS from TMEM
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -76,7 +107,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_kernel(const __grid_constant_
   const uint32_t sK = base + Cfg::OFF_K, sV = base + Cfg::OFF_V;
   auto sQ = [&](int s) { return base + Cfg::OFF_Q + s * TB; };
   auto sdO = [&](int s) { return base + Cfg::OFF_DO + s * TB; };
-  const uint32_t sdS = base + Cfg::OFF_DS;
+  const uint32_t sP = base + Cfg::OFF_P, sDS = base + Cfg::OFF_DS;
   float* lse_s = reinterpret_cast<float*>(smem + Cfg::OFF_LSE);  // [STAGES][2][128]: lse2, delta
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
   const uint32_t b0 = smem_u32(bars);
@@ -92,14 +123,12 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_kernel(const __grid_constant_
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int BH = p.B * p.H;
   const int nq = p.T / 128;
   // Head-major order: the key tiles of one (b,h) run side by side, so their dQ
   // reductions land in the same L2-resident rows; the longest walks (small jt)
   // start first within a head.
   const int bh = int(blockIdx.x) / nq;
   const int jt = int(blockIdx.x) % nq;
-  (void)BH;
   const int nsteps = nq - jt;
   const int row0 = bh * p.T;
 
@@ -167,46 +196,53 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_kernel(const __grid_constant_
     // ---------------- MMA issuer ----------------
     if (elect_one()) {
       bool any = false;
-      if (mbar_wait(kv_full, 0, g, 2)) {
+      // S_n = Q_n K^T and dP_n = dO_n V^T, committed together to st_full.
+      auto issue_sdp = [&](int n) -> bool {
+        const int s = n % STAGES;
+        if (!mbar_wait(qdo_full(s), (n / STAGES) & 1, g, 3)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          mma_ss(tmem + Cfg::S_COL, Tile::kmajor(sQ(s), 128, kk), Tile::kmajor(sK, 128, kk), IDESC_SS, kk > 0 ? 1u : 0u);
+        if (!OVERLAP && n > 0) {  // dP's columns held dQ_{n-1}: wait for its read-out
+          if (!mbar_wait(dq_empty, (n - 1) & 1, g, 4)) return false;
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          mma_ss(tmem + Cfg::DP_COL, Tile::kmajor(sdO(s), 128, kk), Tile::kmajor(sV, 128, kk), IDESC_SS,
+                 kk > 0 ? 1u : 0u);
+        mma_commit(st_full);
+        any = true;
+        return true;
+      };
+      if (mbar_wait(kv_full, 0, g, 2) && issue_sdp(0)) {
         for (int n = 0; n < nsteps; ++n) {
           const int s = n % STAGES;
-          if (!mbar_wait(qdo_full(s), (n / STAGES) & 1, g, 3)) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk)
-            mma_ss(tmem, Tile::kmajor(sK, 128, kk), Tile::kmajor(sQ(s), 128, kk), IDESC_SS, kk > 0 ? 1u : 0u);
-          any = true;
-          if (Cfg::DQ_ALIAS && n > 0) {
-            if (!mbar_wait(dq_empty, (n - 1) & 1, g, 4)) break;
-            tc_fence_after();
-          }
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk)
-            mma_ss(tmem + 128, Tile::kmajor(sV, 128, kk), Tile::kmajor(sdO(s), 128, kk), IDESC_SS, kk > 0 ? 1u : 0u);
-          mma_commit(st_full);
           if (!mbar_wait(ds_full, n & 1, g, 5)) break;
           tc_fence_after();
-          // dV += P^T dO  (P^T from TMEM columns [0, 64) as packed bf16)
+          if (OVERLAP && n + 1 < nsteps && !issue_sdp(n + 1)) break;
+          // dV += P^T dO_n ; dK += dS^T Q_n  (A operands MN-major from shared memory)
 #pragma unroll
           for (int kc = 0; kc < 8; ++kc)
-            mma_ts(tmem + Cfg::DV_COL, tmem + kc * 8, Tile::mnmajor(sdO(s), 128, kc), IDESC_KV,
+            mma_ss(tmem + Cfg::DV_COL, ptile_mn(sP, kc), Tile::mnmajor(sdO(s), 128, kc), IDESC_KV,
                    (n > 0 || kc > 0) ? 1u : 0u);
-          // dK += dS^T Q  (dS^T K-major over the query index)
 #pragma unroll
           for (int kc = 0; kc < 8; ++kc)
-            mma_ss(tmem + Cfg::DK_COL, smem_desc(sdS + (kc >> 2) * 16384 + (kc & 3) * 32, 16, 1024, SW_128B),
-                   Tile::mnmajor(sQ(s), 128, kc), IDESC_KV, (n > 0 || kc > 0) ? 1u : 0u);
-          if (!Cfg::DQ_ALIAS && n > 0) {
+            mma_ss(tmem + Cfg::DK_COL, ptile_mn(sDS, kc), Tile::mnmajor(sQ(s), 128, kc), IDESC_KV,
+                   (n > 0 || kc > 0) ? 1u : 0u);
+          if (OVERLAP && n > 0) {
             if (!mbar_wait(dq_empty, (n - 1) & 1, g, 6)) break;
             tc_fence_after();
           }
-          // dQ = dS K  (dS read MN-major from the same shared-memory tile)
+          // dQ_n = dS K  (dS from TMEM, packed bf16)
 #pragma unroll
           for (int kc = 0; kc < 8; ++kc)
-            mma_ss(tmem + Cfg::DQ_COL, smem_desc(sdS + kc * 2048, 16384, 1024, SW_128B), Tile::mnmajor(sK, 128, kc),
-                   IDESC_DQ, kc > 0 ? 1u : 0u);
+            mma_ts(tmem + Cfg::DQ_COL, tmem + Cfg::DS_COL + kc * 8, Tile::mnmajor(sK, 128, kc), IDESC_DQ,
+                   kc > 0 ? 1u : 0u);
           mma_commit(qdo_empty(s));
           mma_commit(dq_full);
+          if (!OVERLAP && n + 1 < nsteps && !issue_sdp(n + 1)) break;
         }
       }
       if (!g.ok && any) {
@@ -214,69 +250,73 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_kernel(const __grid_constant_
         mbar_drain(drain_bar, 0);
       }
     }
-  } else {
-    // ---------------- compute warps 2..5 ----------------
+  } else if (warp < 6) {
+    // ---------------- softmax warps 2..5: query row r of each tile ----------------
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // key row (S^T, dK, dV) / query row (dQ)
+    const int r = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+    const float sl2 = p.scale_log2;
     bool ok = true;
     for (int n = 0; n < nsteps; ++n) {
       const int s = n % STAGES;
-      const int qi = jt + n;
       ok = mbar_wait(qdo_full(s), (n / STAGES) & 1, g, 7);
       ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, n & 1, g, 8));
       if (!ok) break;
+      if (n > 0) {  // P/dS tiles and the dS TMEM columns are free once step n-1's MMAs are done
+        ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (n - 1) & 1, g, 10));
+        if (!ok) break;
+      }
       tc_fence_after();
-      const float* lse = lse_s + s * 256;
-      const float* dl = lse + 128;
+      const float neg_lse = -lse_s[s * 256 + r];
+      const float dl = lse_s[s * 256 + 128 + r];
       const bool diag = (n == 0);
+      const float2 scale2 = make_float2(sl2, sl2), bias2 = make_float2(neg_lse, neg_lse);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t sv[32], dp[32];
-        tmem_ld32(lane_base + 32 * c, sv);
-        tmem_ld32(lane_base + 128 + 32 * c, dp);
-        tmem_ld_wait();
-        uint32_t pk[16], dsp[16];
+        tmem_ld32(lane_base + Cfg::S_COL + 32 * c, sv);
+        tmem_load32(lane_base + Cfg::DP_COL + 32 * c, dp);
+        tmem_wait_ld_tied(sv);
+        uint32_t pk[16], dsk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          float pv[2], dsv[2];
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            const int col = 32 * c + 2 * e + h2;
-            float pr = ex2(__uint_as_float(sv[2 * e + h2]) * p.scale_log2 - lse[col]);
-            if (diag && col < r) pr = 0.f;
-            pv[h2] = pr;
-            dsv[h2] = pr * (__uint_as_float(dp[2 * e + h2]) - dl[col]);
+          const float2 t = ffma2(make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), scale2, bias2);
+          float p0 = ex2(t.x), p1 = ex2(t.y);
+          if (diag) {  // key column > query row: masked
+            const int c0 = 32 * c + 2 * e;
+            p0 = c0 > r ? 0.f : p0;
+            p1 = c0 + 1 > r ? 0.f : p1;
           }
-          pk[e] = pack_bf16(pv[0], pv[1]);
-          dsp[e] = pack_bf16(dsv[0], dsv[1]);
+          const float ds0 = p0 * (__uint_as_float(dp[2 * e]) - dl);
+          const float ds1 = p1 * (__uint_as_float(dp[2 * e + 1]) - dl);
+          pk[e] = pack_bf16(p0, p1);
+          dsk[e] = pack_bf16(ds0, ds1);
         }
-        tmem_st16(lane_base + 16 * c, pk);
-        // dS^T row r, query columns [32c, 32c+32): 4 16-byte units of chunk c/2, swizzled.
-        const uint32_t row_addr = sdS + (c >> 1) * 16384 + r * 128;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int lu = (c & 1) * 4 + u;
-          const uint32_t addr = row_addr + ((lu ^ (r & 7)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(dsp[4 * u]), "r"(dsp[4 * u + 1]),
-                       "r"(dsp[4 * u + 2]), "r"(dsp[4 * u + 3])
-                       : "memory");
-        }
+        st_tile_row(sP, r, c, pk);
+        st_tile_row(sDS, r, c, dsk);
+        tmem_st16(lane_base + Cfg::DS_COL + 16 * c, dsk);
       }
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
-      // dQ read-out: this thread owns query row r of tile qi.
+    }
+    if (!ok) g.ok = false;
+  } else {
+    // ---------------- read-out warps 6..9: dQ tiles, then dK and dV ----------------
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+    bool ok = true;
+    for (int n = 0; n < nsteps; ++n) {
       ok = __all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, g, 9));
       if (!ok) break;
       tc_fence_after();
-      float* dqrow = p.dq_acc + (size_t(row0) + size_t(qi) * 128 + r) * HD;
+      float* dqrow = p.dq_acc + (size_t(row0) + size_t(jt + n) * 128 + r) * HD;
 #pragma unroll
       for (int c = 0; c < HD; c += 32) {
         uint32_t v[32];
-        tmem_ld32(lane_base + Cfg::DQ_COL + c, v);
-        tmem_ld_wait();
+        tmem_load32(lane_base + Cfg::DQ_COL + c, v);
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           red_add_v4_f32(dqrow + c + 4 * j, __uint_as_float(v[4 * j]) * p.scale, __uint_as_float(v[4 * j + 1]) * p.scale,
@@ -285,7 +325,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_kernel(const __grid_constant_
       tc_fence_before();
       mbar_arrive(dq_empty);
     }
-    // ---- epilogue: dK (scaled) and dV for key row r ----
+    // dK (scaled) and dV for key row r: every MMA completed with the last dq_full.
     if (ok) {
       const int b = bh / p.H, h = bh - b * p.H;
       const int t = jt * 128 + r;
@@ -294,9 +334,8 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_kernel(const __grid_constant_
 #pragma unroll
       for (int c = 0; c < HD; c += 32) {
         uint32_t a[32], v[32];
-        tmem_ld32(lane_base + Cfg::DK_COL + c, a);
-        tmem_ld32(lane_base + Cfg::DV_COL + c, v);
-        tmem_ld_wait();
+        tmem_load32(lane_base + Cfg::DK_COL + c, a);
+        tmem_load32(lane_base + Cfg::DV_COL + c, v);
         uint32_t pa[16], pv[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -330,7 +369,7 @@ static int launch_attn_bwd_t(const AttnBwdMaps& maps, const AttnBwdParams& p, cu
   if (!smem_attr_set(reinterpret_cast<const void*>(kern), int(Cfg::SMEM)))
     return set_error(MEA_ERR_CUDA, "cudaFuncSetAttribute(attn_bwd) failed");
   const int grid = p.B * p.H * (p.T / 128);
-  kern<<<grid, 192, Cfg::SMEM, st>>>(maps, p);
+  kern<<<grid, 320, Cfg::SMEM, st>>>(maps, p);
   return check_launch("attn_bwd_kernel");
 }
 

@@ -59,8 +59,7 @@ __device__ __forceinline__ float score_row_max(uint32_t sb, int r) {
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     uint32_t v[32];
-    tmem_ld32(sb + 32 * c, v);
-    tmem_ld_wait();
+    tmem_load32(sb + 32 * c, v);
     float x[32];
 #pragma unroll
     for (int e = 0; e < 32; ++e) x[e] = (DIAG && 32 * c + e > r) ? -INFINITY : __uint_as_float(v[e]);
@@ -84,8 +83,7 @@ __device__ __forceinline__ float exp_pack_row(uint32_t sb, int r, float sl2, flo
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     uint32_t v[32];
-    tmem_ld32(sb + 32 * c, v);
-    tmem_ld_wait();
+    tmem_load32(sb + 32 * c, v);
     uint32_t pk[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
@@ -266,8 +264,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
 #pragma unroll
           for (int c = 0; c < HD; c += 16) {
             uint32_t ov[16];
-            tmem_ld16(lane_base + Cfg::O_COL + c, ov);
-            tmem_ld_wait();
+            tmem_load16(lane_base + Cfg::O_COL + c, ov);
 #pragma unroll
             for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
             tmem_st16(lane_base + Cfg::O_COL + c, ov);
@@ -296,8 +293,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
 #pragma unroll
       for (int c = 0; c < HD; c += 16) {
         uint32_t ov[16];
-        tmem_ld16(lane_base + Cfg::O_COL + c, ov);
-        tmem_ld_wait();
+        tmem_load16(lane_base + Cfg::O_COL + c, ov);
         const uint4 g0 = *reinterpret_cast<const uint4*>(gsrow + c);
         const uint4 g1 = *reinterpret_cast<const uint4*>(gsrow + c + 8);
         const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};

@@ -93,8 +93,7 @@ template <int BN>
 __device__ __forceinline__ void epi_store(const GemmParams& p, int mode, uint32_t taddr, int m, int n0) {
   for (int c = 0; c < BN; c += 32) {
     uint32_t r[32];
-    tmem_ld32(taddr + c, r);
-    tmem_ld_wait();
+    tmem_load32(taddr + c, r);
     if (mode == EPI_BF16) {
       __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(m) * p.ldo + n0 + c;
 #pragma unroll
@@ -140,8 +139,7 @@ __device__ __forceinline__ void epi_qkvg(const GemmParams& p, uint32_t taddr, in
       float ss = 0.f;
       for (int c = 0; c < hd; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tcol + c, r);
-        tmem_ld_wait();
+        tmem_load32(tcol + c, r);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float v = __uint_as_float(r[j]) * rs;
@@ -155,8 +153,7 @@ __device__ __forceinline__ void epi_qkvg(const GemmParams& p, uint32_t taddr, in
       const float sc = rs * inv;
       for (int c = 0; c < hd; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tcol + c, r);
-        tmem_ld_wait();
+        tmem_load32(tcol + c, r);
         uint32_t pk[16];
 #pragma unroll
         for (int v4 = 0; v4 < 4; ++v4) {
@@ -181,8 +178,7 @@ __device__ __forceinline__ void epi_qkvg(const GemmParams& p, uint32_t taddr, in
       __nv_bfloat16* dst = (typ == 2 ? p.v : p.g) + bht * hd;
       for (int c = 0; c < hd; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tcol + c, r);
-        tmem_ld_wait();
+        tmem_load32(tcol + c, r);
         uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -221,8 +217,7 @@ __device__ __forceinline__ void epi_dgate(const GemmParams& p, uint32_t taddr, i
     float dsum = 0.f;
     for (int c = 0; c < hd; c += 32) {
       uint32_t r[32];
-      tmem_ld32(taddr + s * hd + c, r);
-      tmem_ld_wait();
+      tmem_load32(taddr + s * hd + c, r);
       uint32_t pd[16], pg[16];
 #pragma unroll
       for (int v4 = 0; v4 < 4; ++v4) {
