@@ -76,17 +76,60 @@ __device__ __forceinline__ uint64_t ptile_mn(uint32_t base, int kc) {
   return smem_desc(base + kc * 2048, 16384, 1024, SW_128B);
 }
 
-// Store 16 packed bf16 pairs of row r, key columns [32c, 32c+32), into a
+// Store 8 packed bf16 pairs of row r, key columns [16c, 16c+16), into a
 // [128 x 128] tile with the swizzle the MN-major descriptor expects.
-__device__ __forceinline__ void st_tile_row(uint32_t tile, int r, int c, const uint32_t (&w)[16]) {
-  const uint32_t row_addr = tile + (c >> 1) * 16384 + r * 128;
+__device__ __forceinline__ void st_tile_row16(uint32_t tile, int r, int c, const uint32_t* w) {
+  const uint32_t row_addr = tile + (c >> 2) * 16384 + r * 128;
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int lu = (c & 1) * 4 + u;
+  for (int u = 0; u < 2; ++u) {
+    const int lu = (c & 3) * 2 + u;
     const uint32_t addr = row_addr + ((lu ^ (r & 7)) << 4);
     asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(w[4 * u]), "r"(w[4 * u + 1]),
                  "r"(w[4 * u + 2]), "r"(w[4 * u + 3])
                  : "memory");
+  }
+}
+
+// P and dS for 16 key columns [16c, 16c+16) of query row r.
+template <bool DIAG>
+__device__ __forceinline__ void bwd_chunk(const uint32_t (&sv)[16], const uint32_t (&dp)[16], int c, int r, float2 scale2,
+                                          float2 bias2, float dl, uint32_t (&pk)[64], uint32_t (&dsk)[64]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float2 t = ffma2(make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), scale2, bias2);
+    float p0 = ex2(t.x), p1 = ex2(t.y);
+    if (DIAG) {  // key column > query row: masked
+      const int c0 = 16 * c + 2 * e;
+      p0 = c0 > r ? 0.f : p0;
+      p1 = c0 + 1 > r ? 0.f : p1;
+    }
+    pk[8 * c + e] = pack_bf16(p0, p1);
+    dsk[8 * c + e] = pack_bf16(p0 * (__uint_as_float(dp[2 * e]) - dl), p1 * (__uint_as_float(dp[2 * e + 1]) - dl));
+  }
+}
+
+// Whole 128-column row: S and dP stream out of TMEM in 16-column chunks, the
+// next chunk's loads in flight while the current chunk is computed.
+template <bool DIAG>
+__device__ __forceinline__ void bwd_row(uint32_t s_addr, uint32_t dp_addr, int r, float sl2, float neg_lse, float dl,
+                                        uint32_t (&pk)[64], uint32_t (&dsk)[64]) {
+  const float2 scale2 = make_float2(sl2, sl2), bias2 = make_float2(neg_lse, neg_lse);
+  uint32_t s0[16], d0[16], s1[16], d1[16];
+  tmem_ld16(s_addr, s0);
+  tmem_ld16(dp_addr, d0);
+  tmem_wait_ld_tied2(s0, d0);
+#pragma unroll
+  for (int c = 0; c < 8; c += 2) {
+    tmem_ld16(s_addr + 16 * (c + 1), s1);
+    tmem_ld16(dp_addr + 16 * (c + 1), d1);
+    bwd_chunk<DIAG>(s0, d0, c, r, scale2, bias2, dl, pk, dsk);
+    tmem_wait_ld_tied2(s1, d1);
+    if (c + 2 < 8) {
+      tmem_ld16(s_addr + 16 * (c + 2), s0);
+      tmem_ld16(dp_addr + 16 * (c + 2), d0);
+    }
+    bwd_chunk<DIAG>(s1, d1, c + 1, r, scale2, bias2, dl, pk, dsk);
+    if (c + 2 < 8) tmem_wait_ld_tied2(s0, d0);
   }
 }
 
@@ -262,40 +305,26 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
       ok = mbar_wait(qdo_full(s), (n / STAGES) & 1, g, 7);
       ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, n & 1, g, 8));
       if (!ok) break;
-      if (n > 0) {  // P/dS tiles and the dS TMEM columns are free once step n-1's MMAs are done
-        ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (n - 1) & 1, g, 10));
-        if (!ok) break;
-      }
       tc_fence_after();
       const float neg_lse = -lse_s[s * 256 + r];
       const float dl = lse_s[s * 256 + 128 + r];
-      const bool diag = (n == 0);
-      const float2 scale2 = make_float2(sl2, sl2), bias2 = make_float2(neg_lse, neg_lse);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dp[32];
-        tmem_ld32(lane_base + Cfg::S_COL + 32 * c, sv);
-        tmem_load32(lane_base + Cfg::DP_COL + 32 * c, dp);
-        tmem_wait_ld_tied(sv);
-        uint32_t pk[16], dsk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float2 t = ffma2(make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), scale2, bias2);
-          float p0 = ex2(t.x), p1 = ex2(t.y);
-          if (diag) {  // key column > query row: masked
-            const int c0 = 32 * c + 2 * e;
-            p0 = c0 > r ? 0.f : p0;
-            p1 = c0 + 1 > r ? 0.f : p1;
-          }
-          const float ds0 = p0 * (__uint_as_float(dp[2 * e]) - dl);
-          const float ds1 = p1 * (__uint_as_float(dp[2 * e + 1]) - dl);
-          pk[e] = pack_bf16(p0, p1);
-          dsk[e] = pack_bf16(ds0, ds1);
-        }
-        st_tile_row(sP, r, c, pk);
-        st_tile_row(sDS, r, c, dsk);
-        tmem_st16(lane_base + Cfg::DS_COL + 16 * c, dsk);
+      uint32_t pk[64], dsk[64];
+      if (n == 0)
+        bwd_row<true>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, r, sl2, neg_lse, dl, pk, dsk);
+      else
+        bwd_row<false>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, r, sl2, neg_lse, dl, pk, dsk);
+      if (n > 0) {  // P/dS tiles and the dS TMEM columns are free once step n-1's MMAs are done
+        ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (n - 1) & 1, g, 10));
+        if (!ok) break;
+        tc_fence_after();
       }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        st_tile_row16(sP, r, c, pk + 8 * c);
+        st_tile_row16(sDS, r, c, dsk + 8 * c);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_st16(lane_base + Cfg::DS_COL + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(dsk + 16 * c));
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();

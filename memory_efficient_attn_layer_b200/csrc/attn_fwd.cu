@@ -51,56 +51,83 @@ struct AttnFwdCfg {
   static constexpr size_t SMEM = 1024 + TILE_BYTES * (1 + KS + VS) + 256;
 };
 
-// Row max of one 128-column score row held in TMEM (raw, unscaled scores).
+// Max of 16 raw scores of key columns [16c, 16c+16) into four chains.
+template <bool DIAG>
+__device__ __forceinline__ void max_chunk(const uint32_t (&v)[16], int c, int r, float (&m)[4]) {
+  float x[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) x[e] = (DIAG && 16 * c + e > r) ? -INFINITY : __uint_as_float(v[e]);
+#pragma unroll
+  for (int e = 0; e < 16; e += 8) {
+    m[0] = max3f(m[0], x[e], x[e + 1]);
+    m[1] = max3f(m[1], x[e + 2], x[e + 3]);
+    m[2] = max3f(m[2], x[e + 4], x[e + 5]);
+    m[3] = max3f(m[3], x[e + 6], x[e + 7]);
+  }
+}
+
+// Row max of one 128-column score row held in TMEM (raw, unscaled scores),
+// streamed in 16-column chunks with the next chunk's load in flight.
 // DIAG: the diagonal tile, where key column c > query row r is masked out.
 template <bool DIAG>
 __device__ __forceinline__ float score_row_max(uint32_t sb, int r) {
-  float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  uint32_t a[16], b[16];
+  tmem_ld16(sb, a);
+  tmem_wait_ld_tied(a);
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t v[32];
-    tmem_load32(sb + 32 * c, v);
-    float x[32];
-#pragma unroll
-    for (int e = 0; e < 32; ++e) x[e] = (DIAG && 32 * c + e > r) ? -INFINITY : __uint_as_float(v[e]);
-#pragma unroll
-    for (int e = 0; e < 32; e += 8) {
-      m0 = max3f(m0, x[e], x[e + 1]);
-      m1 = max3f(m1, x[e + 2], x[e + 3]);
-      m2 = max3f(m2, x[e + 4], x[e + 5]);
-      m3 = max3f(m3, x[e + 6], x[e + 7]);
-    }
+  for (int c = 0; c < 8; c += 2) {
+    tmem_ld16(sb + 16 * (c + 1), b);
+    max_chunk<DIAG>(a, c, r, m);
+    tmem_wait_ld_tied(b);
+    if (c + 2 < 8) tmem_ld16(sb + 16 * (c + 2), a);
+    max_chunk<DIAG>(b, c + 1, r, m);
+    if (c + 2 < 8) tmem_wait_ld_tied(a);
   }
-  return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
 }
 
-// P = exp2(s * sl2 - m) for one row: written back over the scores as packed
+// exp2 of 16 scores, packed bf16 P for key columns [16c, 16c+16) stored over the
+// score buffer at packed columns [8c, 8c+8); accumulates the row sum.
+template <bool DIAG>
+__device__ __forceinline__ void exp_chunk(const uint32_t (&v)[16], uint32_t sb, int c, int r, float2 scale2, float2 bias2,
+                                          float2& acc0, float2& acc1) {
+  uint32_t pk[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float2 t = ffma2(make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), scale2, bias2);
+    float p0 = ex2(t.x), p1 = ex2(t.y);
+    if (DIAG) {
+      const int c0 = 16 * c + 2 * e;
+      p0 = c0 > r ? 0.f : p0;
+      p1 = c0 + 1 > r ? 0.f : p1;
+    }
+    if (e & 1)
+      acc1 = fadd2(acc1, make_float2(p0, p1));
+    else
+      acc0 = fadd2(acc0, make_float2(p0, p1));
+    pk[e] = pack_bf16(p0, p1);
+  }
+  tmem_st8(sb + 8 * c, pk);
+}
+
+// P = exp2(s * sl2 - m) for one row, written back over the scores as packed
 // bf16 pairs (columns [0, 64) of the S buffer); returns the row sum of P.
 template <bool DIAG>
 __device__ __forceinline__ float exp_pack_row(uint32_t sb, int r, float sl2, float neg_m) {
   float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
   const float2 scale2 = make_float2(sl2, sl2), bias2 = make_float2(neg_m, neg_m);
+  uint32_t a[16], b[16];
+  tmem_ld16(sb, a);
+  tmem_wait_ld_tied(a);
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t v[32];
-    tmem_load32(sb + 32 * c, v);
-    uint32_t pk[16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const float2 t = ffma2(make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), scale2, bias2);
-      float p0 = ex2(t.x), p1 = ex2(t.y);
-      if (DIAG) {
-        const int c0 = 32 * c + 2 * e;
-        p0 = c0 > r ? 0.f : p0;
-        p1 = c0 + 1 > r ? 0.f : p1;
-      }
-      if (e & 1)
-        acc1 = fadd2(acc1, make_float2(p0, p1));
-      else
-        acc0 = fadd2(acc0, make_float2(p0, p1));
-      pk[e] = pack_bf16(p0, p1);
-    }
-    tmem_st16(sb + 16 * c, pk);
+  for (int c = 0; c < 8; c += 2) {
+    tmem_ld16(sb + 16 * (c + 1), b);
+    exp_chunk<DIAG>(a, sb, c, r, scale2, bias2, acc0, acc1);
+    tmem_wait_ld_tied(b);
+    if (c + 2 < 8) tmem_ld16(sb + 16 * (c + 2), a);
+    exp_chunk<DIAG>(b, sb, c + 1, r, scale2, bias2, acc0, acc1);
+    if (c + 2 < 8) tmem_wait_ld_tied(a);
   }
   return (acc0.x + acc0.y) + (acc1.x + acc1.y);
 }
