@@ -12,12 +12,13 @@
 //   dV += P^T dO_i   (P staged in swizzled shared memory, read MN-major)
 //   dK += dS^T Q_i   (dS staged in shared memory, read MN-major)
 //   dQ_i = dS K      (dS also written to TMEM as packed bf16: A operand from TMEM)
-// dK and dV stay in TMEM for the whole walk.  A separate read-out warpgroup
-// adds each dQ_i tile (fp32) into the accumulator in global memory ([B,H,T,N],
-// zeroed by the caller) and finally writes dK and dV.
+// dK and dV stay in TMEM for the whole walk.  The softmax warps also add each
+// finished dQ_i tile (fp32) into the accumulator in global memory ([B,H,T,N],
+// zeroed by the caller) and finally write dK and dV.
 //
-// Warps: 0 TMA, 1 MMA issue, 2..5 softmax (query row = TMEM lane), 6..9 dQ
-// read-out + epilogue.
+// Warps: 0 TMA, 1 MMA issue, 2..9 softmax: query row = TMEM lane, warps 2..5
+// take key columns [0,64) and warps 6..9 [64,128) (two warps per SM
+// sub-partition, so one can issue while the other waits).
 //
 // Schedules (TMEM has 512 columns):
 //  * N <= 64 ("overlapped"): S [0,128), dP [128,256), dS [256,320), dV, dK, dQ
@@ -90,16 +91,16 @@ __device__ __forceinline__ void st_tile_row16(uint32_t tile, int r, int c, const
   }
 }
 
-// P and dS for 16 key columns [16c, 16c+16) of query row r.
+// P and dS for 16 key columns [16(cbase+c), 16(cbase+c)+16) of query row r.
 template <bool DIAG>
-__device__ __forceinline__ void bwd_chunk(const uint32_t (&sv)[16], const uint32_t (&dp)[16], int c, int r, float2 scale2,
-                                          float2 bias2, float dl, uint32_t (&pk)[64], uint32_t (&dsk)[64]) {
+__device__ __forceinline__ void bwd_chunk(const uint32_t (&sv)[16], const uint32_t (&dp)[16], int c, int cbase, int r,
+                                          float2 scale2, float2 bias2, float dl, uint32_t (&pk)[32], uint32_t (&dsk)[32]) {
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const float2 t = ffma2(make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), scale2, bias2);
     float p0 = ex2(t.x), p1 = ex2(t.y);
     if (DIAG) {  // key column > query row: masked
-      const int c0 = 16 * c + 2 * e;
+      const int c0 = 16 * (cbase + c) + 2 * e;
       p0 = c0 > r ? 0.f : p0;
       p1 = c0 + 1 > r ? 0.f : p1;
     }
@@ -108,28 +109,47 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t (&sv)[16], const uint32
   }
 }
 
-// Whole 128-column row: S and dP stream out of TMEM in 16-column chunks, the
-// next chunk's loads in flight while the current chunk is computed.
+// Half a row: key columns [64*hh, 64*hh + 64) of query row r.  S and dP stream
+// out of TMEM in 16-column chunks with the next chunk's loads in flight while
+// the current chunk is computed; P and dS are kept packed (bf16 pairs).
 template <bool DIAG>
-__device__ __forceinline__ void bwd_row(uint32_t s_addr, uint32_t dp_addr, int r, float sl2, float neg_lse, float dl,
-                                        uint32_t (&pk)[64], uint32_t (&dsk)[64]) {
+__device__ __forceinline__ void bwd_half_row(uint32_t s_addr, uint32_t dp_addr, int hh, int r, float sl2, float neg_lse,
+                                             float dl, uint32_t (&pk)[32], uint32_t (&dsk)[32]) {
   const float2 scale2 = make_float2(sl2, sl2), bias2 = make_float2(neg_lse, neg_lse);
+  const int col0 = 64 * hh;
   uint32_t s0[16], d0[16], s1[16], d1[16];
-  tmem_ld16(s_addr, s0);
-  tmem_ld16(dp_addr, d0);
+  tmem_ld16(s_addr + col0, s0);
+  tmem_ld16(dp_addr + col0, d0);
   tmem_wait_ld_tied2(s0, d0);
 #pragma unroll
-  for (int c = 0; c < 8; c += 2) {
-    tmem_ld16(s_addr + 16 * (c + 1), s1);
-    tmem_ld16(dp_addr + 16 * (c + 1), d1);
-    bwd_chunk<DIAG>(s0, d0, c, r, scale2, bias2, dl, pk, dsk);
+  for (int c = 0; c < 4; c += 2) {
+    tmem_ld16(s_addr + col0 + 16 * (c + 1), s1);
+    tmem_ld16(dp_addr + col0 + 16 * (c + 1), d1);
+    bwd_chunk<DIAG>(s0, d0, c, 4 * hh, r, scale2, bias2, dl, pk, dsk);
     tmem_wait_ld_tied2(s1, d1);
-    if (c + 2 < 8) {
-      tmem_ld16(s_addr + 16 * (c + 2), s0);
-      tmem_ld16(dp_addr + 16 * (c + 2), d0);
+    if (c + 2 < 4) {
+      tmem_ld16(s_addr + col0 + 16 * (c + 2), s0);
+      tmem_ld16(dp_addr + col0 + 16 * (c + 2), d0);
     }
-    bwd_chunk<DIAG>(s1, d1, c + 1, r, scale2, bias2, dl, pk, dsk);
-    if (c + 2 < 8) tmem_wait_ld_tied2(s0, d0);
+    bwd_chunk<DIAG>(s1, d1, c + 1, 4 * hh, r, scale2, bias2, dl, pk, dsk);
+    if (c + 2 < 4) tmem_wait_ld_tied2(s0, d0);
+  }
+}
+
+// Add this thread's share of a dQ tile (row r, columns [hh*HD/2, (hh+1)*HD/2),
+// scaled) into the fp32 accumulator row.
+template <int HD>
+__device__ __forceinline__ void dq_readout(uint32_t dq_addr, int hh, float* dqrow, float scale) {
+  constexpr int HALF = HD / 2;
+#pragma unroll
+  for (int c = 0; c < HALF; c += 16) {
+    uint32_t v[16];
+    tmem_load16(dq_addr + hh * HALF + c, v);
+    float* dst = dqrow + hh * HALF + c;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      red_add_v4_f32(dst + 4 * j, __uint_as_float(v[4 * j]) * scale, __uint_as_float(v[4 * j + 1]) * scale,
+                     __uint_as_float(v[4 * j + 2]) * scale, __uint_as_float(v[4 * j + 3]) * scale);
   }
 }
 
@@ -182,9 +202,9 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
       mbar_init(qdo_empty(s), 1);
     }
     mbar_init(st_full, 1);
-    mbar_init(ds_full, 128);
+    mbar_init(ds_full, 256);
     mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 128);
+    mbar_init(dq_empty, 256);
     mbar_init(drain_bar, 1);
     fence_mbar_init();
   }
@@ -293,9 +313,13 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
         mbar_drain(drain_bar, 0);
       }
     }
-  } else if (warp < 6) {
-    // ---------------- softmax warps 2..5: query row r of each tile ----------------
+  } else {
+    // ---------------- softmax warps 2..9 ----------------
+    // Query row r = TMEM lane; warps 2..5 take key columns [0, 64), warps 6..9
+    // [64, 128), so each sub-partition runs two softmax warps.  The same warps
+    // add each finished dQ tile into global memory and write dK / dV at the end.
     const int quarter = warp & 3;
+    const int hh = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
@@ -308,78 +332,76 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
       tc_fence_after();
       const float neg_lse = -lse_s[s * 256 + r];
       const float dl = lse_s[s * 256 + 128 + r];
-      uint32_t pk[64], dsk[64];
+      uint32_t pk[32], dsk[32];
       if (n == 0)
-        bwd_row<true>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, r, sl2, neg_lse, dl, pk, dsk);
+        bwd_half_row<true>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk);
       else
-        bwd_row<false>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, r, sl2, neg_lse, dl, pk, dsk);
+        bwd_half_row<false>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk);
       if (n > 0) {  // P/dS tiles and the dS TMEM columns are free once step n-1's MMAs are done
         ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (n - 1) & 1, g, 10));
         if (!ok) break;
         tc_fence_after();
       }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        st_tile_row16(sP, r, c, pk + 8 * c);
-        st_tile_row16(sDS, r, c, dsk + 8 * c);
+      for (int c = 0; c < 4; ++c) {
+        st_tile_row16(sP, r, 4 * hh + c, pk + 8 * c);
+        st_tile_row16(sDS, r, 4 * hh + c, dsk + 8 * c);
       }
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_st16(lane_base + Cfg::DS_COL + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(dsk + 16 * c));
+      for (int c = 0; c < 2; ++c)
+        tmem_st16(lane_base + Cfg::DS_COL + 32 * hh + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(dsk + 16 * c));
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
-    }
-    if (!ok) g.ok = false;
-  } else {
-    // ---------------- read-out warps 6..9: dQ tiles, then dK and dV ----------------
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
-    bool ok = true;
-    for (int n = 0; n < nsteps; ++n) {
-      ok = __all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, g, 9));
-      if (!ok) break;
-      tc_fence_after();
-      float* dqrow = p.dq_acc + (size_t(row0) + size_t(jt + n) * 128 + r) * HD;
-#pragma unroll
-      for (int c = 0; c < HD; c += 32) {
-        uint32_t v[32];
-        tmem_load32(lane_base + Cfg::DQ_COL + c, v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          red_add_v4_f32(dqrow + c + 4 * j, __uint_as_float(v[4 * j]) * p.scale, __uint_as_float(v[4 * j + 1]) * p.scale,
-                         __uint_as_float(v[4 * j + 2]) * p.scale, __uint_as_float(v[4 * j + 3]) * p.scale);
+      // dQ read-out: tile n-1 (already complete) when overlapped, else tile n.
+      const int nq_out = OVERLAP ? n - 1 : n;
+      if (nq_out >= 0) {
+        if (!OVERLAP) {
+          ok = __all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, g, 9));
+          if (!ok) break;
+          tc_fence_after();
+        }
+        dq_readout<HD>(lane_base + Cfg::DQ_COL, hh, p.dq_acc + (size_t(row0) + size_t(jt + nq_out) * 128 + r) * HD,
+                       p.scale);
+        tc_fence_before();
+        mbar_arrive(dq_empty);
       }
-      tc_fence_before();
-      mbar_arrive(dq_empty);
     }
-    // dK (scaled) and dV for key row r: every MMA completed with the last dq_full.
+    if (ok && OVERLAP) {  // the last dQ tile
+      ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (nsteps - 1) & 1, g, 11));
+      if (ok) {
+        tc_fence_after();
+        dq_readout<HD>(lane_base + Cfg::DQ_COL, hh,
+                       p.dq_acc + (size_t(row0) + size_t(jt + nsteps - 1) * 128 + r) * HD, p.scale);
+      }
+    }
+    // dK (scaled) and dV for key row r, columns [hh*HD/2, (hh+1)*HD/2): every MMA
+    // completed with the last dq_full.
     if (ok) {
+      constexpr int HALF = HD / 2;
       const int b = bh / p.H, h = bh - b * p.H;
       const int t = jt * 128 + r;
-      __nv_bfloat16* dkrow = p.dk + (size_t(row0) + t) * HD;
-      __nv_bfloat16* dvrow = p.dv + (size_t(b) * p.T + t) * p.ld_dv + size_t(h) * HD;
+      __nv_bfloat16* dkrow = p.dk + (size_t(row0) + t) * HD + hh * HALF;
+      __nv_bfloat16* dvrow = p.dv + (size_t(b) * p.T + t) * p.ld_dv + size_t(h) * HD + hh * HALF;
 #pragma unroll
-      for (int c = 0; c < HD; c += 32) {
-        uint32_t a[32], v[32];
-        tmem_load32(lane_base + Cfg::DK_COL + c, a);
-        tmem_load32(lane_base + Cfg::DV_COL + c, v);
-        uint32_t pa[16], pv[16];
+      for (int c = 0; c < HALF; c += 16) {
+        uint32_t a[16], v[16];
+        tmem_load16(lane_base + Cfg::DK_COL + hh * HALF + c, a);
+        tmem_load16(lane_base + Cfg::DV_COL + hh * HALF + c, v);
+        uint32_t pa[8], pv[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
+        for (int j = 0; j < 8; ++j) {
           pa[j] = pack_bf16(__uint_as_float(a[2 * j]) * p.scale, __uint_as_float(a[2 * j + 1]) * p.scale);
           pv[j] = pack_bf16(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          st_global_v4(dkrow + c + 8 * j, pa[4 * j], pa[4 * j + 1], pa[4 * j + 2], pa[4 * j + 3]);
-          st_global_v4(dvrow + c + 8 * j, pv[4 * j], pv[4 * j + 1], pv[4 * j + 2], pv[4 * j + 3]);
-        }
+        st_global_v4(dkrow + c, pa[0], pa[1], pa[2], pa[3]);
+        st_global_v4(dkrow + c + 8, pa[4], pa[5], pa[6], pa[7]);
+        st_global_v4(dvrow + c, pv[0], pv[1], pv[2], pv[3]);
+        st_global_v4(dvrow + c + 8, pv[4], pv[5], pv[6], pv[7]);
       }
-    } else {
-      g.ok = false;
     }
+    if (!ok) g.ok = false;
   }
 
   tc_fence_before();
