@@ -7,13 +7,13 @@ namespace mea {
 
 template <int BN, int AM, int BMD, int EPI>
 static int launch_gemm_t(const GemmMaps& maps, const GemmParams& p, cudaStream_t st) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, EPI>;
   auto kern = gemm_kernel<BN, AM, BMD, EPI>;
   if (!smem_attr_set(reinterpret_cast<const void*>(kern), int(Cfg::SMEM)))
     return set_error(MEA_ERR_CUDA, "cudaFuncSetAttribute(gemm) failed");
   const int ntiles = p.m_tiles * p.n_tiles * p.k_splits;
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
-  kern<<<grid, GEMM_THREADS, Cfg::SMEM, st>>>(maps, p);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(maps, p);
   return check_launch("gemm_kernel");
 }
 
@@ -78,6 +78,16 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
     if (rc) return set_error(MEA_ERR_CUDA, "gemm: B tensor map %d failed (%d)", i, rc);
   }
   for (int i = nb; i < 4; ++i) maps.b[i] = maps.b[0];
+  for (int i = 0; i < 4; ++i) maps.out[i] = maps.b[0];
+  if (L.epi == EPI_QKVG) {  // TMA store maps for q, k, v, g viewed as [B*H*T, N]
+    const int hd = L.slab_rows;
+    const uint32_t swb = hd >= 64 ? 128 : 64;
+    for (int i = 0; i < 4; ++i) {
+      if (!L.outs[i]) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: projection output %d is null", i);
+      rc = make_tmap_2d(&maps.out[i], L.outs[i], hd, L.out_rows, uint64_t(hd) * 2, swb / 2, GEMM_BM, swizzle_for(swb));
+      if (rc) return set_error(MEA_ERR_CUDA, "gemm: output tensor map %d failed (%d)", i, rc);
+    }
+  }
 
   p.M = L.M;
   p.N = L.N;

@@ -33,6 +33,7 @@ enum EpiMode : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_RED_F32 = 2, EPI_QKVG = 3, E
 struct GemmMaps {
   CUtensorMap a;
   CUtensorMap b[4];
+  CUtensorMap out[4];  // EPI_QKVG: q, k, v, g as [B*H*T, N] for TMA stores
 };
 
 struct GemmParams {
@@ -59,18 +60,24 @@ struct GemmParams {
   float* delta;
 };
 
-constexpr int GEMM_THREADS = 192;
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr uint32_t GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
 
-template <int BN>
+// EPI_QKVG runs eight epilogue warps (two groups splitting the q/k/v/g slabs)
+// and writes its outputs through a shared-memory staging tile with TMA stores;
+// the other epilogues run four warps storing straight from registers.
+template <int BN, int EPI>
 struct GemmCfg {
-  static constexpr int STAGES = BN >= 256 ? 4 : 6;
+  static constexpr bool STAGED = EPI == EPI_QKVG;
+  static constexpr int EPI_WARPS = STAGED ? 8 : 4;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int STAGES = STAGED ? 3 : (BN >= 256 ? 4 : 6);
   static constexpr uint32_t B_BYTES = BN * GEMM_BK * 2;
   static constexpr uint32_t STAGE_BYTES = GEMM_A_BYTES + B_BYTES;
+  static constexpr uint32_t STAGING_BYTES = STAGED ? GEMM_BM * BN * 2 : 0;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + 256;
+  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + STAGING_BYTES + 256;
 };
 
 __device__ __forceinline__ void gemm_decode(const GemmParams& p, int BN, int t, int& m0, int& n0, int& kb0, int& kb1) {
@@ -197,6 +204,96 @@ __device__ __forceinline__ void epi_qkvg(const GemmParams& p, uint32_t taddr, in
   }
 }
 
+// EPI_QKVG through shared memory: this thread's row of each slab the group owns
+// (slabs s with s % 2 == wg) is written bf16 into the staging tile, laid out
+// per slab as [N/64 column chunks][128 rows][row of min(128, 2N) bytes] with
+// the TMA swizzle, so that one TMA store per chunk writes the slab's 128
+// contiguous rows of q/k/v/g.
+template <int BN>
+__device__ __forceinline__ void epi_qkvg_staged(const GemmParams& p, uint32_t taddr, int m, int n0, int wg, int r,
+                                                uint32_t stg) {
+  const int hd = p.hd;
+  const int swb = hd >= 64 ? 128 : 64;
+  const int b = m / p.T;
+  const int t = m - b * p.T;
+  const float rs = p.row_scale ? p.row_scale[m] : 1.0f;
+  const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
+  const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
+  const int nslab = BN / hd;
+  const int swz = swb == 128 ? (r & 7) : ((r >> 1) & 3);
+  for (int s = wg; s < nslab; s += 2) {
+    const int sg = n0 / hd + s;
+    const int head = sg >> 2;
+    const int typ = sg & 3;
+    const uint32_t tcol = taddr + s * hd;
+    const uint32_t slab = stg + s * (GEMM_BM * hd * 2);
+    float sc = rs;
+    if (typ < 2) {
+      float ss = 0.f;
+      for (int c = 0; c < hd; c += 32) {
+        uint32_t v[32];
+        tmem_load32(tcol + c, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float x = __uint_as_float(v[j]) * rs;
+          ss = fmaf(x, x, ss);
+        }
+      }
+      const float inv = rsqrtf(ss / float(hd) + p.eps);
+      float* rdst = typ == 0 ? p.rq : p.rk;
+      if (rdst) rdst[(size_t(b) * p.H + head) * p.T + t] = inv;
+      sc = rs * inv;
+    }
+    for (int c = 0; c < hd; c += 32) {
+      uint32_t v[32];
+      tmem_load32(tcol + c, v);
+      uint32_t pk[16];
+      if (typ < 2) {
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4) {
+          const uint4 a1 = *reinterpret_cast<const uint4*>(f1row + c + 8 * v4);
+          const uint4 a2 = *reinterpret_cast<const uint4*>(f2row + c + 8 * v4);
+          const uint32_t w1[4] = {a1.x, a1.y, a1.z, a1.w};
+          const uint32_t w2[4] = {a2.x, a2.y, a2.z, a2.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = v4 * 4 + e;
+            const float qa = round_bf16(__uint_as_float(v[2 * j]) * sc);
+            const float qb = round_bf16(__uint_as_float(v[2 * j + 1]) * sc);
+            pk[j] = pack_bf16(qa * bf16_lo(w1[e]) + qb * bf16_lo(w2[e]), qb * bf16_hi(w1[e]) + qa * bf16_hi(w2[e]));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float a = __uint_as_float(v[2 * j]) * rs;
+          float bb = __uint_as_float(v[2 * j + 1]) * rs;
+          if (typ == 3) {
+            a = 1.0f / (1.0f + __expf(-a));
+            bb = 1.0f / (1.0f + __expf(-bb));
+          }
+          pk[j] = pack_bf16(a, bb);
+        }
+      }
+      // 32 columns = 4 16-byte units of the row, in column chunk c / 64
+      const uint32_t row_addr = slab + (c >> 6) * (GEMM_BM * swb) + r * swb;
+      const int u0 = (c & 63) >> 3;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t addr = row_addr + (((u0 + j) ^ swz) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(pk[4 * j]), "r"(pk[4 * j + 1]),
+                     "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
+                     : "memory");
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(tmap), "r"(src), "r"(c0), "r"(c1) : "memory");
+}
+
 // Gate backward fused on the dGated = dY * Wo tile (fast_triton_attn.py:576-584, :601):
 //   dO = dGated*g  -> [B,H,T,N] bf16 (input of the attention backward)
 //   dg_pre = dGated*O*g*(1-g) -> the g slot of the projection-gradient buffer
@@ -252,8 +349,8 @@ __device__ __forceinline__ void epi_dgate(const GemmParams& p, uint32_t taddr, i
 // The kernel
 // ---------------------------------------------------------------------------
 template <int BN, int AM, int BMD, int EPI>
-__global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
-  using Cfg = GemmCfg<BN>;
+__global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
+  using Cfg = GemmCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = idesc_bf16(GEMM_BM, BN, AM == A_MN ? 1u : 0u, (BMD == B_MN || BMD == B_MN_KSPLIT4) ? 1u : 0u);
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
@@ -282,7 +379,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_kernel(const __grid_cons
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf_bar(b), 1);
-      mbar_init(acce_bar(b), 128);
+      mbar_init(acce_bar(b), 32 * Cfg::EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
     fence_mbar_init();
@@ -398,9 +495,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_kernel(const __grid_cons
       }
     }
   } else {
-    // ---------------- Epilogue: warps 2..5 ----------------
+    // ---------------- Epilogue: warps 2 .. 2+EPI_WARPS-1 ----------------
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
+    const int wg = (warp - 2) >> 2;                          // epilogue group (STAGED: 0 or 1)
+    const bool leader = Cfg::STAGED && quarter == 2 && lane == 0;  // warps 2 and 6
+    const uint32_t stg = sA + STAGES * Cfg::STAGE_BYTES;
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       int m0, n0, kb0, kb1;
@@ -415,15 +515,39 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_kernel(const __grid_cons
       tc_fence_after();
       const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + buf * BN;
       const int m = m0 + row;
-      if (EPI == EPI_QKVG)
-        epi_qkvg<BN>(p, taddr, m, n0);
-      else if (EPI == EPI_DGATE)
-        epi_dgate<BN>(p, taddr, m, n0);
-      else
-        epi_store<BN>(p, EPI, taddr, m, n0);
-      tc_fence_before();
-      mbar_arrive(acce_bar(buf));
+      if constexpr (Cfg::STAGED) {
+        // the group's previous TMA stores must have finished reading the staging tile
+        if (leader) bulk_wait_read0();
+        named_bar_sync(1 + wg, 128);
+        epi_qkvg_staged<BN>(p, taddr, m, n0, wg, row, stg);
+        tc_fence_before();
+        mbar_arrive(acce_bar(buf));
+        fence_proxy_async_smem();
+        named_bar_sync(1 + wg, 128);
+        if (leader) {
+          const int hd = p.hd;
+          const int swb = hd >= 64 ? 128 : 64;
+          const int b = m0 / p.T, t0 = m0 - (m0 / p.T) * p.T;
+          for (int s = wg; s < BN / hd; s += 2) {
+            const int sg = n0 / hd + s;
+            const int orow = (b * p.H + (sg >> 2)) * p.T + t0;
+            for (int c = 0; c < hd; c += swb / 2)
+              tma_store_2d(&maps.out[sg & 3], stg + s * (GEMM_BM * hd * 2) + (c / 64) * (GEMM_BM * swb), c, orow);
+          }
+          bulk_commit();
+        }
+      } else {
+        if (EPI == EPI_QKVG)
+          epi_qkvg<BN>(p, taddr, m, n0);
+        else if (EPI == EPI_DGATE)
+          epi_dgate<BN>(p, taddr, m, n0);
+        else
+          epi_store<BN>(p, EPI, taddr, m, n0);
+        tc_fence_before();
+        mbar_arrive(acce_bar(buf));
+      }
     }
+    if (leader) bulk_wait0();
   }
 
   __syncthreads();
