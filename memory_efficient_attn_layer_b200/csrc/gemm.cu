@@ -5,10 +5,10 @@
 
 namespace mea {
 
-template <int BN, int AM, int BMD, int EPI>
+template <int BN, int AM, int BMD, int EPI, int HD>
 static int launch_gemm_t(const GemmMaps& maps, const GemmParams& p, cudaStream_t st) {
   using Cfg = GemmCfg<BN, EPI>;
-  auto kern = gemm_kernel<BN, AM, BMD, EPI>;
+  auto kern = gemm_kernel<BN, AM, BMD, EPI, HD>;
   if (!smem_attr_set(reinterpret_cast<const void*>(kern), int(Cfg::SMEM)))
     return set_error(MEA_ERR_CUDA, "cudaFuncSetAttribute(gemm) failed");
   const int ntiles = p.m_tiles * p.n_tiles * p.k_splits;
@@ -19,17 +19,24 @@ static int launch_gemm_t(const GemmMaps& maps, const GemmParams& p, cudaStream_t
 
 #define MEA_GEMM_CASE(BN_, AM_, BMD_, EPI_)                                   \
   if (bn == BN_ && am == AM_ && bmd == BMD_ && epi == EPI_)                   \
-    return launch_gemm_t<BN_, AM_, BMD_, EPI_>(maps, p, st);
+    return launch_gemm_t<BN_, AM_, BMD_, EPI_, 0>(maps, p, st);
+// per-head epilogues: one instantiation per head dim
+#define MEA_GEMM_CASE_HD(BN_, AM_, BMD_, EPI_)                                \
+  if (bn == BN_ && am == AM_ && bmd == BMD_ && epi == EPI_) {                 \
+    if (p.hd == 32) return launch_gemm_t<BN_, AM_, BMD_, EPI_, 32>(maps, p, st);   \
+    if (p.hd == 64) return launch_gemm_t<BN_, AM_, BMD_, EPI_, 64>(maps, p, st);   \
+    if (p.hd == 128) return launch_gemm_t<BN_, AM_, BMD_, EPI_, 128>(maps, p, st); \
+  }
 
 static int dispatch(int bn, int am, int bmd, int epi, const GemmMaps& maps, const GemmParams& p, cudaStream_t st) {
   // forward: fused projections, o_proj
-  MEA_GEMM_CASE(256, A_K, B_SLABS, EPI_QKVG)
-  MEA_GEMM_CASE(128, A_K, B_SLABS, EPI_QKVG)
+  MEA_GEMM_CASE_HD(256, A_K, B_SLABS, EPI_QKVG)
+  MEA_GEMM_CASE_HD(128, A_K, B_SLABS, EPI_QKVG)
   MEA_GEMM_CASE(256, A_K, B_K, EPI_BF16)
   MEA_GEMM_CASE(128, A_K, B_K, EPI_BF16)
   // backward: dGated (+ gate bwd), dx_normed, weight gradients
-  MEA_GEMM_CASE(256, A_K, B_MN, EPI_DGATE)
-  MEA_GEMM_CASE(128, A_K, B_MN, EPI_DGATE)
+  MEA_GEMM_CASE_HD(256, A_K, B_MN, EPI_DGATE)
+  MEA_GEMM_CASE_HD(128, A_K, B_MN, EPI_DGATE)
   MEA_GEMM_CASE(256, A_K, B_MN_KSPLIT4, EPI_BF16)
   MEA_GEMM_CASE(128, A_K, B_MN_KSPLIT4, EPI_BF16)
   MEA_GEMM_CASE(256, A_MN, B_MN, EPI_RED_F32)
@@ -46,6 +53,7 @@ static int dispatch(int bn, int am, int bmd, int epi, const GemmMaps& maps, cons
   return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: no kernel for bn=%d amode=%d bmode=%d epi=%d", bn, am, bmd, epi);
 }
 #undef MEA_GEMM_CASE
+#undef MEA_GEMM_CASE_HD
 
 int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
   const int bn = L.bn;

@@ -123,138 +123,81 @@ __device__ __forceinline__ void epi_store(const GemmParams& p, int mode, uint32_
   }
 }
 
-// q/k RMSNorm over the head dim, bf16 rounding of the normed value, then
-// interleaved rotary out[n] = qn[n]*f1[t,n] + qn[n^1]*f2[t,n]
-// (fast_triton_attn.py:102-106, :132-141).  v is stored as is
-// (fast_triton_attn.py:108) and g as sigmoid(g) (fast_triton_attn.py:123).
-template <int BN>
-__device__ __forceinline__ void epi_qkvg(const GemmParams& p, uint32_t taddr, int m, int n0) {
-  const int hd = p.hd;
-  const int b = m / p.T;
-  const int t = m - b * p.T;
-  const float rs = p.row_scale ? p.row_scale[m] : 1.0f;
-  const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
-  const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
-  const int nslab = BN / hd;
-  for (int s = 0; s < nslab; ++s) {
-    const int sg = n0 / hd + s;
-    const int head = sg >> 2;
-    const int typ = sg & 3;
-    const uint32_t tcol = taddr + s * hd;
-    const size_t bht = (size_t(b) * p.H + head) * p.T + t;
-    if (typ < 2) {
-      float ss = 0.f;
-      for (int c = 0; c < hd; c += 32) {
-        uint32_t r[32];
-        tmem_load32(tcol + c, r);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float v = __uint_as_float(r[j]) * rs;
-          ss = fmaf(v, v, ss);
-        }
-      }
-      const float inv = rsqrtf(ss / float(hd) + p.eps);
-      float* rdst = typ == 0 ? p.rq : p.rk;
-      if (rdst) rdst[bht] = inv;
-      __nv_bfloat16* dst = (typ == 0 ? p.q : p.k) + bht * hd;
-      const float sc = rs * inv;
-      for (int c = 0; c < hd; c += 32) {
-        uint32_t r[32];
-        tmem_load32(tcol + c, r);
-        uint32_t pk[16];
-#pragma unroll
-        for (int v4 = 0; v4 < 4; ++v4) {
-          const uint4 a1 = *reinterpret_cast<const uint4*>(f1row + c + 8 * v4);
-          const uint4 a2 = *reinterpret_cast<const uint4*>(f2row + c + 8 * v4);
-          const uint32_t w1[4] = {a1.x, a1.y, a1.z, a1.w};
-          const uint32_t w2[4] = {a2.x, a2.y, a2.z, a2.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int j = v4 * 4 + e;  // pair index within the chunk
-            const float qa = round_bf16(__uint_as_float(r[2 * j]) * sc);
-            const float qb = round_bf16(__uint_as_float(r[2 * j + 1]) * sc);
-            const float oa = qa * bf16_lo(w1[e]) + qb * bf16_lo(w2[e]);
-            const float ob = qb * bf16_hi(w1[e]) + qa * bf16_hi(w2[e]);
-            pk[j] = pack_bf16(oa, ob);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) st_global_v4(dst + c + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-      }
-    } else {
-      __nv_bfloat16* dst = (typ == 2 ? p.v : p.g) + bht * hd;
-      for (int c = 0; c < hd; c += 32) {
-        uint32_t r[32];
-        tmem_load32(tcol + c, r);
-        uint32_t pk[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float a = __uint_as_float(r[2 * j]) * rs;
-          float bb = __uint_as_float(r[2 * j + 1]) * rs;
-          if (typ == 3) {
-            a = 1.0f / (1.0f + __expf(-a));
-            bb = 1.0f / (1.0f + __expf(-bb));
-          }
-          pk[j] = pack_bf16(a, bb);
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) st_global_v4(dst + c + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-      }
-    }
-  }
-}
-
 // EPI_QKVG through shared memory: this thread's row of each slab the group owns
 // (slabs s with s % 2 == wg) is written bf16 into the staging tile, laid out
 // per slab as [N/64 column chunks][128 rows][row of min(128, 2N) bytes] with
 // the TMA swizzle, so that one TMA store per chunk writes the slab's 128
 // contiguous rows of q/k/v/g.
-template <int BN>
+template <int HD>
+__device__ __forceinline__ void load_tab_chunk(const __nv_bfloat16* f1row, const __nv_bfloat16* f2row, int c,
+                                               uint4 (&t1)[4], uint4 (&t2)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    t1[j] = *reinterpret_cast<const uint4*>(f1row + c + 8 * j);
+    t2[j] = *reinterpret_cast<const uint4*>(f2row + c + 8 * j);
+  }
+}
+
+// q/k RMSNorm over the head dim, bf16 rounding of the normed value, then
+// interleaved rotary out[n] = qn[n]*f1[t,n] + qn[n^1]*f2[t,n]
+// (fast_triton_attn.py:102-106, :132-141); v stored as is (fast_triton_attn.py:108)
+// and g as sigmoid(g) (fast_triton_attn.py:123).  This thread's row of each
+// slab its group owns (slabs s with s % 2 == wg) is written bf16 into the
+// staging tile, laid out per slab as [N/64 column chunks][128 rows][row of
+// min(128, 2N) bytes] with the TMA swizzle, so one TMA store per chunk writes
+// the slab's 128 contiguous rows.  Rotary-table rows are loaded one 32-column
+// chunk ahead of their use.
+template <int BN, int HD>
 __device__ __forceinline__ void epi_qkvg_staged(const GemmParams& p, uint32_t taddr, int m, int n0, int wg, int r,
                                                 uint32_t stg) {
-  const int hd = p.hd;
-  const int swb = hd >= 64 ? 128 : 64;
+  constexpr int SWB = HD >= 64 ? 128 : 64;
+  constexpr int NCH = HD / 32;
   const int b = m / p.T;
   const int t = m - b * p.T;
   const float rs = p.row_scale ? p.row_scale[m] : 1.0f;
   const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
   const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
-  const int nslab = BN / hd;
-  const int swz = swb == 128 ? (r & 7) : ((r >> 1) & 3);
-  for (int s = wg; s < nslab; s += 2) {
-    const int sg = n0 / hd + s;
+  constexpr int NSLAB = BN / HD;
+  const int swz = SWB == 128 ? (r & 7) : ((r >> 1) & 3);
+#pragma unroll 1
+  for (int s = wg; s < NSLAB; s += 2) {
+    const int sg = n0 / HD + s;
     const int head = sg >> 2;
     const int typ = sg & 3;
-    const uint32_t tcol = taddr + s * hd;
-    const uint32_t slab = stg + s * (GEMM_BM * hd * 2);
+    const uint32_t tcol = taddr + s * HD;
+    const uint32_t slab = stg + s * (GEMM_BM * HD * 2);
+    uint4 t1[2][4], t2[2][4];
     float sc = rs;
     if (typ < 2) {
+      load_tab_chunk<HD>(f1row, f2row, 0, t1[0], t2[0]);
       float ss = 0.f;
-      for (int c = 0; c < hd; c += 32) {
+#pragma unroll
+      for (int ci = 0; ci < NCH; ++ci) {
         uint32_t v[32];
-        tmem_load32(tcol + c, v);
+        tmem_load32(tcol + 32 * ci, v);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float x = __uint_as_float(v[j]) * rs;
           ss = fmaf(x, x, ss);
         }
       }
-      const float inv = rsqrtf(ss / float(hd) + p.eps);
+      const float inv = rsqrtf(ss / float(HD) + p.eps);
       float* rdst = typ == 0 ? p.rq : p.rk;
       if (rdst) rdst[(size_t(b) * p.H + head) * p.T + t] = inv;
       sc = rs * inv;
     }
-    for (int c = 0; c < hd; c += 32) {
+#pragma unroll
+    for (int ci = 0; ci < NCH; ++ci) {
+      const int c = 32 * ci;
+      if (typ < 2 && ci + 1 < NCH) load_tab_chunk<HD>(f1row, f2row, c + 32, t1[(ci + 1) & 1], t2[(ci + 1) & 1]);
       uint32_t v[32];
       tmem_load32(tcol + c, v);
       uint32_t pk[16];
       if (typ < 2) {
 #pragma unroll
         for (int v4 = 0; v4 < 4; ++v4) {
-          const uint4 a1 = *reinterpret_cast<const uint4*>(f1row + c + 8 * v4);
-          const uint4 a2 = *reinterpret_cast<const uint4*>(f2row + c + 8 * v4);
-          const uint32_t w1[4] = {a1.x, a1.y, a1.z, a1.w};
-          const uint32_t w2[4] = {a2.x, a2.y, a2.z, a2.w};
+          const uint32_t w1[4] = {t1[ci & 1][v4].x, t1[ci & 1][v4].y, t1[ci & 1][v4].z, t1[ci & 1][v4].w};
+          const uint32_t w2[4] = {t2[ci & 1][v4].x, t2[ci & 1][v4].y, t2[ci & 1][v4].z, t2[ci & 1][v4].w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int j = v4 * 4 + e;
@@ -276,7 +219,7 @@ __device__ __forceinline__ void epi_qkvg_staged(const GemmParams& p, uint32_t ta
         }
       }
       // 32 columns = 4 16-byte units of the row, in column chunk c / 64
-      const uint32_t row_addr = slab + (c >> 6) * (GEMM_BM * swb) + r * swb;
+      const uint32_t row_addr = slab + (c >> 6) * (GEMM_BM * SWB) + r * SWB;
       const int u0 = (c & 63) >> 3;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -298,12 +241,14 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int
 //   dO = dGated*g  -> [B,H,T,N] bf16 (input of the attention backward)
 //   dg_pre = dGated*O*g*(1-g) -> the g slot of the projection-gradient buffer
 //   delta = rowsum(dO*O) per (b,h,t)  (the attention backward's D term)
-template <int BN>
+template <int BN, int HD>
 __device__ __forceinline__ void epi_dgate(const GemmParams& p, uint32_t taddr, int m, int n0) {
-  const int hd = p.hd;
+  constexpr int hd = HD;
   const int b = m / p.T;
   const int t = m - b * p.T;
-  const int nslab = BN / hd;
+  constexpr int nslab = BN / hd;
+  constexpr int nch = hd / 32;
+#pragma unroll 1
   for (int s = 0; s < nslab; ++s) {
     const int head = n0 / hd + s;
     const size_t bht = (size_t(b) * p.H + head) * p.T + t;
@@ -312,14 +257,31 @@ __device__ __forceinline__ void epi_dgate(const GemmParams& p, uint32_t taddr, i
     __nv_bfloat16* dorow = p.do_out + bht * hd;
     __nv_bfloat16* dgrow = p.dg_out + size_t(m) * p.ld_dg + size_t(head) * hd;
     float dsum = 0.f;
-    for (int c = 0; c < hd; c += 32) {
+    // O and sigmoid(g) of the row are loaded one 32-column chunk ahead of their use.
+    uint4 ob[2][4], gb[2][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      ob[0][j] = *reinterpret_cast<const uint4*>(orow + 8 * j);
+      gb[0][j] = *reinterpret_cast<const uint4*>(grow + 8 * j);
+    }
+#pragma unroll
+    for (int ci = 0; ci < nch; ++ci) {
+      const int c = 32 * ci;
+      const int cur = ci & 1;
+      if (ci + 1 < nch) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          ob[cur ^ 1][j] = *reinterpret_cast<const uint4*>(orow + c + 32 + 8 * j);
+          gb[cur ^ 1][j] = *reinterpret_cast<const uint4*>(grow + c + 32 + 8 * j);
+        }
+      }
       uint32_t r[32];
       tmem_load32(taddr + s * hd + c, r);
       uint32_t pd[16], pg[16];
 #pragma unroll
       for (int v4 = 0; v4 < 4; ++v4) {
-        const uint4 ov = *reinterpret_cast<const uint4*>(orow + c + 8 * v4);
-        const uint4 gv = *reinterpret_cast<const uint4*>(grow + c + 8 * v4);
+        const uint4 ov = ob[cur][v4];
+        const uint4 gv = gb[cur][v4];
         const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
         const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
 #pragma unroll
@@ -348,7 +310,8 @@ __device__ __forceinline__ void epi_dgate(const GemmParams& p, uint32_t taddr, i
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int BN, int AM, int BMD, int EPI>
+// HD: head dim for the per-head epilogues (EPI_QKVG, EPI_DGATE), 0 otherwise.
+template <int BN, int AM, int BMD, int EPI, int HD>
 __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
   using Cfg = GemmCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
@@ -519,7 +482,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
         // the group's previous TMA stores must have finished reading the staging tile
         if (leader) bulk_wait_read0();
         named_bar_sync(1 + wg, 128);
-        epi_qkvg_staged<BN>(p, taddr, m, n0, wg, row, stg);
+        epi_qkvg_staged<BN, HD>(p, taddr, m, n0, wg, row, stg);
         tc_fence_before();
         mbar_arrive(acce_bar(buf));
         fence_proxy_async_smem();
@@ -537,10 +500,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
           bulk_commit();
         }
       } else {
-        if (EPI == EPI_QKVG)
-          epi_qkvg<BN>(p, taddr, m, n0);
-        else if (EPI == EPI_DGATE)
-          epi_dgate<BN>(p, taddr, m, n0);
+        if constexpr (EPI == EPI_DGATE)
+          epi_dgate<BN, HD>(p, taddr, m, n0);
         else
           epi_store<BN>(p, EPI, taddr, m, n0);
         tc_fence_before();
