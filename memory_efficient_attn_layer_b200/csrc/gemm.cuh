@@ -147,88 +147,111 @@ __device__ __forceinline__ void load_tab_chunk(const __nv_bfloat16* f1row, const
 // min(128, 2N) bytes] with the TMA swizzle, so one TMA store per chunk writes
 // the slab's 128 contiguous rows.  Rotary-table rows are loaded one 32-column
 // chunk ahead of their use.
-template <int BN, int HD>
-__device__ __forceinline__ void epi_qkvg_staged(const GemmParams& p, uint32_t taddr, int m, int n0, int wg, int r,
-                                                uint32_t stg) {
+// One slab (q, k, v or g of one head) of this thread's row, into the staging tile.
+// QK: q or k (per-head RMSNorm + rotary, with the rotary rows of chunks 0 and 1
+// preloaded in t1/t2 and later chunks streamed one ahead); else v or sigmoid(g).
+template <int HD, bool QK>
+__device__ __forceinline__ void qkvg_slab(const GemmParams& p, uint32_t tcol, uint32_t slab, int typ, int r, int swz,
+                                          float rs, size_t bht, const __nv_bfloat16* f1row,
+                                          const __nv_bfloat16* f2row, uint4 (&t1)[2][4], uint4 (&t2)[2][4]) {
   constexpr int SWB = HD >= 64 ? 128 : 64;
   constexpr int NCH = HD / 32;
+  float sc = rs;
+  if (QK) {
+    float ss = 0.f;
+#pragma unroll
+    for (int ci = 0; ci < NCH; ++ci) {
+      uint32_t v[32];
+      tmem_load32(tcol + 32 * ci, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float x = __uint_as_float(v[j]) * rs;
+        ss = fmaf(x, x, ss);
+      }
+    }
+    const float inv = rsqrtf(ss / float(HD) + p.eps);
+    float* rdst = typ == 0 ? p.rq : p.rk;
+    if (rdst) rdst[bht] = inv;
+    sc = rs * inv;
+  }
+#pragma unroll
+  for (int ci = 0; ci < NCH; ++ci) {
+    const int c = 32 * ci;
+    if (QK && ci >= 1 && ci + 1 < NCH) load_tab_chunk<HD>(f1row, f2row, c + 32, t1[(ci + 1) & 1], t2[(ci + 1) & 1]);
+    uint32_t v[32];
+    tmem_load32(tcol + c, v);
+    uint32_t pk[16];
+    if (QK) {
+#pragma unroll
+      for (int v4 = 0; v4 < 4; ++v4) {
+        const uint32_t w1[4] = {t1[ci & 1][v4].x, t1[ci & 1][v4].y, t1[ci & 1][v4].z, t1[ci & 1][v4].w};
+        const uint32_t w2[4] = {t2[ci & 1][v4].x, t2[ci & 1][v4].y, t2[ci & 1][v4].z, t2[ci & 1][v4].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = v4 * 4 + e;
+          const float qa = round_bf16(__uint_as_float(v[2 * j]) * sc);
+          const float qb = round_bf16(__uint_as_float(v[2 * j + 1]) * sc);
+          pk[j] = pack_bf16(qa * bf16_lo(w1[e]) + qb * bf16_lo(w2[e]), qb * bf16_hi(w1[e]) + qa * bf16_hi(w2[e]));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float a = __uint_as_float(v[2 * j]) * rs;
+        float bb = __uint_as_float(v[2 * j + 1]) * rs;
+        if (typ == 3) {
+          a = __fdividef(1.0f, 1.0f + __expf(-a));
+          bb = __fdividef(1.0f, 1.0f + __expf(-bb));
+        }
+        pk[j] = pack_bf16(a, bb);
+      }
+    }
+    // 32 columns = 4 16-byte units of the row, in column chunk c / 64
+    const uint32_t row_addr = slab + (c >> 6) * (GEMM_BM * SWB) + r * SWB;
+    const int u0 = (c & 63) >> 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t addr = row_addr + (((u0 + j) ^ swz) << 4);
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(pk[4 * j]), "r"(pk[4 * j + 1]),
+                   "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
+                   : "memory");
+    }
+  }
+}
+
+// q/k RMSNorm over the head dim, bf16 rounding of the normed value, then
+// interleaved rotary out[n] = qn[n]*f1[t,n] + qn[n^1]*f2[t,n]
+// (fast_triton_attn.py:102-106, :132-141); v stored as is (fast_triton_attn.py:108)
+// and g as sigmoid(g) (fast_triton_attn.py:123).  This thread's row of each
+// slab its group owns (slabs s with s % 2 == wg) is written bf16 into the
+// staging tile, laid out per slab as [N/64 column chunks][128 rows][row of
+// min(128, 2N) bytes] with the TMA swizzle, so one TMA store per chunk writes
+// the slab's 128 contiguous rows.  q/k slabs go first, while the rotary rows
+// preloaded by the caller are live; v/g slabs follow.
+template <int BN, int HD>
+__device__ __forceinline__ void epi_qkvg_staged(const GemmParams& p, uint32_t taddr, int m, int n0, int wg, int r,
+                                                uint32_t stg, uint4 (&t1)[2][4], uint4 (&t2)[2][4]) {
+  constexpr int SWB = HD >= 64 ? 128 : 64;
+  constexpr int NSLAB = BN / HD;
   const int b = m / p.T;
   const int t = m - b * p.T;
   const float rs = p.row_scale ? p.row_scale[m] : 1.0f;
   const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
   const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
-  constexpr int NSLAB = BN / HD;
   const int swz = SWB == 128 ? (r & 7) : ((r >> 1) & 3);
 #pragma unroll 1
   for (int s = wg; s < NSLAB; s += 2) {
     const int sg = n0 / HD + s;
-    const int head = sg >> 2;
-    const int typ = sg & 3;
-    const uint32_t tcol = taddr + s * HD;
-    const uint32_t slab = stg + s * (GEMM_BM * HD * 2);
-    uint4 t1[2][4], t2[2][4];
-    float sc = rs;
-    if (typ < 2) {
-      load_tab_chunk<HD>(f1row, f2row, 0, t1[0], t2[0]);
-      float ss = 0.f;
-#pragma unroll
-      for (int ci = 0; ci < NCH; ++ci) {
-        uint32_t v[32];
-        tmem_load32(tcol + 32 * ci, v);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float x = __uint_as_float(v[j]) * rs;
-          ss = fmaf(x, x, ss);
-        }
-      }
-      const float inv = rsqrtf(ss / float(HD) + p.eps);
-      float* rdst = typ == 0 ? p.rq : p.rk;
-      if (rdst) rdst[(size_t(b) * p.H + head) * p.T + t] = inv;
-      sc = rs * inv;
-    }
-#pragma unroll
-    for (int ci = 0; ci < NCH; ++ci) {
-      const int c = 32 * ci;
-      if (typ < 2 && ci + 1 < NCH) load_tab_chunk<HD>(f1row, f2row, c + 32, t1[(ci + 1) & 1], t2[(ci + 1) & 1]);
-      uint32_t v[32];
-      tmem_load32(tcol + c, v);
-      uint32_t pk[16];
-      if (typ < 2) {
-#pragma unroll
-        for (int v4 = 0; v4 < 4; ++v4) {
-          const uint32_t w1[4] = {t1[ci & 1][v4].x, t1[ci & 1][v4].y, t1[ci & 1][v4].z, t1[ci & 1][v4].w};
-          const uint32_t w2[4] = {t2[ci & 1][v4].x, t2[ci & 1][v4].y, t2[ci & 1][v4].z, t2[ci & 1][v4].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int j = v4 * 4 + e;
-            const float qa = round_bf16(__uint_as_float(v[2 * j]) * sc);
-            const float qb = round_bf16(__uint_as_float(v[2 * j + 1]) * sc);
-            pk[j] = pack_bf16(qa * bf16_lo(w1[e]) + qb * bf16_lo(w2[e]), qb * bf16_hi(w1[e]) + qa * bf16_hi(w2[e]));
-          }
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float a = __uint_as_float(v[2 * j]) * rs;
-          float bb = __uint_as_float(v[2 * j + 1]) * rs;
-          if (typ == 3) {
-            a = 1.0f / (1.0f + __expf(-a));
-            bb = 1.0f / (1.0f + __expf(-bb));
-          }
-          pk[j] = pack_bf16(a, bb);
-        }
-      }
-      // 32 columns = 4 16-byte units of the row, in column chunk c / 64
-      const uint32_t row_addr = slab + (c >> 6) * (GEMM_BM * SWB) + r * SWB;
-      const int u0 = (c & 63) >> 3;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t addr = row_addr + (((u0 + j) ^ swz) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(pk[4 * j]), "r"(pk[4 * j + 1]),
-                     "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
-                     : "memory");
-      }
-    }
+    if ((sg & 3) < 2)
+      qkvg_slab<HD, true>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs,
+                          (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row, t1, t2);
+  }
+#pragma unroll 1
+  for (int s = wg; s < NSLAB; s += 2) {
+    const int sg = n0 / HD + s;
+    if ((sg & 3) >= 2)
+      qkvg_slab<HD, false>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs, 0, f1row, f2row, t1,
+                           t2);
   }
 }
 
@@ -469,6 +492,16 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
       int m0, n0, kb0, kb1;
       gemm_decode(p, BN, t, m0, n0, kb0, kb1);
       const int buf = it & 1;
+      // Projection epilogue: the rotary-table rows of this thread's token are
+      // loaded before the accumulator wait, which hides their latency.
+      uint4 pre1[2][4], pre2[2][4];
+      if constexpr (Cfg::STAGED) {
+        const int t = (m0 + row) % p.T;
+        const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
+        const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
+        load_tab_chunk<HD>(f1row, f2row, 0, pre1[0], pre2[0]);
+        if (HD > 32) load_tab_chunk<HD>(f1row, f2row, 32, pre1[1], pre2[1]);
+      }
       bool ok = mbar_wait(accf_bar(buf), (it >> 1) & 1, g, 4);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
@@ -482,7 +515,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
         // the group's previous TMA stores must have finished reading the staging tile
         if (leader) bulk_wait_read0();
         named_bar_sync(1 + wg, 128);
-        epi_qkvg_staged<BN, HD>(p, taddr, m, n0, wg, row, stg);
+        epi_qkvg_staged<BN, HD>(p, taddr, m, n0, wg, row, stg, pre1, pre2);
         tc_fence_before();
         mbar_arrive(acce_bar(buf));
         fence_proxy_async_smem();
