@@ -94,7 +94,7 @@ struct Carve {
 };
 
 struct FwdWs {
-  size_t xn, rx, q, k, v, gs, gated, total;
+  size_t xn, rx, q, k, v, gs, gated, bound, total;
 };
 static FwdWs fwd_layout(const mea_block_dims& d) {
   const size_t M = size_t(d.B) * d.T, HN = size_t(d.H) * d.N;
@@ -107,12 +107,13 @@ static FwdWs fwd_layout(const mea_block_dims& d) {
   w.v = c.take(M * HN * 2);
   w.gs = c.take(M * HN * 2);
   w.gated = c.take(M * HN * 2);
+  w.bound = c.take(4);
   w.total = c.off;
   return w;
 }
 
 struct BwdWs {
-  size_t xn, rx, q, k, v, gs, rq, rk, gated, o, lse, dO, delta, dacc, dqacc, dk, dxn, dw32, total;
+  size_t xn, rx, q, k, v, gs, rq, rk, gated, o, dO, delta, dacc, dqacc, dk, dxn, dw32, total;
 };
 static BwdWs bwd_layout(const mea_block_dims& d) {
   const size_t M = size_t(d.B) * d.T, HN = size_t(d.H) * d.N, BHT = size_t(d.B) * d.H * d.T;
@@ -128,7 +129,6 @@ static BwdWs bwd_layout(const mea_block_dims& d) {
   w.rk = c.take(BHT * 4);
   w.gated = c.take(M * HN * 2);
   w.o = c.take(M * HN * 2);
-  w.lse = c.take(BHT * 4);
   w.dO = c.take(M * HN * 2);
   w.delta = c.take(BHT * 4);
   w.dacc = c.take(M * 4 * HN * 2);
@@ -362,8 +362,15 @@ int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, co
   MEA_STAGE(ST_FWD_NORM, run_rmsnorm_fwd(M, d->C, d->eps, x, ws + w.xn, reinterpret_cast<float*>(ws + w.rx), st));
   MEA_STAGE(ST_FWD_QKVG, qkvg(*d, ws + w.xn, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, nullptr,
                nullptr, status, st));
-  MEA_STAGE(ST_FWD_ATTN, run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated, lse2, nullptr,
-                       status, st));
+  {
+    // Scores are bounded through the per-head norm and the rotary tables, so
+    // the attention uses that bound as its exp2 reference (no row-max pass).
+    StageScope scope_(ST_FWD_ATTN, st);
+    float* bound = reinterpret_cast<float*>(ws + w.bound);
+    MEA_TRY(run_rope_bound(d->T, d->N, factor1, factor2, d->N, bound, st));
+    MEA_TRY(run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated, lse2, nullptr,
+                         bound, nullptr, status, st));
+  }
   GemmLaunch L{};
   L.M = M;
   L.N = d->C;
@@ -412,8 +419,10 @@ int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, c
   MEA_STAGE(ST_BWD_NORM, run_rmsnorm_fwd(M, C, d->eps, x, ws + w.xn, rx, st));
   MEA_STAGE(ST_BWD_QKVG, qkvg(*d, ws + w.xn, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, rq, rk,
                status, st));
+  // The recompute takes the forward's LSE as its exp2 reference: P comes out
+  // normalised, the same P the attention backward rebuilds.
   MEA_STAGE(ST_BWD_ATTN_FWD, run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated,
-                       reinterpret_cast<float*>(ws + w.lse), ws + w.o, status, st));
+                       nullptr, ws + w.o, nullptr, lse2, status, st));
   {
     StageScope scope_(ST_BWD_MEMSET, st);
     MEA_TRY(memset_async(dw32, size_t(5) * HN * C * 4, st));
@@ -482,7 +491,7 @@ int mea_qkvg_forward(const mea_block_dims* d, const void* xn, const void* wq, co
 
 int mea_attention_forward(int B, int H, int T, int N, const void* q, const void* k, const void* v, const void* gs,
                           void* gated, float* lse2, void* o, int* status, void* stream) {
-  return run_attn_fwd(B, H, T, N, q, k, v, gs, gated, lse2, o, status, static_cast<cudaStream_t>(stream));
+  return run_attn_fwd(B, H, T, N, q, k, v, gs, gated, lse2, o, nullptr, nullptr, status, static_cast<cudaStream_t>(stream));
 }
 
 int mea_gemm(int M, int N, int K, const void* a, long long lda, int a_mn, const void* b, long long ldb, int b_mn,

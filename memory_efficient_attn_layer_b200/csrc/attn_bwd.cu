@@ -14,7 +14,11 @@
 //   dQ_i = dS K      (dS also written to TMEM as packed bf16: A operand from TMEM)
 // dK and dV stay in TMEM for the whole walk.  The softmax warps also add each
 // finished dQ_i tile (fp32) into the accumulator in global memory ([B,H,T,N],
-// zeroed by the caller) and finally write dK and dV.
+// zeroed by the caller) and finally write dK and dV.  For N <= 64 the dQ tile
+// is staged in swizzled shared memory and added by one TMA reduce-add per
+// 32-column box, which keeps the reductions off the load/store unit that the
+// P/dS tile stores need; for N = 128 (no room for the staging tile) the warps
+// issue vector red.global.add directly.
 //
 // Warps: 0 TMA, 1 MMA issue, 2..9 softmax: query row = TMEM lane, warps 2..5
 // take key columns [0,64) and warps 6..9 [64,128) (two warps per SM
@@ -22,9 +26,10 @@
 //
 // Schedules (TMEM has 512 columns):
 //  * N <= 64 ("overlapped"): S [0,128), dP [128,256), dS [256,320), dV, dK, dQ
-//    after it.  As soon as the softmax warps have read S_i and dP_i, the MMA
-//    warp issues S_{i+1}, dP_{i+1} and only then dV_i, dK_i, dQ_i, so the next
-//    tile's exponentials overlap this tile's gradient MMAs.
+//    after it.  As soon as the softmax warps have read S_i and dP_i (st_empty),
+//    the MMA warp issues S_{i+1}, dP_{i+1}, ahead of dV_i, dK_i, dQ_i, so the
+//    next tile's scores are ready when the softmax warps finish storing P_i and
+//    dS_i, and its exponentials overlap this tile's gradient MMAs.
 //  * N = 128 ("serial"): S [0,128) (dS written over it), dP [128,256) (dQ written
 //    over it after dP is read), dV [256,384), dK [384,512); S_{i+1} is issued
 //    after dQ_i, and dP_{i+1} after the read-out of dQ_i.
@@ -49,6 +54,7 @@ struct AttnBwdParams {
 
 struct AttnBwdMaps {
   CUtensorMap q, k, v, dO;
+  CUtensorMap dq;  // dq_acc as [B*H*T, N] fp32, 32x128 boxes, 128-byte swizzle (N <= 64)
 };
 
 template <int HD>
@@ -67,7 +73,10 @@ struct AttnBwdCfg {
   static constexpr uint32_t OFF_K = 0, OFF_V = TB, OFF_Q = 2 * TB, OFF_DO = OFF_Q + STAGES * TB;
   static constexpr uint32_t OFF_P = OFF_DO + STAGES * TB, OFF_DS = OFF_P + PT;
   static constexpr uint32_t OFF_LSE = OFF_DS + PT;
-  static constexpr uint32_t OFF_BAR = OFF_LSE + STAGES * 1024;
+  static constexpr bool TMA_DQ = OVERLAP;                      // dQ staged for a TMA reduce-add
+  static constexpr uint32_t OFF_DQ = OFF_LSE + STAGES * 1024;  // HD/32 boxes of [128 x 32] fp32
+  static constexpr uint32_t DQ_BYTES = TMA_DQ ? HD * 512 : 0;
+  static constexpr uint32_t OFF_BAR = OFF_DQ + DQ_BYTES;
   static constexpr size_t SMEM = 1024 + OFF_BAR + 256;
 };
 
@@ -98,7 +107,8 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t (&sv)[16], const uint32
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const float2 t = ffma2(make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), scale2, bias2);
-    float p0 = ex2(t.x), p1 = ex2(t.y);
+    const float2 pp = exp2_pair(t, (kPolyPairs >> e) & 1);
+    float p0 = pp.x, p1 = pp.y;
     if (DIAG) {  // key column > query row: masked
       const int c0 = 16 * (cbase + c) + 2 * e;
       p0 = c0 > r ? 0.f : p0;
@@ -153,6 +163,30 @@ __device__ __forceinline__ void dq_readout(uint32_t dq_addr, int hh, float* dqro
   }
 }
 
+// Stage this thread's share of a dQ tile (row r, columns [hh*HD/2, (hh+1)*HD/2),
+// scaled) into the fp32 staging tile: HD/32 boxes of 128 rows x 128 bytes in
+// the 128-byte swizzle the TMA reduce-add unswizzles (16-byte unit u of row r
+// at u ^ (r & 7)).
+template <int HD>
+__device__ __forceinline__ void dq_stage(uint32_t dq_addr, int hh, int r, uint32_t stg, float scale) {
+  constexpr int HALF = HD / 2;
+#pragma unroll
+  for (int c = 0; c < HALF; c += 16) {
+    uint32_t v[16];
+    tmem_load16(dq_addr + hh * HALF + c, v);
+    const int col0 = hh * HALF + c;
+    const uint32_t row = stg + (col0 >> 5) * 16384 + r * 128;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int unit = ((col0 & 31) >> 2) + u;
+      asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(row + ((unit ^ (r & 7)) << 4)),
+                   "f"(__uint_as_float(v[4 * u]) * scale), "f"(__uint_as_float(v[4 * u + 1]) * scale),
+                   "f"(__uint_as_float(v[4 * u + 2]) * scale), "f"(__uint_as_float(v[4 * u + 3]) * scale)
+                   : "memory");
+    }
+  }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant__ AttnBwdMaps maps, const AttnBwdParams p) {
   using Cfg = AttnBwdCfg<HD>;
@@ -182,7 +216,10 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
   const uint32_t dq_full = st_full + 16;
   const uint32_t dq_empty = st_full + 24;
   const uint32_t drain_bar = st_full + 32;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6 + 2 * STAGES);
+  const uint32_t st_empty = st_full + 40;   // softmax warps have read S_n and dP_n
+  const uint32_t stg_full = st_full + 48;   // dQ staging tile written
+  const uint32_t stg_empty = st_full + 56;  // previous TMA reduce has read the staging tile
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9 + 2 * STAGES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -206,6 +243,9 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 256);
     mbar_init(drain_bar, 1);
+    mbar_init(st_empty, 256);
+    mbar_init(stg_full, 256);
+    mbar_init(stg_empty, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -282,9 +322,13 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
       if (mbar_wait(kv_full, 0, g, 2) && issue_sdp(0)) {
         for (int n = 0; n < nsteps; ++n) {
           const int s = n % STAGES;
+          if (OVERLAP && n + 1 < nsteps) {  // S_n, dP_n read: issue the next scores now
+            if (!mbar_wait(st_empty, n & 1, g, 12)) break;
+            tc_fence_after();
+            if (!issue_sdp(n + 1)) break;
+          }
           if (!mbar_wait(ds_full, n & 1, g, 5)) break;
           tc_fence_after();
-          if (OVERLAP && n + 1 < nsteps && !issue_sdp(n + 1)) break;
           // dV += P^T dO_n ; dK += dS^T Q_n  (A operands MN-major from shared memory)
 #pragma unroll
           for (int kc = 0; kc < 8; ++kc)
@@ -323,6 +367,33 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
+    const bool lead = (warp == 2 && lane == 0);  // issues the dQ reduce-adds
+    const uint32_t stg = base + Cfg::OFF_DQ;
+    // dQ tile k out of TMEM into the staging tile, then one TMA reduce-add per
+    // 32-column box.  The staging tile is reused once the previous reduce-add has
+    // read it (stg_empty); the lead thread waits for all 256 writers (stg_full).
+    auto dq_out_tma = [&](int k) -> bool {
+      if (k > 0) {
+        if (lead) {
+          bulk_wait_read0();
+          mbar_arrive(stg_empty);
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(stg_empty, (k - 1) & 1, g, 13))) return false;
+      }
+      dq_stage<HD>(lane_base + Cfg::DQ_COL, hh, r, stg, p.scale);
+      tc_fence_before();
+      mbar_arrive(dq_empty);
+      fence_proxy_async_smem();
+      mbar_arrive(stg_full);
+      if (lead) {
+        if (!mbar_wait(stg_full, k & 1, g, 14)) return false;
+        const int qrow = row0 + (jt + k) * 128;
+#pragma unroll
+        for (int bx = 0; bx < HD / 32; ++bx) tma_reduce_add_2d(&maps.dq, stg + bx * 16384, bx * 32, qrow);
+        bulk_commit();
+      }
+      return true;
+    };
     bool ok = true;
     for (int n = 0; n < nsteps; ++n) {
       const int s = n % STAGES;
@@ -337,6 +408,10 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
         bwd_half_row<true>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk);
       else
         bwd_half_row<false>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk);
+      if (OVERLAP) {  // every TMEM load of S_n / dP_n has completed
+        tc_fence_before();
+        mbar_arrive(st_empty);
+      }
       if (n > 0) {  // P/dS tiles and the dS TMEM columns are free once step n-1's MMAs are done
         ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (n - 1) & 1, g, 10));
         if (!ok) break;
@@ -362,19 +437,31 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
           if (!ok) break;
           tc_fence_after();
         }
-        dq_readout<HD>(lane_base + Cfg::DQ_COL, hh, p.dq_acc + (size_t(row0) + size_t(jt + nq_out) * 128 + r) * HD,
-                       p.scale);
-        tc_fence_before();
-        mbar_arrive(dq_empty);
+        if constexpr (Cfg::TMA_DQ) {
+          ok = dq_out_tma(nq_out);
+          if (!ok) break;
+        } else {
+          dq_readout<HD>(lane_base + Cfg::DQ_COL, hh, p.dq_acc + (size_t(row0) + size_t(jt + nq_out) * 128 + r) * HD,
+                         p.scale);
+          tc_fence_before();
+          mbar_arrive(dq_empty);
+        }
       }
     }
     if (ok && OVERLAP) {  // the last dQ tile
       ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (nsteps - 1) & 1, g, 11));
       if (ok) {
         tc_fence_after();
-        dq_readout<HD>(lane_base + Cfg::DQ_COL, hh,
-                       p.dq_acc + (size_t(row0) + size_t(jt + nsteps - 1) * 128 + r) * HD, p.scale);
+        if constexpr (Cfg::TMA_DQ) {
+          ok = dq_out_tma(nsteps - 1);
+        } else {
+          dq_readout<HD>(lane_base + Cfg::DQ_COL, hh,
+                         p.dq_acc + (size_t(row0) + size_t(jt + nsteps - 1) * 128 + r) * HD, p.scale);
+        }
       }
+    }
+    if constexpr (Cfg::TMA_DQ) {
+      if (lead) bulk_wait0();  // every reduce-add has landed before the CTA exits
     }
     // dK (scaled) and dV for key row r, columns [hh*HD/2, (hh+1)*HD/2): every MMA
     // completed with the last dq_full.
@@ -442,6 +529,10 @@ int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, cons
   rc |= make_tmap_2d(&maps.k, k, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
   rc |= make_tmap_2d(&maps.v, v, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
   rc |= make_tmap_2d(&maps.dO, dO, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
+  maps.dq = maps.q;
+  if (HD <= 64)
+    rc |= make_tmap_2d(&maps.dq, dq_acc, HD, rows, uint64_t(HD) * 4, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B,
+                       CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
   if (rc) return set_error(MEA_ERR_CUDA, "attention backward: tensor map encode failed");
   AttnBwdParams p;
   p.B = B;

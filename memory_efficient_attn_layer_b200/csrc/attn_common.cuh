@@ -9,6 +9,18 @@
 
 namespace mea {
 
+// Pairs of each 16-score softmax chunk whose exp2 runs as a polynomial on the
+// FMA pipe (bit e = pair e, exp2_poly2); the rest use MUFU ex2.  Three of eight
+// roughly balances the two pipes.
+constexpr uint32_t kPolyPairs = 0x4A;
+
+// exp2 of a pair, on the FMA pipe when `poly` (argument clamped at -127, where
+// the result is negligible next to the row's largest term) else on MUFU.
+__device__ __forceinline__ float2 exp2_pair(float2 t, bool poly) {
+  if (poly) return exp2_poly2(make_float2(fmaxf(t.x, -127.f), fmaxf(t.y, -127.f)));
+  return make_float2(ex2(t.x), ex2(t.y));
+}
+
 template <int HD>
 struct HeadTile {
   static constexpr int SWB = HD * 2 >= 128 ? 128 : HD * 2;   // bytes per swizzled row

@@ -13,10 +13,17 @@
 // rings; warp 1 issues S_j = Q K_j^T and then O += P_j V_j with P read straight
 // from TMEM (the softmax warps overwrite S_j with bf16 P_j in place; S_{j+1}
 // is issued after PV_j, and tcgen05 MMAs of one thread run in issue order);
-// warps 2..5 run the online softmax, one query row per thread.  The running
-// max is refreshed lazily: O and the row sum are rescaled only when a row's max
-// grows by more than 2^8 (every P value stays <= 256).  Key tiles above the
+// warps 2..5 run the softmax, one query row per thread.  Key tiles above the
 // diagonal are never loaded (causal skipping); the diagonal tile is masked.
+//
+// The reference value subtracted before exp2 is one of:
+// * a bound on every scaled score of the call (forward of the block: q and k
+//   are RMS-normalised per head, so the rotary tables bound |q.k|): one pass
+//   over each score row, no row max, no rescaling of O;
+// * the saved row log-sum-exp (the backward's recompute): P comes out
+//   normalised, exactly the P the attention backward rebuilds;
+// * the online running max, refreshed lazily: O and the row sum are rescaled
+//   only when a row's max grows by more than 2^8 (every P value stays <= 256).
 //
 // Outputs: gated[b, t, h*N + n] = (O/l)[n] * gs[b,h,t,n] (bf16), the row
 // log-sum-exp in log2 units lse2 = m + log2(l) (fp32, [B,H,T]), and
@@ -32,8 +39,10 @@ struct AttnFwdParams {
   float scale_log2;         // softmax scale * log2(e)
   const __nv_bfloat16* gs;  // sigmoid(g), [B,H,T,N]
   __nv_bfloat16* gated;     // [B,T,H*N]
-  float* lse2;              // [B,H,T]
+  float* lse2;              // [B,H,T]; NULL when lse_in is given
   __nv_bfloat16* o_out;     // optional [B,H,T,N]
+  const float* bound;       // optional device scalar: bound on every scaled score (log2 units)
+  const float* lse_in;      // optional saved lse2: normalised recompute
   int* status;
 };
 
@@ -96,7 +105,8 @@ __device__ __forceinline__ void exp_chunk(const uint32_t (&v)[16], uint32_t sb, 
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const float2 t = ffma2(make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), scale2, bias2);
-    float p0 = ex2(t.x), p1 = ex2(t.y);
+    const float2 pp = exp2_pair(t, (kPolyPairs >> e) & 1);
+    float p0 = pp.x, p1 = pp.y;
     if (DIAG) {
       const int c0 = 16 * c + 2 * e;
       p0 = c0 > r ? 0.f : p0;
@@ -272,6 +282,21 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     const int r = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
+    const int t = qt * 128 + r;
+    const size_t bht = size_t(bh) * p.T + t;
+    // Reference for exp2 (uniform over the CTA): 2 = saved LSE, 1 = score bound, 0 = online max.
+    int mode = 0;
+    float ref = 0.f;
+    if (p.lse_in) {
+      mode = 2;
+      ref = p.lse_in[bht];
+    } else if (p.bound) {
+      const float bnd = __ldg(p.bound);
+      if (bnd <= ATTN_MAX_BOUND) {
+        mode = 1;
+        ref = bnd;
+      }
+    }
     float m_run = -INFINITY, l_run = 0.f;  // m_run in scaled log2 units
     bool ok = true;
     for (int j = 0; j < nkv && ok; ++j) {
@@ -280,6 +305,14 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       tc_fence_after();
       const uint32_t sb = lane_base + Cfg::S_COL;
       const bool diag = (j == qt);
+      if (mode != 0) {
+        // Fixed reference: one pass, P = exp2(s*c - ref) <= 1 (up to bf16 rounding of q, k).
+        l_run += diag ? exp_pack_row<true>(sb, r, sl2, -ref) : exp_pack_row<false>(sb, r, sl2, -ref);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full);
+        continue;
+      }
       const float mx = (diag ? score_row_max<true>(sb, r) : score_row_max<false>(sb, r)) * sl2;
       // Lazy rescale: refresh the reference max only when it grows by > 8 (log2 units).
       const bool need = mx > m_run + 8.0f;
@@ -311,9 +344,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     if (ok) {
       tc_fence_after();
       const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
-      const int t = qt * 128 + r;
-      const size_t bht = size_t(bh) * p.T + t;
-      const float inv_l = 1.0f / l_run;
+      if (mode != 0) m_run = ref;
+      const float inv_l = mode == 2 ? 1.0f : 1.0f / l_run;
       const __nv_bfloat16* gsrow = p.gs + bht * HD;
       __nv_bfloat16* grow = p.gated + (size_t(b) * p.T + t) * size_t(p.H * HD) + size_t(h) * HD;
       __nv_bfloat16* orow = p.o_out ? p.o_out + bht * HD : nullptr;
@@ -339,7 +371,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
           st_global_v4(orow + c + 8, oo[4], oo[5], oo[6], oo[7]);
         }
       }
-      p.lse2[bht] = m_run + __log2f(l_run);
+      if (p.lse2) p.lse2[bht] = m_run + __log2f(l_run);
     }
     if (!ok) g.ok = false;
   }
@@ -364,7 +396,7 @@ static int launch_attn_fwd_t(const AttnFwdMaps& maps, const AttnFwdParams& p, cu
 }
 
 int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* gs, void* gated,
-                 float* lse2, void* o_out, int* status, cudaStream_t st) {
+                 float* lse2, void* o_out, const float* bound, const float* lse_in, int* status, cudaStream_t st) {
   if (HD != 32 && HD != 64 && HD != 128)
     return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "attention: head dim %d not in {32, 64, 128}", HD);
   if (T % 128 != 0 || T <= 0 || B <= 0 || H <= 0)
@@ -385,8 +417,10 @@ int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, cons
   p.scale_log2 = 1.4426950408889634f / sqrtf(float(HD));
   p.gs = static_cast<const __nv_bfloat16*>(gs);
   p.gated = static_cast<__nv_bfloat16*>(gated);
-  p.lse2 = lse2;
   p.o_out = static_cast<__nv_bfloat16*>(o_out);
+  p.bound = lse_in ? nullptr : bound;
+  p.lse_in = lse_in;
+  p.lse2 = lse_in ? nullptr : lse2;
   p.status = status;
   switch (HD) {
     case 32: return launch_attn_fwd_t<32>(maps, p, st);

@@ -215,8 +215,56 @@ __global__ void cast_f32_bf16_kernel(long long n, const float* __restrict__ src,
 }
 
 // ---------------------------------------------------------------------------
+// Upper bound on every scaled attention score, from the rotary tables.
+//
+// q and k reach the attention after the parameter-free per-head RMSNorm
+// (||x_n||^2 = N ms / (ms + eps) < N) and the rotary x*f1 + swap(x)*f2, which
+// maps each pair (x_2i, x_2i+1) through M = [[f1_2i, f2_2i], [f2_2i+1,
+// f1_2i+1]].  Hence ||q_t|| <= sigma_max(t) sqrt(N) with sigma_max^2 the larger
+// eigenvalue of M^T M, (F + sqrt(F^2 - 4 det^2)) / 2 with F = ||M||_F^2, and
+// |q_t . k_s| * scale <= max_t sigma_max^2 * N / sqrt(N).  The bound (in log2
+// units, with 1% + 0.05 of slack for the bf16 rounding of q and k) lets the
+// attention forward use one fixed reference for exp2 instead of a running max.
+// One CTA; every table row below T is read once.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) rope_bound_kernel(int T, int HD, const __nv_bfloat16* __restrict__ f1,
+                                                         const __nv_bfloat16* __restrict__ f2, long long ldf,
+                                                         float* __restrict__ out) {
+  __shared__ float red[16];
+  const int pairs = HD / 2;
+  float s2 = 0.f;
+  for (int i = threadIdx.x; i < T * pairs; i += blockDim.x) {
+    const int t = i / pairs, e = 2 * (i - t * pairs);
+    const __nv_bfloat16* r1 = f1 + size_t(t) * ldf + e;
+    const __nv_bfloat16* r2 = f2 + size_t(t) * ldf + e;
+    const float a = __bfloat162float(r1[0]), d = __bfloat162float(r1[1]);
+    const float b = __bfloat162float(r2[0]), c = __bfloat162float(r2[1]);
+    const float fro = a * a + b * b + c * c + d * d;
+    const float det = a * d - b * c;
+    const float disc = fmaxf(fro * fro - 4.f * det * det, 0.f);
+    s2 = fmaxf(s2, 0.5f * (fro + sqrtf(disc)));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s2 = fmaxf(s2, __shfl_xor_sync(0xffffffffu, s2, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s2;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.f;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+    *out = (m * sqrtf(float(HD)) * 1.4426950408889634f) * 1.01f + 0.05f;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
+int run_rope_bound(int T, int HD, const void* f1, const void* f2, long long ldf, float* out, cudaStream_t st) {
+  if (T <= 0 || HD % 2 || !f1 || !f2 || !out) return set_error(MEA_ERR_INVALID_ARGUMENT, "rope bound: bad arguments");
+  rope_bound_kernel<<<1, 512, 0, st>>>(T, HD, static_cast<const __nv_bfloat16*>(f1),
+                                       static_cast<const __nv_bfloat16*>(f2), ldf, out);
+  return check_launch("rope_bound_kernel");
+}
+
 int run_rmsnorm_fwd(int rows, int C, float eps, const void* x, void* xn, float* r, cudaStream_t st) {
   if (C % 8 || C <= 0 || rows <= 0) return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "rmsnorm: C=%d must be a multiple of 8", C);
   const int threads = 256;

@@ -41,8 +41,13 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st);
 int auto_splits(int m_tiles, int n_tiles, int kb_total, int waves);
 
 // ---- attention (attn_fwd.cu, attn_bwd.cu) ----
+// Reference for the exponentials: `lse_in` (the saved row log-sum-exp; O comes
+// out normalised and lse2 is not written), else `*bound` when it is at most
+// ATTN_MAX_BOUND (a device scalar bounding every scaled score), else the
+// online running max.  Both pointers may be NULL.
+constexpr float ATTN_MAX_BOUND = 50.f;
 int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* gs, void* gated,
-                 float* lse2, void* o_out, int* status, cudaStream_t st);
+                 float* lse2, void* o_out, const float* bound, const float* lse_in, int* status, cudaStream_t st);
 int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
                  const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv, int* status,
                  cudaStream_t st);
@@ -54,5 +59,7 @@ int run_qk_norm_rope_bwd(int B, int H, int T, int HD, const float* dq_acc, const
                          const void* k_rot, const float* rq, const float* rk, const void* f1, const void* f2,
                          long long ldf, void* dacc, long long ld_dacc, float* df1, float* df2, cudaStream_t st);
 int run_cast_f32_bf16(long long n, const float* src, void* dst, cudaStream_t st);
+// *out = bound (log2 units) on every scaled score q.k/sqrt(N) of the block.
+int run_rope_bound(int T, int HD, const void* f1, const void* f2, long long ldf, float* out, cudaStream_t st);
 
 }  // namespace mea

@@ -140,6 +140,12 @@ __device__ __forceinline__ void bulk_reduce_add_f32(void* dst, uint32_t src, uin
   asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;"
                ::"l"(dst), "r"(src), "r"(bytes) : "memory");
 }
+// Tiled TMA reduce-add (fp32 add into global) of one box from shared memory;
+// completion tracked by the issuing thread's bulk group.
+__device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, uint32_t src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(tmap), "r"(src), "r"(c0), "r"(c1) : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -299,6 +305,46 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
       : "=f"(d.x), "=f"(d.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
+}
+// a + b rounded toward -infinity, two lanes.
+__device__ __forceinline__ float2 fadd2_rm(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rm.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fsub2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// 2^x for two lanes on the FMA pipe, to offload part of a softmax row from the
+// MUFU unit (ex2 issues at 16 lanes/clk/SM, an f32x2 FMA at 128).
+// Cody-Waite split x = n + f with n = floor(x) (x + 1.5*2^23 rounded toward
+// -inf puts n in the low mantissa bits) and f in [0, 1); 2^f from a degree-3
+// polynomial fitted to 2^f on [0, 1] by Lawson's iteratively reweighted least
+// squares for minimax relative error (8.4e-5, well under bf16's 2^-9); 2^n is
+// added to the exponent field as an integer.  Valid for x in [-126, 127]:
+// callers clamp x from below when it is not bounded.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  const float2 magic = make_float2(12582912.f, 12582912.f);
+  const float2 t = fadd2_rm(x, magic);                   // 1.5*2^23 + floor(x)
+  const float2 f = fsub2(x, fsub2(t, magic));            // x - floor(x)
+  float2 p = ffma2(make_float2(7.808303833e-02f, 7.808303833e-02f), f,
+                   make_float2(2.261252254e-01f, 2.261252254e-01f));
+  p = ffma2(p, f, make_float2(6.957332492e-01f, 6.957332492e-01f));
+  p = ffma2(p, f, make_float2(9.999415278e-01f, 9.999415278e-01f));
+  // bits(t) << 23 == floor(x) << 23 (mod 2^32): the magic's own bits shift out.
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

@@ -72,6 +72,15 @@ def test_block_nonorthogonal_table_is_exact():
     check(run_block(inp, 2, 64), block_fwd_bwd(inp, 2, 64), ["y", *GRAD_NAMES])
 
 
+def test_block_large_table_takes_online_max():
+    """Tables of magnitude 1.9 at N=128 put the score bound sigma^2 sqrt(N) log2(e)
+    at ~59.6 > 50 (log2 units), where exp2 against the bound could underflow
+    whole rows: the forward then falls back to the online row max and must
+    still match."""
+    inp = make_inputs(1, 256, 256, 2, 128, seed=12, mscale=1.9)
+    check(run_block(inp, 2, 128), block_fwd_bwd(inp, 2, 128), ["y", *GRAD_NAMES])
+
+
 def test_block_without_factor_grads():
     inp = make_inputs(1, 256, 256, 4, 64, seed=8)
     got = run_block(inp, 4, 64, factor_grads=False)
