@@ -20,9 +20,12 @@
 // P/dS tile stores need; for N = 128 (no room for the staging tile) the warps
 // issue vector red.global.add directly.
 //
-// Warps: 0 TMA, 1 MMA issue, 2..9 softmax: query row = TMEM lane, warps 2..5
-// take key columns [0,64) and warps 6..9 [64,128) (two warps per SM
-// sub-partition, so one can issue while the other waits).
+// Warps (four warpgroups, registers rebalanced with setmaxnreg): warpgroup 0 =
+// warp 0 TMA, warp 1 MMA issue (warps 2, 3 idle); warpgroups 1-2 = softmax:
+// query row = TMEM lane, warps 4..7 take key columns [0,64) and warps 8..11
+// [64,128) (two warps per SM sub-partition, so one can issue while the other
+// waits); warpgroup 3 = dQ read-out, one query row per thread, off the softmax
+// warps' critical path.
 //
 // Schedules (TMEM has 512 columns):
 //  * N <= 64 ("overlapped"): S [0,128), dP [128,256), dS [256,320), dV, dK, dQ
@@ -146,16 +149,14 @@ __device__ __forceinline__ void bwd_half_row(uint32_t s_addr, uint32_t dp_addr, 
   }
 }
 
-// Add this thread's share of a dQ tile (row r, columns [hh*HD/2, (hh+1)*HD/2),
-// scaled) into the fp32 accumulator row.
+// Add row r of a dQ tile (all HD columns, scaled) into the fp32 accumulator row.
 template <int HD>
-__device__ __forceinline__ void dq_readout(uint32_t dq_addr, int hh, float* dqrow, float scale) {
-  constexpr int HALF = HD / 2;
+__device__ __forceinline__ void dq_readout(uint32_t dq_addr, float* dqrow, float scale) {
 #pragma unroll
-  for (int c = 0; c < HALF; c += 16) {
+  for (int c = 0; c < HD; c += 16) {
     uint32_t v[16];
-    tmem_load16(dq_addr + hh * HALF + c, v);
-    float* dst = dqrow + hh * HALF + c;
+    tmem_load16(dq_addr + c, v);
+    float* dst = dqrow + c;
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       red_add_v4_f32(dst + 4 * j, __uint_as_float(v[4 * j]) * scale, __uint_as_float(v[4 * j + 1]) * scale,
@@ -163,18 +164,16 @@ __device__ __forceinline__ void dq_readout(uint32_t dq_addr, int hh, float* dqro
   }
 }
 
-// Stage this thread's share of a dQ tile (row r, columns [hh*HD/2, (hh+1)*HD/2),
-// scaled) into the fp32 staging tile: HD/32 boxes of 128 rows x 128 bytes in
-// the 128-byte swizzle the TMA reduce-add unswizzles (16-byte unit u of row r
-// at u ^ (r & 7)).
+// Stage row r of a dQ tile (all HD columns, scaled) into the fp32 staging tile:
+// HD/32 boxes of 128 rows x 128 bytes in the 128-byte swizzle the TMA
+// reduce-add unswizzles (16-byte unit u of row r at u ^ (r & 7)).
 template <int HD>
-__device__ __forceinline__ void dq_stage(uint32_t dq_addr, int hh, int r, uint32_t stg, float scale) {
-  constexpr int HALF = HD / 2;
+__device__ __forceinline__ void dq_stage(uint32_t dq_addr, int r, uint32_t stg, float scale) {
 #pragma unroll
-  for (int c = 0; c < HALF; c += 16) {
+  for (int c = 0; c < HD; c += 16) {
     uint32_t v[16];
-    tmem_load16(dq_addr + hh * HALF + c, v);
-    const int col0 = hh * HALF + c;
+    tmem_load16(dq_addr + c, v);
+    const int col0 = c;
     const uint32_t row = stg + (col0 >> 5) * 16384 + r * 128;
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -188,7 +187,7 @@ __device__ __forceinline__ void dq_stage(uint32_t dq_addr, int hh, int r, uint32
 }
 
 template <int HD>
-__global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant__ AttnBwdMaps maps, const AttnBwdParams p) {
+__global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant__ AttnBwdMaps maps, const AttnBwdParams p) {
   using Cfg = AttnBwdCfg<HD>;
   using Tile = HeadTile<HD>;
   constexpr int STAGES = Cfg::STAGES;
@@ -241,10 +240,10 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
     mbar_init(st_full, 1);
     mbar_init(ds_full, 256);
     mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 256);
+    mbar_init(dq_empty, 128);
     mbar_init(drain_bar, 1);
     mbar_init(st_empty, 256);
-    mbar_init(stg_full, 256);
+    mbar_init(stg_full, 128);
     mbar_init(stg_empty, 1);
     fence_mbar_init();
   }
@@ -258,7 +257,22 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
   const uint32_t tmem = *tmem_slot;
   Guard g(p.status, KID_ATTN_BWD);
 
-  if (warp == 0) {
+  // Each warpgroup ends here: TMEM is freed once every warp is done with it.
+  auto finish = [&]() {
+    tc_fence_before();
+    named_bar_sync(1, 512);
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
+  };
+  // Register shares per warpgroup (launched with 512 threads x 128 = 65536):
+  // 128 x 72 (TMA/MMA) + 256 x 184 (softmax) + 128 x 72 (dQ) = 65536.  Each role
+  // sets its share first and ends in `finish`, so every role is compiled
+  // against its own budget.
+  if (warp < 4) {
+    reg_dealloc<72>();
+    if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (elect_one()) {
       tma_prefetch_desc(&maps.q);
@@ -357,43 +371,21 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
         mbar_drain(drain_bar, 0);
       }
     }
-  } else {
-    // ---------------- softmax warps 2..9 ----------------
-    // Query row r = TMEM lane; warps 2..5 take key columns [0, 64), warps 6..9
+    }
+    finish();
+    return;
+  }
+  if (warp < 12) {
+    reg_alloc<184>();
+    // ---------------- softmax warps 4..11 ----------------
+    // Query row r = TMEM lane; warps 4..7 take key columns [0, 64), warps 8..11
     // [64, 128), so each sub-partition runs two softmax warps.  The same warps
-    // add each finished dQ tile into global memory and write dK / dV at the end.
+    // write dK / dV at the end.
     const int quarter = warp & 3;
-    const int hh = (warp - 2) >> 2;
+    const int hh = (warp - 4) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
-    const bool lead = (warp == 2 && lane == 0);  // issues the dQ reduce-adds
-    const uint32_t stg = base + Cfg::OFF_DQ;
-    // dQ tile k out of TMEM into the staging tile, then one TMA reduce-add per
-    // 32-column box.  The staging tile is reused once the previous reduce-add has
-    // read it (stg_empty); the lead thread waits for all 256 writers (stg_full).
-    auto dq_out_tma = [&](int k) -> bool {
-      if (k > 0) {
-        if (lead) {
-          bulk_wait_read0();
-          mbar_arrive(stg_empty);
-        }
-        if (!__all_sync(0xffffffffu, mbar_wait(stg_empty, (k - 1) & 1, g, 13))) return false;
-      }
-      dq_stage<HD>(lane_base + Cfg::DQ_COL, hh, r, stg, p.scale);
-      tc_fence_before();
-      mbar_arrive(dq_empty);
-      fence_proxy_async_smem();
-      mbar_arrive(stg_full);
-      if (lead) {
-        if (!mbar_wait(stg_full, k & 1, g, 14)) return false;
-        const int qrow = row0 + (jt + k) * 128;
-#pragma unroll
-        for (int bx = 0; bx < HD / 32; ++bx) tma_reduce_add_2d(&maps.dq, stg + bx * 16384, bx * 32, qrow);
-        bulk_commit();
-      }
-      return true;
-    };
     bool ok = true;
     for (int n = 0; n < nsteps; ++n) {
       const int s = n % STAGES;
@@ -429,42 +421,12 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
-      // dQ read-out: tile n-1 (already complete) when overlapped, else tile n.
-      const int nq_out = OVERLAP ? n - 1 : n;
-      if (nq_out >= 0) {
-        if (!OVERLAP) {
-          ok = __all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, g, 9));
-          if (!ok) break;
-          tc_fence_after();
-        }
-        if constexpr (Cfg::TMA_DQ) {
-          ok = dq_out_tma(nq_out);
-          if (!ok) break;
-        } else {
-          dq_readout<HD>(lane_base + Cfg::DQ_COL, hh, p.dq_acc + (size_t(row0) + size_t(jt + nq_out) * 128 + r) * HD,
-                         p.scale);
-          tc_fence_before();
-          mbar_arrive(dq_empty);
-        }
-      }
     }
-    if (ok && OVERLAP) {  // the last dQ tile
+    if (ok) {  // every MMA of the walk has completed with the last dq_full
       ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (nsteps - 1) & 1, g, 11));
-      if (ok) {
-        tc_fence_after();
-        if constexpr (Cfg::TMA_DQ) {
-          ok = dq_out_tma(nsteps - 1);
-        } else {
-          dq_readout<HD>(lane_base + Cfg::DQ_COL, hh,
-                         p.dq_acc + (size_t(row0) + size_t(jt + nsteps - 1) * 128 + r) * HD, p.scale);
-        }
-      }
+      if (ok) tc_fence_after();
     }
-    if constexpr (Cfg::TMA_DQ) {
-      if (lead) bulk_wait0();  // every reduce-add has landed before the CTA exits
-    }
-    // dK (scaled) and dV for key row r, columns [hh*HD/2, (hh+1)*HD/2): every MMA
-    // completed with the last dq_full.
+    // dK (scaled) and dV for key row r, columns [hh*HD/2, (hh+1)*HD/2).
     if (ok) {
       constexpr int HALF = HD / 2;
       const int b = bh / p.H, h = bh - b * p.H;
@@ -489,13 +451,62 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_kernel(const __grid_constant_
       }
     }
     if (!ok) g.ok = false;
+    finish();
+    return;
   }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  {
+    reg_dealloc<72>();
+    // ---------------- dQ read-out warps 12..15 ----------------
+    // Row r of each finished dQ tile out of TMEM (dq_full), scaled, added into
+    // the fp32 accumulator: N <= 64 through the staging tile and one TMA
+    // reduce-add per 32-column box (the lead thread waits for all 128 writers,
+    // stg_full, and the tile is reused once the previous reduce-add has read it,
+    // stg_empty); N = 128 with vector red.global.add.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+    const bool lead = (warp == 12 && lane == 0);
+    const uint32_t stg = base + Cfg::OFF_DQ;
+    bool ok = true;
+    for (int k = 0; k < nsteps && ok; ++k) {
+      ok = __all_sync(0xffffffffu, mbar_wait(dq_full, k & 1, g, 9));
+      if (!ok) break;
+      tc_fence_after();
+      if constexpr (Cfg::TMA_DQ) {
+        if (k > 0) {
+          if (lead) {
+            bulk_wait_read0();
+            mbar_arrive(stg_empty);
+          }
+          ok = __all_sync(0xffffffffu, mbar_wait(stg_empty, (k - 1) & 1, g, 13));
+          if (!ok) break;
+        }
+        dq_stage<HD>(lane_base + Cfg::DQ_COL, r, stg, p.scale);
+        tc_fence_before();
+        mbar_arrive(dq_empty);
+        fence_proxy_async_smem();
+        mbar_arrive(stg_full);
+        if (lead) {
+          ok = mbar_wait(stg_full, k & 1, g, 14);
+          if (ok) {
+            const int qrow = row0 + (jt + k) * 128;
+#pragma unroll
+            for (int bx = 0; bx < HD / 32; ++bx) tma_reduce_add_2d(&maps.dq, stg + bx * 16384, bx * 32, qrow);
+            bulk_commit();
+          }
+        }
+        ok = __all_sync(0xffffffffu, ok);
+      } else {
+        dq_readout<HD>(lane_base + Cfg::DQ_COL, p.dq_acc + (size_t(row0) + size_t(jt + k) * 128 + r) * HD, p.scale);
+        tc_fence_before();
+        mbar_arrive(dq_empty);
+      }
+    }
+    if constexpr (Cfg::TMA_DQ) {
+      if (lead) bulk_wait0();  // every reduce-add has landed before the CTA exits
+    }
+    if (!ok) g.ok = false;
+    finish();
   }
 }
 
@@ -507,7 +518,7 @@ static int launch_attn_bwd_t(const AttnBwdMaps& maps, const AttnBwdParams& p, cu
   if (!smem_attr_set(reinterpret_cast<const void*>(kern), int(Cfg::SMEM)))
     return set_error(MEA_ERR_CUDA, "cudaFuncSetAttribute(attn_bwd) failed");
   const int grid = p.B * p.H * (p.T / 128);
-  kern<<<grid, 320, Cfg::SMEM, st>>>(maps, p);
+  kern<<<grid, 512, Cfg::SMEM, st>>>(maps, p);
   return check_launch("attn_bwd_kernel");
 }
 

@@ -109,6 +109,18 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// Per-warpgroup register budget (executed by all four warps of a warpgroup).
+// The increases draw on what the decreases release from the launch's
+// threads x registers, so the shares must add up to at most that total.
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
