@@ -6,15 +6,21 @@
 // (fast_triton_attn.py:559-570).
 //
 // One CTA = one (b, h, 128-row query tile), two CTAs per SM: each holds 256
-// TMEM columns (score tile S [0,128) and output O [128, 128+N)), so while one
-// CTA's softmax warps work on exponentials the other CTA's MMAs keep the
-// tensor core busy, and one CTA's prologue/epilogue overlaps the other's
-// main loop.  Warp 0 loads Q once and streams K and V through separate TMA
-// rings; warp 1 issues S_j = Q K_j^T and then O += P_j V_j with P read straight
-// from TMEM (the softmax warps overwrite S_j with bf16 P_j in place; S_{j+1}
-// is issued after PV_j, and tcgen05 MMAs of one thread run in issue order);
-// warps 2..5 run the softmax, one query row per thread.  Key tiles above the
-// diagonal are never loaded (causal skipping); the diagonal tile is masked.
+// TMEM columns, so while one CTA's softmax warps work on exponentials the
+// other CTA's MMAs keep the tensor core busy, and one CTA's prologue/epilogue
+// overlaps the other's main loop.  Warp 0 loads Q once and streams K and V
+// through separate TMA rings; warp 1 issues S_j = Q K_j^T and O += P_j V_j with
+// P read straight from TMEM; warps 2..5 run the softmax, one query row per
+// thread.  Key tiles above the diagonal are never loaded (causal skipping); the
+// diagonal tile is masked.
+//
+// TMEM, N <= 64: S [0,128), P [128,192), O [192, 192+N).  The softmax warps
+// build a whole row of bf16 P in registers, release S_j (s_empty) once read,
+// so S_{j+1} = Q K_{j+1}^T runs while they finish, and write P_j into its own
+// columns once PV_{j-1} has consumed the previous P (pv_done): the per-tile
+// chain is softmax + S MMA, with PV off it.  N = 128 (O needs 128 columns): S
+// [0,128) with P written over it in place, O [128,256); S_{j+1} is issued after
+// PV_j (tcgen05 MMAs of one thread run in issue order).
 //
 // The reference value subtracted before exp2 is one of:
 // * a bound on every scaled score of the call (forward of the block: q and k
@@ -55,7 +61,8 @@ struct AttnFwdCfg {
   static constexpr int KS = HD <= 64 ? 2 : 1;  // K ring depth
   static constexpr int VS = HD <= 64 ? 2 : 1;  // V ring depth
   static constexpr uint32_t TILE_BYTES = 128 * HD * 2;
-  static constexpr uint32_t S_COL = 0, O_COL = 128;
+  static constexpr bool SEP_P = HD <= 64;  // P in its own TMEM columns
+  static constexpr uint32_t S_COL = 0, P_COL = SEP_P ? 128 : 0, O_COL = SEP_P ? 192 : 128;
   static constexpr uint32_t TMEM_COLS = 256;
   static constexpr size_t SMEM = 1024 + TILE_BYTES * (1 + KS + VS) + 256;
 };
@@ -142,6 +149,46 @@ __device__ __forceinline__ float exp_pack_row(uint32_t sb, int r, float sl2, flo
   return (acc0.x + acc0.y) + (acc1.x + acc1.y);
 }
 
+// P = exp2(s * sl2 - m) for one row into registers (packed bf16 pairs, key
+// columns [2i, 2i+2) in pk[i]); returns the row sum of P.  Every TMEM load of
+// the score row has completed on return.
+template <bool DIAG>
+__device__ __forceinline__ float exp_row_regs(uint32_t sb, int r, float sl2, float neg_m, uint32_t (&pk)[64]) {
+  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+  const float2 scale2 = make_float2(sl2, sl2), bias2 = make_float2(neg_m, neg_m);
+  uint32_t a[16], b[16];
+  auto chunk = [&](const uint32_t(&v)[16], int c) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float2 t = ffma2(make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), scale2, bias2);
+      const float2 pp = exp2_pair(t, (kPolyPairs >> e) & 1);
+      float p0 = pp.x, p1 = pp.y;
+      if (DIAG) {
+        const int c0 = 16 * c + 2 * e;
+        p0 = c0 > r ? 0.f : p0;
+        p1 = c0 + 1 > r ? 0.f : p1;
+      }
+      if (e & 1)
+        acc1 = fadd2(acc1, make_float2(p0, p1));
+      else
+        acc0 = fadd2(acc0, make_float2(p0, p1));
+      pk[8 * c + e] = pack_bf16(p0, p1);
+    }
+  };
+  tmem_ld16(sb, a);
+  tmem_wait_ld_tied(a);
+#pragma unroll
+  for (int c = 0; c < 8; c += 2) {
+    tmem_ld16(sb + 16 * (c + 1), b);
+    chunk(a, c);
+    tmem_wait_ld_tied(b);
+    if (c + 2 < 8) tmem_ld16(sb + 16 * (c + 2), a);
+    chunk(b, c + 1);
+    if (c + 2 < 8) tmem_wait_ld_tied(a);
+  }
+  return (acc0.x + acc0.y) + (acc1.x + acc1.y);
+}
+
 template <int HD>
 __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ AttnFwdMaps maps, const AttnFwdParams p) {
   using Cfg = AttnFwdCfg<HD>;
@@ -167,7 +214,9 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
   const uint32_t p_full = s_full + 8;
   const uint32_t o_bar = s_full + 16;
   const uint32_t drain_bar = s_full + 24;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5 + 2 * KS + 2 * VS);
+  const uint32_t s_empty = s_full + 32;  // (SEP_P) softmax has read S_j
+  const uint32_t pv_done = s_full + 40;  // (SEP_P) PV_j has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7 + 2 * KS + 2 * VS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -195,6 +244,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     mbar_init(p_full, 128);
     mbar_init(o_bar, 1);
     mbar_init(drain_bar, 1);
+    mbar_init(s_empty, 128);
+    mbar_init(pv_done, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -248,7 +299,41 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     // ---------------- MMA issuer ----------------
     if (elect_one()) {
       bool any = false;
-      if (mbar_wait(q_full, 0, g, 5)) {
+      auto issue_s = [&](int j) {
+        const int sk = j % KS;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          mma_ss(tmem + Cfg::S_COL, Tile::kmajor(sQ, 128, kk), Tile::kmajor(sK + sk * TB, 128, kk), IDESC_S,
+                 kk > 0 ? 1u : 0u);
+        mma_commit(k_empty(sk));
+        mma_commit(s_full);
+      };
+      if constexpr (Cfg::SEP_P) {
+        if (mbar_wait(q_full, 0, g, 5) && mbar_wait(k_full(0), 0, g, 2)) {
+          tc_fence_after();
+          issue_s(0);
+          any = true;
+          for (int j = 0; j < nkv; ++j) {
+            const int sv = j % VS;
+            if (j + 1 < nkv) {  // S_{j+1} as soon as S_j has been read
+              if (!mbar_wait(s_empty, j & 1, g, 10)) break;
+              if (!mbar_wait(k_full((j + 1) % KS), ((j + 1) / KS) & 1, g, 2)) break;
+              tc_fence_after();
+              issue_s(j + 1);
+            }
+            if (!mbar_wait(p_full, j & 1, g, 3)) break;
+            if (!mbar_wait(v_full(sv), (j / VS) & 1, g, 4)) break;
+            tc_fence_after();
+#pragma unroll
+            for (int kc = 0; kc < 8; ++kc)
+              mma_ts(tmem + Cfg::O_COL, tmem + Cfg::P_COL + kc * 8, Tile::mnmajor(sV + sv * TB, 128, kc), IDESC_O,
+                     (j > 0 || kc > 0) ? 1u : 0u);
+            mma_commit(v_empty(sv));
+            mma_commit(pv_done);
+          }
+          if (g.ok) mma_commit(o_bar);
+        }
+      } else if (mbar_wait(q_full, 0, g, 5)) {
         for (int j = 0; j < nkv; ++j) {
           const int sk = j % KS, sv = j % VS;
           if (!mbar_wait(k_full(sk), (j / KS) & 1, g, 2)) break;
@@ -299,6 +384,57 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     }
     float m_run = -INFINITY, l_run = 0.f;  // m_run in scaled log2 units
     bool ok = true;
+    if constexpr (Cfg::SEP_P) {
+      const uint32_t sb = lane_base + Cfg::S_COL;
+      for (int j = 0; j < nkv && ok; ++j) {
+        ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, g, 6));
+        if (!ok) break;
+        tc_fence_after();
+        const bool diag = (j == qt);
+        bool pv_seen = (j == 0);  // PV_{j-1} has completed (O and the P columns are free)
+        if (mode == 0) {
+          const float mx = (diag ? score_row_max<true>(sb, r) : score_row_max<false>(sb, r)) * sl2;
+          // Lazy rescale: refresh the reference max only when it grows by > 8 (log2 units).
+          const bool need = mx > m_run + 8.0f;
+          if (__any_sync(0xffffffffu, need)) {
+            const float m_new = need ? mx : m_run;
+            const float alpha = ex2(m_run - m_new);  // 0 when m_run = -inf
+            if (j > 0) {
+              ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, g, 11));
+              if (!ok) break;
+              tc_fence_after();
+              pv_seen = true;
+#pragma unroll
+              for (int c = 0; c < HD; c += 16) {
+                uint32_t ov[16];
+                tmem_load16(lane_base + Cfg::O_COL + c, ov);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+                tmem_st16(lane_base + Cfg::O_COL + c, ov);
+              }
+            }
+            l_run *= alpha;
+            m_run = m_new;
+          }
+        }
+        const float neg_m = mode != 0 ? -ref : -m_run;
+        uint32_t pk[64];
+        l_run += diag ? exp_row_regs<true>(sb, r, sl2, neg_m, pk) : exp_row_regs<false>(sb, r, sl2, neg_m, pk);
+        tc_fence_before();
+        mbar_arrive(s_empty);  // S_j fully read: S_{j+1} may overwrite it
+        if (!pv_seen) {
+          ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, g, 12));
+          if (!ok) break;
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+          tmem_st16(lane_base + Cfg::P_COL + 16 * q4, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * q4));
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full);
+      }
+    } else
     for (int j = 0; j < nkv && ok; ++j) {
       ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, g, 6));
       if (!ok) break;
