@@ -227,31 +227,53 @@ __global__ void cast_f32_bf16_kernel(long long n, const float* __restrict__ src,
 // attention forward use one fixed reference for exp2 instead of a running max.
 // One CTA; every table row below T is read once.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) rope_bound_kernel(int T, int HD, const __nv_bfloat16* __restrict__ f1,
-                                                         const __nv_bfloat16* __restrict__ f2, long long ldf,
-                                                         float* __restrict__ out) {
-  __shared__ float red[16];
-  const int pairs = HD / 2;
+__device__ __forceinline__ float pair_sigma2(float a, float d, float b, float c) {
+  const float fro = a * a + b * b + c * c + d * d;
+  const float det = a * d - b * c;
+  return 0.5f * (fro + sqrtf(fmaxf(fro * fro - 4.f * det * det, 0.f)));
+}
+
+// One CTA of 1024 threads; each thread reads 16-byte pieces (4 rotary pairs of
+// each table), all of its loads issued before any is used.
+__global__ void __launch_bounds__(1024) rope_bound_kernel(int T, int HD, const __nv_bfloat16* __restrict__ f1,
+                                                          const __nv_bfloat16* __restrict__ f2, long long ldf,
+                                                          float* __restrict__ out) {
+  __shared__ float red[32];
+  const int per_row = HD / 8;  // 16-byte pieces per table row
+  const int n = T * per_row;
   float s2 = 0.f;
-  for (int i = threadIdx.x; i < T * pairs; i += blockDim.x) {
-    const int t = i / pairs, e = 2 * (i - t * pairs);
-    const __nv_bfloat16* r1 = f1 + size_t(t) * ldf + e;
-    const __nv_bfloat16* r2 = f2 + size_t(t) * ldf + e;
-    const float a = __bfloat162float(r1[0]), d = __bfloat162float(r1[1]);
-    const float b = __bfloat162float(r2[0]), c = __bfloat162float(r2[1]);
-    const float fro = a * a + b * b + c * c + d * d;
-    const float det = a * d - b * c;
-    const float disc = fmaxf(fro * fro - 4.f * det * det, 0.f);
-    s2 = fmaxf(s2, 0.5f * (fro + sqrtf(disc)));
+  constexpr int U = 4;
+  for (int base = threadIdx.x; base < n; base += U * blockDim.x) {
+    uint4 a[U], b[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < n) {
+        const int t = i / per_row, e = (i - t * per_row) * 8;
+        a[u] = __ldg(reinterpret_cast<const uint4*>(f1 + size_t(t) * ldf + e));
+        b[u] = __ldg(reinterpret_cast<const uint4*>(f2 + size_t(t) * ldf + e));
+      } else {
+        a[u] = make_uint4(0, 0, 0, 0);
+        b[u] = a[u];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t wa[4] = {a[u].x, a[u].y, a[u].z, a[u].w}, wb[4] = {b[u].x, b[u].y, b[u].z, b[u].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)  // pair (2i, 2i+1): f1 = (lo, hi) of wa[q], f2 = (lo, hi) of wb[q]
+        s2 = fmaxf(s2, pair_sigma2(bf16_lo(wa[q]), bf16_hi(wa[q]), bf16_lo(wb[q]), bf16_hi(wb[q])));
+    }
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) s2 = fmaxf(s2, __shfl_xor_sync(0xffffffffu, s2, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s2;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float m = 0.f;
-    for (int w = 0; w < int(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
-    *out = (m * sqrtf(float(HD)) * 1.4426950408889634f) * 1.01f + 0.05f;
+  if (threadIdx.x < 32) {
+    float m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0) *out = (m * sqrtf(float(HD)) * 1.4426950408889634f) * 1.01f + 0.05f;
   }
 }
 
@@ -259,8 +281,11 @@ __global__ void __launch_bounds__(512) rope_bound_kernel(int T, int HD, const __
 // Launchers
 // ---------------------------------------------------------------------------
 int run_rope_bound(int T, int HD, const void* f1, const void* f2, long long ldf, float* out, cudaStream_t st) {
-  if (T <= 0 || HD % 2 || !f1 || !f2 || !out) return set_error(MEA_ERR_INVALID_ARGUMENT, "rope bound: bad arguments");
-  rope_bound_kernel<<<1, 512, 0, st>>>(T, HD, static_cast<const __nv_bfloat16*>(f1),
+  if (T <= 0 || HD % 8 || ldf % 8 || !f1 || !f2 || !out)
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "rope bound: bad arguments");
+  if ((reinterpret_cast<uintptr_t>(f1) | reinterpret_cast<uintptr_t>(f2)) & 15)
+    return set_error(MEA_ERR_ALIGNMENT, "rope bound: tables must be 16-byte aligned");
+  rope_bound_kernel<<<1, 1024, 0, st>>>(T, HD, static_cast<const __nv_bfloat16*>(f1),
                                        static_cast<const __nv_bfloat16*>(f2), ldf, out);
   return check_launch("rope_bound_kernel");
 }
