@@ -7,7 +7,8 @@
 One step = forward + backward of the block (fast_triton_attn.py:374-675) over
 one batch of synthetic input already resident in HBM, through the public
 autograd API; with N > 1 ranks the batch is sharded by sequence (B per rank
-fixed: weak scaling) and the five weight gradients are all-reduced over NCCL.
+fixed: weak scaling) and the five weight gradients are all-reduced over NCCL
+as one coalesced fp32 bucket (memory_efficient_attn_layer_b200.dp).
 
 --impl reference : the reference path's CPU implementation timed on the host
                    cores (the eager block restated in oracle/eager.py), on a
@@ -40,7 +41,14 @@ CONFIGS = {
     "c4": dict(B=4, T=16384, C=2048, H=16, N=128, name="c4: long-context block B=4 T=16384 C=2048 H=16 N=128"),
     "c5": dict(B=128, T=2048, C=768, H=12, N=64, name="c5: DP block, global B=1024 T=2048 C=768 H=12 N=64 (B=128 per GPU at 8 GPUs)"),
 }
-LAUNCHES_PER_STAGE = {"bwd.cast": 5, "bwd.memset": 0}
+LAUNCHES_PER_STAGE = {"bwd.cast": 5, "bwd.memset": 0, "fwd.attention": 2}
+# DRAM bytes per launch and per sequence, dram__bytes.sum from ncu captures of the c2 kernels at
+# B=16 (every sequence is independent, so the traffic scales with B); the roofline's "traffic".
+DRAM_BYTES_PER_SEQ = {
+    "c2": {"bwd.attention_bwd": 295.1e6 / 16, "fwd.attention": 154.6e6 / 16,
+           "bwd.attention_recompute": 179.1e6 / 16, "fwd.qkvg_gemm": 116.8e6 / 16,
+           "bwd.qk_norm_rope_bwd": 216.5e6 / 16},
+}
 
 
 def model_flops(B, T, C, H, N):
@@ -216,6 +224,7 @@ def run_gpu(args, cfg, rank, world, device):
     import torch.distributed as dist
 
     from memory_efficient_attn_layer_b200 import FusedAttentionFunction, _lib
+    from memory_efficient_attn_layer_b200.dp import allreduce_grads
 
     B, T, C, H, N = (cfg[k] for k in ("B", "T", "C", "H", "N"))
     tokens_rank = B * T
@@ -231,8 +240,7 @@ def run_gpu(args, cfg, rank, world, device):
         y = fwd(inp)
         y.backward(grad)
         if world > 1:
-            for w in ws:
-                dist.all_reduce(w.grad)
+            allreduce_grads(ws)
         for w in ws:
             w.grad = None
         return y
@@ -296,8 +304,7 @@ def run_gpu(args, cfg, rank, world, device):
         loss = (y * dyd).sum(dtype=torch.float32)
         loss.backward()
         if world > 1:
-            for w in ws:
-                dist.all_reduce(w.grad)
+            allreduce_grads(ws)
         for w in ws:
             w.grad = None
         loss_h.copy_(loss.detach().view(1), non_blocking=True)
@@ -354,17 +361,19 @@ def run_gpu(args, cfg, rank, world, device):
         line["stages"] = table
         top = max(stages, key=lambda k: stages[k][0])
         avg = stages[top][0] / stages[top][1]
+        per_seq = DRAM_BYTES_PER_SEQ.get(cfg.get("key", ""), {}).get(top)
+        traffic = per_seq * B if per_seq else None
         if top in sf:
             ach = sf[top] / (avg / 1e3) / 1e12
             line["roofline"] = {"kernel": top, "bound": "tensor", "achieved": ach,
                                 "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                                "frac": ach / peaks["bf16_tflops_sustained"], "traffic": None,
+                                "frac": ach / peaks["bf16_tflops_sustained"], "traffic": traffic,
                                 "peak_source": peaks["source"] + " sustained",
                                 "algorithmic": f"{sf[top]:.4g} flop per launch"}
         else:
             ach = sb[top] / (avg / 1e3) / 1e9
             line["roofline"] = {"kernel": top, "bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"],
-                                "unit": "GB/s", "frac": ach / peaks["hbm_gbs"], "traffic": None,
+                                "unit": "GB/s", "frac": ach / peaks["hbm_gbs"], "traffic": traffic,
                                 "peak_source": peaks["source"]}
         line["gpu_launches"] = sum(cnt * LAUNCHES_PER_STAGE.get(n, 1) for n, (_, cnt) in stages.items())
     line["e2e"] = {"value": e2e_value, "unit": "tokens/s",
@@ -391,7 +400,7 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    cfg = dict(CONFIGS[args.config])
+    cfg = dict(CONFIGS[args.config], key=args.config)
     if args.batch > 0:
         cfg["B"] = args.batch
         cfg["name"] += f" [batch override B={args.batch}]"

@@ -1,0 +1,66 @@
+"""Host side of the data-parallel path on CPU: two gloo ranks exchange the
+weight gradients through allreduce_grads (coalesced fp32 bucket, mean), the
+call the GPU bench makes over NCCL after every backward."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from memory_efficient_attn_layer_b200.dp import allreduce_grads
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _grads_for(rank):
+    g = torch.Generator().manual_seed(100 + rank)
+    shapes = [(64, 32), (64, 32), (64, 32), (64, 32), (32, 64)]
+    out = []
+    for i, sh in enumerate(shapes):
+        p = torch.zeros(sh, dtype=torch.bfloat16 if i < 4 else torch.float32, requires_grad=True)
+        p.grad = torch.randn(sh, generator=g).to(p.dtype)
+        out.append(p)
+    out.append(torch.zeros(3, requires_grad=True))  # no gradient: skipped
+    return out
+
+
+def _worker(rank, world, port, average, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        params = _grads_for(rank)
+        allreduce_grads(params, average=average)
+        q.put((rank, [p.grad.float() if p.grad is not None else None for p in params]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("average", [True, False])
+def test_allreduce_grads_two_ranks(average):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, average, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = [_grads_for(r) for r in range(world)]
+    for i in range(5):
+        want = sum(ref[r][i].grad.float() for r in range(world))
+        if average:
+            want = want / world
+        want = want.to(ref[0][i].grad.dtype).float()  # written back in the parameter's dtype
+        for r in range(world):
+            assert torch.equal(results[r][i], want), (i, r)
+    assert results[0][5] is None and results[1][5] is None
