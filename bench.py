@@ -291,34 +291,58 @@ def run_gpu(args, cfg, rank, world, device):
     ms_step = ms / args.steps
     value = world * tokens_rank * args.steps / (ms / 1e3)
 
-    # ---- end to end through the public API: pinned host input -> device, fwd+bwd, loss back to host
+    # ---- end to end through the public API: every step's x and dy come from pinned host memory and
+    # its loss goes back to the host.  Inputs are double-buffered: step i+1's host->device copy runs on
+    # a copy stream while step i computes (as a data loader feeding a training step would), each copy
+    # ordered after the step that last read its buffer.
     xh = x.detach().cpu().pin_memory()
     dyh = dy.detach().cpu().pin_memory()
     loss_h = torch.empty(1, dtype=torch.float32).pin_memory()
     e2e_steps = max(3, args.steps // 10)
+    comp = torch.cuda.current_stream(device)
+    copy_stream = torch.cuda.Stream(device)
+    xbuf = [torch.empty_like(x) for _ in range(2)]
+    dybuf = [torch.empty_like(dy) for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        xd = xh.to(device, non_blocking=True)
-        dyd = dyh.to(device, non_blocking=True)
-        y = fwd(xd)
-        loss = (y * dyd).sum(dtype=torch.float32)
+    def e2e_copy(i):
+        b = i % 2
+        with torch.cuda.stream(copy_stream):
+            if i >= 2:
+                copy_stream.wait_event(consumed[b])
+            xbuf[b].copy_(xh, non_blocking=True)
+            dybuf[b].copy_(dyh, non_blocking=True)
+            copied[b].record(copy_stream)
+
+    def e2e_step(i, n):
+        b = i % 2
+        if i + 1 < n:
+            e2e_copy(i + 1)
+        comp.wait_event(copied[b])
+        y = fwd(xbuf[b])
+        loss = (y * dybuf[b]).sum(dtype=torch.float32)
         loss.backward()
+        consumed[b].record(comp)
         if world > 1:
             allreduce_grads(ws)
         for w in ws:
             w.grad = None
         loss_h.copy_(loss.detach().view(1), non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
+    def e2e_run(n):
+        e2e_copy(0)
+        for i in range(n):
+            e2e_step(i, n)
+
+    e2e_run(2)
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
+    e0.record(comp)
+    e2e_run(e2e_steps)
+    e1.record(comp)
     torch.cuda.synchronize(device)
     ems = e0.elapsed_time(e1)
     if world > 1:
@@ -379,8 +403,9 @@ def run_gpu(args, cfg, rank, world, device):
     line["e2e"] = {"value": e2e_value, "unit": "tokens/s",
                    "h2d_bytes_per_step": world * (x.numel() * x.element_size() + dy.numel() * dy.element_size()),
                    "d2h_bytes_per_step": world * 4,
-                   "path": "FusedAttentionFunction.apply + loss=(y*dy).sum() + backward, pinned host x/dy copied in, "
-                           "loss copied out, every step"}
+                   "path": "FusedAttentionFunction.apply + loss=(y*dy).sum() + backward; every step's x and dy "
+                           "copied in from pinned host memory (double-buffered: the next step's copy overlaps this "
+                           "step's compute) and its loss copied out"}
     line["clocks"] = clk
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(cfg)
