@@ -307,6 +307,12 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
         mbar_drain(kv_full, 0);
         for (int s = 0; s < STAGES; ++s)
           if (last_par[s] >= 0) mbar_drain(qdo_full(s), uint32_t(last_par[s]));
+      } else {
+        // Tail: wait for the MMA warp's release (tcgen05.commit) of every Q/dO
+        // slot's last fill, so no asynchronous arrive targets this CTA's shared
+        // memory after it exits.
+        for (int s = 0; s < STAGES; ++s)
+          if (last_par[s] >= 0) mbar_wait(qdo_empty(s), uint32_t(last_par[s]), g, 15);
       }
     }
   } else if (warp == 1) {

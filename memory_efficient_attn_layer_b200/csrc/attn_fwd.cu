@@ -293,6 +293,14 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
           if (kpar[s] >= 0) mbar_drain(k_full(s), uint32_t(kpar[s]));
         for (int s = 0; s < VS; ++s)
           if (vpar[s] >= 0) mbar_drain(v_full(s), uint32_t(vpar[s]));
+      } else {
+        // Tail: wait for the MMA warp's release (tcgen05.commit) of the last K and
+        // V tile of every ring slot, so no asynchronous arrive targets this CTA's
+        // shared memory after it exits.
+        for (int s = 0; s < KS; ++s)
+          if (kpar[s] >= 0) mbar_wait(k_empty(s), uint32_t(kpar[s]), g, 13);
+        for (int s = 0; s < VS; ++s)
+          if (vpar[s] >= 0) mbar_wait(v_empty(s), uint32_t(vpar[s]), g, 14);
       }
     }
   } else if (warp == 1) {
@@ -477,6 +485,9 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     }
     // ---- epilogue: O / l, gate, repack ----
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_bar, 0, g, 8));
+    if constexpr (Cfg::SEP_P) {  // the last PV's own completion arrive, before the CTA can exit
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkv - 1) & 1, g, 15));
+    }
     if (ok) {
       tc_fence_after();
       const int b = bh / p.H, h = bh - (bh / p.H) * p.H;

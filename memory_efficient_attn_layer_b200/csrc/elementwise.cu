@@ -105,7 +105,9 @@ __global__ void rmsnorm_bwd_kernel(int rows, int C, const __nv_bfloat16* __restr
 //
 // Grid: x = position t, y = chunk of the B*H rows; each block loops over its
 // (b,h) rows at fixed t so the table gradients reduce in registers and leave
-// the block with one atomic per (t, n).
+// the block with one atomic per (t, n).  Each thread owns 8 consecutive
+// elements (4 pairs) of a row: 16-byte loads of q, k, dk and two of dq, and the
+// loads of U rows are issued before any of them is used.
 // ---------------------------------------------------------------------------
 template <int HD>
 __global__ void __launch_bounds__(256) qk_bwd_kernel(int BH, int H, int T, int bh_per_block,
@@ -118,20 +120,31 @@ __global__ void __launch_bounds__(256) qk_bwd_kernel(int BH, int H, int T, int b
                                                      const __nv_bfloat16* __restrict__ f2, long long ldf,
                                                      __nv_bfloat16* __restrict__ dacc, long long ld_dacc,
                                                      float* __restrict__ df1, float* __restrict__ df2) {
-  constexpr int TPR = HD / 2 < 32 ? HD / 2 : 32;  // threads per row
-  constexpr int EPT = HD / TPR;                    // elements per thread (2 or 4)
-  constexpr int RPB = 256 / TPR;                   // rows in flight per block
+  constexpr int EPT = 8;             // elements per thread
+  constexpr int TPR = HD / EPT;      // threads per row (4, 8, 16)
+  constexpr int RPB = 256 / TPR;     // rows per pass of the block
+  constexpr int U = 2;               // passes whose loads are in flight together
   const int t = blockIdx.x;
   const int sub = threadIdx.x % TPR;
   const int grp = threadIdx.x / TPR;
   const int n0 = sub * EPT;
   const int HN = H * HD;
 
-  float tf1[EPT], tf2[EPT];
+  // This position's table entries for our 4 pairs, and each pair's inverse (recovers qn from q_rot).
+  float tf1[EPT], tf2[EPT], inv[EPT / 2];
+  {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(f1 + size_t(t) * ldf + n0));
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(f2 + size_t(t) * ldf + n0));
+    const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-  for (int e = 0; e < EPT; ++e) {
-    tf1[e] = __bfloat162float(f1[size_t(t) * ldf + n0 + e]);
-    tf2[e] = __bfloat162float(f2[size_t(t) * ldf + n0 + e]);
+    for (int q = 0; q < 4; ++q) {
+      tf1[2 * q] = bf16_lo(wa[q]);
+      tf1[2 * q + 1] = bf16_hi(wa[q]);
+      tf2[2 * q] = bf16_lo(wb[q]);
+      tf2[2 * q + 1] = bf16_hi(wb[q]);
+      const float det = tf1[2 * q] * tf1[2 * q + 1] - tf2[2 * q] * tf2[2 * q + 1];
+      inv[q] = fabsf(det) > 1e-30f ? 1.0f / det : 0.f;
+    }
   }
   float a1[EPT], a2[EPT];
 #pragma unroll
@@ -141,50 +154,79 @@ __global__ void __launch_bounds__(256) qk_bwd_kernel(int BH, int H, int T, int b
   const int bh_end = min(bh_begin + bh_per_block, BH);
   // Trip count is uniform across the block so the row shuffles below always
   // see every lane; lanes past the end work on zeros and store nothing.
-  for (int base = bh_begin; base < bh_end; base += RPB) {
-    const int bh = base + grp;
-    const bool valid = bh < bh_end;
-    const size_t row = size_t(valid ? bh : bh_begin) * T + t;
-    const int b = (valid ? bh : bh_begin) / H, h = (valid ? bh : bh_begin) % H;
-    __nv_bfloat16* drow = dacc + (size_t(b) * T + t) * ld_dacc + size_t(h) * HD + n0;
+  for (int base = bh_begin; base < bh_end; base += U * RPB) {
+    float4 gq[U][2];
+    uint4 gk[U], yq[U], yk[U];
+    float r_q[U], r_k[U];
 #pragma unroll
-    for (int which = 0; which < 2; ++which) {
-      float g[EPT], y[EPT];
-      const __nv_bfloat16* src = (which == 0 ? q_rot : k_rot) + row * HD + n0;
-#pragma unroll
-      for (int e = 0; e < EPT; ++e) {
-        g[e] = !valid ? 0.f : (which == 0 ? dq_acc[row * HD + n0 + e] : __bfloat162float(dk[row * HD + n0 + e]));
-        y[e] = !valid ? 0.f : __bfloat162float(src[e]);
+    for (int u = 0; u < U; ++u) {
+      const int bh = base + u * RPB + grp;
+      const size_t row = size_t(bh) * T + t;
+      if (bh < bh_end) {
+        const float4* dqp = reinterpret_cast<const float4*>(dq_acc + row * HD + n0);
+        gq[u][0] = __ldg(dqp);
+        gq[u][1] = __ldg(dqp + 1);
+        gk[u] = __ldg(reinterpret_cast<const uint4*>(dk + row * HD + n0));
+        yq[u] = __ldg(reinterpret_cast<const uint4*>(q_rot + row * HD + n0));
+        yk[u] = __ldg(reinterpret_cast<const uint4*>(k_rot + row * HD + n0));
+        r_q[u] = __ldg(rq + row);
+        r_k[u] = __ldg(rk + row);
+      } else {
+        gq[u][0] = gq[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        gk[u] = yq[u] = yk[u] = make_uint4(0, 0, 0, 0);
+        r_q[u] = r_k[u] = 0.f;
       }
-      const float r = valid ? (which == 0 ? rq : rk)[row] : 0.f;
-      float dot = 0.f;
+    }
 #pragma unroll
-      for (int e = 0; e < EPT; ++e) dot = fmaf(g[e], y[e], dot);
+    for (int u = 0; u < U; ++u) {
+      const int bh = base + u * RPB + grp;
+      const bool valid = bh < bh_end;
+      const int b = valid ? bh / H : 0, h = valid ? bh - (bh / H) * H : 0;
+      __nv_bfloat16* drow = dacc + (size_t(b) * T + t) * ld_dacc + size_t(h) * HD + n0;
 #pragma unroll
-      for (int o = TPR / 2; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o, TPR);
-      const float kk = dot / float(HD);
-      uint32_t out[EPT / 2];
+      for (int which = 0; which < 2; ++which) {
+        float g[EPT], y[EPT];
+        const uint4 yv = which == 0 ? yq[u] : yk[u];
+        const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
+        if (which == 0) {
+          const float4 g0 = gq[u][0], g1 = gq[u][1];
+          g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w;
+          g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+        } else {
+          const uint32_t gw[4] = {gk[u].x, gk[u].y, gk[u].z, gk[u].w};
 #pragma unroll
-      for (int e = 0; e < EPT; e += 2) {
-        const float fe1 = tf1[e], fo1 = tf1[e + 1], fe2 = tf2[e], fo2 = tf2[e + 1];
-        const float det = fe1 * fo1 - fe2 * fo2;
-        const float inv = fabsf(det) > 1e-30f ? 1.0f / det : 0.f;
-        const float qa = (fo1 * y[e] - fe2 * y[e + 1]) * inv;
-        const float qb = (fe1 * y[e + 1] - fo2 * y[e]) * inv;
-        const float da = fe1 * g[e] + fo2 * g[e + 1];
-        const float db = fe2 * g[e] + fo1 * g[e + 1];
-        out[e / 2] = pack_bf16(r * (da - qa * kk), r * (db - qb * kk));
-        a1[e] = fmaf(g[e], qa, a1[e]);
-        a1[e + 1] = fmaf(g[e + 1], qb, a1[e + 1]);
-        a2[e] = fmaf(g[e], qb, a2[e]);
-        a2[e + 1] = fmaf(g[e + 1], qa, a2[e + 1]);
-      }
-      __nv_bfloat16* d = drow + (which == 0 ? 0 : HN);
-      if (valid) {
-        if (EPT == 2)
-          *reinterpret_cast<uint32_t*>(d) = out[0];
-        else
-          *reinterpret_cast<uint2*>(d) = make_uint2(out[0], out[EPT / 2 - 1]);
+          for (int q = 0; q < 4; ++q) {
+            g[2 * q] = bf16_lo(gw[q]);
+            g[2 * q + 1] = bf16_hi(gw[q]);
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          y[2 * q] = bf16_lo(yw[q]);
+          y[2 * q + 1] = bf16_hi(yw[q]);
+        }
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) dot = fmaf(g[e], y[e], dot);
+#pragma unroll
+        for (int o = TPR / 2; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o, TPR);
+        const float kk = dot / float(HD);
+        const float r = which == 0 ? r_q[u] : r_k[u];
+        uint32_t out[EPT / 2];
+#pragma unroll
+        for (int e = 0; e < EPT; e += 2) {
+          const float fe1 = tf1[e], fo1 = tf1[e + 1], fe2 = tf2[e], fo2 = tf2[e + 1], iv = inv[e / 2];
+          const float qa = (fo1 * y[e] - fe2 * y[e + 1]) * iv;
+          const float qb = (fe1 * y[e + 1] - fo2 * y[e]) * iv;
+          const float da = fe1 * g[e] + fo2 * g[e + 1];
+          const float db = fe2 * g[e] + fo1 * g[e + 1];
+          out[e / 2] = pack_bf16(r * (da - qa * kk), r * (db - qb * kk));
+          a1[e] = fmaf(g[e], qa, a1[e]);
+          a1[e + 1] = fmaf(g[e + 1], qb, a1[e + 1]);
+          a2[e] = fmaf(g[e], qb, a2[e]);
+          a2[e + 1] = fmaf(g[e + 1], qa, a2[e + 1]);
+        }
+        if (valid) st_global_v4(drow + (which == 0 ? 0 : HN), out[0], out[1], out[2], out[3]);
       }
     }
   }
@@ -313,8 +355,14 @@ int run_qk_norm_rope_bwd(int B, int H, int T, int HD, const float* dq_acc, const
                          const void* k_rot, const float* rq, const float* rk, const void* f1, const void* f2,
                          long long ldf, void* dacc, long long ld_dacc, float* df1, float* df2, cudaStream_t st) {
   const int BH = B * H;
-  const int bh_per_block = BH < 64 ? BH : 64;
+  // 2 passes x 256/(HD/8) rows per block iteration, 4 iterations per block at most
+  const int rows_per_iter = 2 * 256 / (HD / 8);
+  const int bh_per_block = BH < 4 * rows_per_iter ? BH : 4 * rows_per_iter;
   dim3 grid(T, (BH + bh_per_block - 1) / bh_per_block);
+  if ((reinterpret_cast<uintptr_t>(dq_acc) | reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(q_rot) |
+       reinterpret_cast<uintptr_t>(k_rot) | reinterpret_cast<uintptr_t>(f1) | reinterpret_cast<uintptr_t>(f2) |
+       reinterpret_cast<uintptr_t>(dacc)) & 15 || ldf % 8 || ld_dacc % 8)
+    return set_error(MEA_ERR_ALIGNMENT, "qk backward: operands must be 16-byte aligned");
   auto f1p = static_cast<const __nv_bfloat16*>(f1);
   auto f2p = static_cast<const __nv_bfloat16*>(f2);
   auto dkp = static_cast<const __nv_bfloat16*>(dk);

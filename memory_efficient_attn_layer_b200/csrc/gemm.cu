@@ -1,4 +1,6 @@
 // Host-side set-up and dispatch of the tcgen05 GEMM (gemm.cuh).
+#include <cstdio>
+
 #include "gemm.cuh"
 #include "launch.h"
 #include "tma.h"
@@ -14,7 +16,10 @@ static int launch_gemm_t(const GemmMaps& maps, const GemmParams& p, cudaStream_t
   const int ntiles = p.m_tiles * p.n_tiles * p.k_splits;
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
   kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(maps, p);
-  return check_launch("gemm_kernel");
+  char what[96];
+  snprintf(what, sizeof(what), "gemm_kernel<%d,%d,%d,%d,%d> M=%d N=%d K=%d splits=%d", BN, AM, BMD, EPI, HD, p.M, p.N,
+           p.K, p.k_splits);
+  return check_launch(what);
 }
 
 #define MEA_GEMM_CASE(BN_, AM_, BMD_, EPI_)                                   \

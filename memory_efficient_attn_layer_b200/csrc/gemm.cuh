@@ -436,6 +436,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
         // Abort: let every copy this thread issued land before the CTA exits.
         for (int s = 0; s < STAGES; ++s)
           if (last_par[s] >= 0) mbar_drain(full_bar(s), uint32_t(last_par[s]));
+      } else {
+        // Tail: wait for the MMA warp's release (tcgen05.commit) of every stage's
+        // last fill, so no asynchronous arrive targets this CTA's shared memory
+        // after it exits.
+        for (int s = 0; s < STAGES; ++s)
+          if (last_par[s] >= 0) mbar_wait(empty_bar(s), uint32_t(last_par[s]), g, 6);
       }
     }
   } else if (warp == 1) {
