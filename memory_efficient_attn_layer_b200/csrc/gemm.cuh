@@ -219,6 +219,87 @@ __device__ __forceinline__ void qkvg_slab(const GemmParams& p, uint32_t tcol, ui
   }
 }
 
+// The same for head dims <= 64, with one TMEM round trip per slab: the whole
+// row of the slab is loaded at once (both 32-column chunks in flight), the
+// rotary-table row is fetched alongside so its latency overlaps the TMEM wait,
+// and the values stay in registers from the sum of squares to the rotary.
+template <int HD, bool QK>
+__device__ __forceinline__ void qkvg_slab_row(const GemmParams& p, uint32_t tcol, uint32_t slab, int typ, int r,
+                                              int swz, float rs, size_t bht, const __nv_bfloat16* f1row,
+                                              const __nv_bfloat16* f2row) {
+  static_assert(HD == 32 || HD == 64, "row-at-once slab: head dim 32 or 64");
+  constexpr int SWB = HD >= 64 ? 128 : 64;
+  constexpr int NCH = HD / 32;
+  uint32_t v[NCH][32];
+  uint4 w1[HD / 8], w2[HD / 8];
+#pragma unroll
+  for (int ci = 0; ci < NCH; ++ci) tmem_ld32(tcol + 32 * ci, v[ci]);
+  if (QK) {
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      w1[j] = __ldg(reinterpret_cast<const uint4*>(f1row) + j);
+      w2[j] = __ldg(reinterpret_cast<const uint4*>(f2row) + j);
+    }
+  }
+#pragma unroll
+  for (int ci = 0; ci < NCH; ++ci) tmem_wait_ld_tied(v[ci]);
+  float sc = rs;
+  if (QK) {
+    float ss0 = 0.f, ss1 = 0.f;
+#pragma unroll
+    for (int ci = 0; ci < NCH; ++ci)
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const float x0 = __uint_as_float(v[ci][j]) * rs, x1 = __uint_as_float(v[ci][j + 1]) * rs;
+        ss0 = fmaf(x0, x0, ss0);
+        ss1 = fmaf(x1, x1, ss1);
+      }
+    const float inv = rsqrtf((ss0 + ss1) / float(HD) + p.eps);
+    float* rdst = typ == 0 ? p.rq : p.rk;
+    if (rdst) rdst[bht] = inv;
+    sc = rs * inv;
+  }
+#pragma unroll
+  for (int ci = 0; ci < NCH; ++ci) {
+    const int c = 32 * ci;
+    uint32_t pk[16];
+    if (QK) {
+#pragma unroll
+      for (int v4 = 0; v4 < 4; ++v4) {
+        const uint4 a1 = w1[ci * 4 + v4], a2 = w2[ci * 4 + v4];
+        const uint32_t x1[4] = {a1.x, a1.y, a1.z, a1.w}, x2[4] = {a2.x, a2.y, a2.z, a2.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = v4 * 4 + e;
+          const float qa = round_bf16(__uint_as_float(v[ci][2 * j]) * sc);
+          const float qb = round_bf16(__uint_as_float(v[ci][2 * j + 1]) * sc);
+          pk[j] = pack_bf16(qa * bf16_lo(x1[e]) + qb * bf16_lo(x2[e]), qb * bf16_hi(x1[e]) + qa * bf16_hi(x2[e]));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float a = __uint_as_float(v[ci][2 * j]) * rs;
+        float bb = __uint_as_float(v[ci][2 * j + 1]) * rs;
+        if (typ == 3) {
+          a = __fdividef(1.0f, 1.0f + __expf(-a));
+          bb = __fdividef(1.0f, 1.0f + __expf(-bb));
+        }
+        pk[j] = pack_bf16(a, bb);
+      }
+    }
+    const uint32_t row_addr = slab + (c >> 6) * (GEMM_BM * SWB) + r * SWB;
+    const int u0 = (c & 63) >> 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t addr = row_addr + (((u0 + j) ^ swz) << 4);
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(pk[4 * j]), "r"(pk[4 * j + 1]),
+                   "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
+                   : "memory");
+    }
+  }
+}
+
 // q/k RMSNorm over the head dim, bf16 rounding of the normed value, then
 // interleaved rotary out[n] = qn[n]*f1[t,n] + qn[n^1]*f2[t,n]
 // (fast_triton_attn.py:102-106, :132-141); v stored as is (fast_triton_attn.py:108)
@@ -239,19 +320,32 @@ __device__ __forceinline__ void epi_qkvg_staged(const GemmParams& p, uint32_t ta
   const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
   const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
   const int swz = SWB == 128 ? (r & 7) : ((r >> 1) & 3);
+  if constexpr (HD <= 64) {
 #pragma unroll 1
-  for (int s = wg; s < NSLAB; s += 2) {
-    const int sg = n0 / HD + s;
-    if ((sg & 3) < 2)
-      qkvg_slab<HD, true>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs,
-                          (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row, t1, t2);
-  }
+    for (int s = wg; s < NSLAB; s += 2) {
+      const int sg = n0 / HD + s;
+      if ((sg & 3) < 2)
+        qkvg_slab_row<HD, true>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs,
+                                (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row);
+      else
+        qkvg_slab_row<HD, false>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs, 0, f1row,
+                                 f2row);
+    }
+  } else {
 #pragma unroll 1
-  for (int s = wg; s < NSLAB; s += 2) {
-    const int sg = n0 / HD + s;
-    if ((sg & 3) >= 2)
-      qkvg_slab<HD, false>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs, 0, f1row, f2row, t1,
-                           t2);
+    for (int s = wg; s < NSLAB; s += 2) {
+      const int sg = n0 / HD + s;
+      if ((sg & 3) < 2)
+        qkvg_slab<HD, true>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs,
+                            (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row, t1, t2);
+    }
+#pragma unroll 1
+    for (int s = wg; s < NSLAB; s += 2) {
+      const int sg = n0 / HD + s;
+      if ((sg & 3) >= 2)
+        qkvg_slab<HD, false>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs, 0, f1row, f2row,
+                             t1, t2);
+    }
   }
 }
 
@@ -501,7 +595,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
       // Projection epilogue: the rotary-table rows of this thread's token are
       // loaded before the accumulator wait, which hides their latency.
       uint4 pre1[2][4], pre2[2][4];
-      if constexpr (Cfg::STAGED) {
+      if constexpr (Cfg::STAGED && HD > 64) {
         const int t = (m0 + row) % p.T;
         const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
         const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
