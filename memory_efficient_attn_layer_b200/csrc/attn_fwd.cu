@@ -484,6 +484,12 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       mbar_arrive(p_full);
     }
     // ---- epilogue: O / l, gate, repack ----
+    // sigmoid(g) of this row is fetched while the last PV completes.
+    uint4 gv[HD / 8];
+    if (ok) {
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c) gv[c] = __ldg(reinterpret_cast<const uint4*>(p.gs + bht * HD) + c);
+    }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_bar, 0, g, 8));
     if constexpr (Cfg::SEP_P) {  // the last PV's own completion arrive, before the CTA can exit
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkv - 1) & 1, g, 15));
@@ -493,15 +499,13 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
       if (mode != 0) m_run = ref;
       const float inv_l = mode == 2 ? 1.0f : 1.0f / l_run;
-      const __nv_bfloat16* gsrow = p.gs + bht * HD;
       __nv_bfloat16* grow = p.gated + (size_t(b) * p.T + t) * size_t(p.H * HD) + size_t(h) * HD;
       __nv_bfloat16* orow = p.o_out ? p.o_out + bht * HD : nullptr;
 #pragma unroll
       for (int c = 0; c < HD; c += 16) {
         uint32_t ov[16];
         tmem_load16(lane_base + Cfg::O_COL + c, ov);
-        const uint4 g0 = *reinterpret_cast<const uint4*>(gsrow + c);
-        const uint4 g1 = *reinterpret_cast<const uint4*>(gsrow + c + 8);
+        const uint4 g0 = gv[c / 8], g1 = gv[c / 8 + 1];
         const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
         uint32_t go[8], oo[8];
 #pragma unroll
