@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Forward + backward throughput of one gated causal attention block on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|eager]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|eager|triton]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N
 
 One step = forward + backward of the block (fast_triton_attn.py:374-675) over
@@ -13,6 +13,9 @@ as one coalesced fp32 bucket (memory_efficient_attn_layer_b200.dp).
 --impl reference : the reference path's CPU implementation timed on the host
                    cores (the eager block restated in oracle/eager.py), on a
                    bounded sample (one sequence of the workload per step).
+--impl triton    : the reference's own GPU path, unmodified (fast_triton_attn.fused_attn, its Triton
+                   kernels + ATen flash attention), imported from baseline/_ref, on the same
+                   weights, tables and inputs; a comparator, like --impl eager.
 --impl eager     : the reference's eager GPU equivalent (README.md:42-64:
                    checkpointed norm/projections/rotary + SDPA flash + gated
                    o_proj) in plain PyTorch, as an informative comparator.
@@ -220,6 +223,18 @@ def eager_block(x, ws, yarn, H, N, eps=1e-6):
     return F.linear(o * torch.sigmoid(g), wo)
 
 
+def reference_triton_block():
+    """The reference's fused_attn (fast_triton_attn.py:681) from baseline/_ref, or None if absent."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.exists(os.path.join(ref_dir, "fast_triton_attn.py")):
+        return None
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    import fast_triton_attn
+
+    return fast_triton_attn.fused_attn
+
+
 def run_gpu(args, cfg, rank, world, device):
     import torch.distributed as dist
 
@@ -229,9 +244,24 @@ def run_gpu(args, cfg, rank, world, device):
     B, T, C, H, N = (cfg[k] for k in ("B", "T", "C", "H", "N"))
     tokens_rank = B * T
     x, ws, yarn, dy = make_block_inputs(cfg, device, rank)
-    eager = args.impl == "eager"
+    eager = args.impl in ("eager", "triton")  # comparators: no library profiler
+    ref_fused = None
+    if args.impl == "triton":
+        ref_fused = reference_triton_block()
+        if ref_fused is None:
+            if rank == 0:
+                print(json.dumps({"impl": "triton", "unavailable": "baseline/_ref/fast_triton_attn.py not installed"}))
+            return
+        lins = []
+        for w in ws:  # nn.Linear views of the same weight tensors (the reference reads .weight)
+            lin = torch.nn.Linear(w.shape[1], w.shape[0], bias=False, device=device, dtype=w.dtype)
+            lin.weight = torch.nn.Parameter(w.data, requires_grad=True)
+            lins.append(lin)
+        ws = [lin.weight for lin in lins]
 
     def fwd(inp):
+        if ref_fused is not None:
+            return ref_fused(inp, *lins, yarn, H, N)
         if eager:
             return eager_block(inp, ws, yarn, H, N)
         return FusedAttentionFunction.apply(inp, *ws, yarn.factor1, yarn.factor2, H, N, 1e-6)
@@ -365,7 +395,7 @@ def run_gpu(args, cfg, rank, world, device):
                    "l2": f"inputs larger than L2 (x is {2 * B * T * C / 1e6:.0f} MB per GPU), no flush"},
     }
     if eager:
-        line["impl"] = "eager"
+        line["impl"] = args.impl
     line["tensor_pipe_frac_step"] = {
         "achieved_tflops": F_step / (ms_step / 1e3) / 1e12, "peak_tflops": peaks["bf16_tflops_sustained"],
         "frac": F_step / (ms_step / 1e3) / 1e12 / peaks["bf16_tflops_sustained"],
@@ -403,7 +433,9 @@ def run_gpu(args, cfg, rank, world, device):
     line["e2e"] = {"value": e2e_value, "unit": "tokens/s",
                    "h2d_bytes_per_step": world * (x.numel() * x.element_size() + dy.numel() * dy.element_size()),
                    "d2h_bytes_per_step": world * 4,
-                   "path": "FusedAttentionFunction.apply + loss=(y*dy).sum() + backward; every step's x and dy "
+                   "path": {"ours": "FusedAttentionFunction.apply", "triton": "reference fast_triton_attn.fused_attn",
+                            "eager": "eager README block"}[args.impl]
+                           + " + loss=(y*dy).sum() + backward; every step's x and dy "
                            "copied in from pinned host memory (double-buffered: the next step's copy overlaps this "
                            "step's compute) and its loss copied out"}
     line["clocks"] = clk
@@ -417,7 +449,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", choices=["ours", "reference", "eager"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "eager", "triton"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0,
