@@ -165,11 +165,6 @@ static int qkvg(const mea_block_dims& d, const void* xn, const void* wq, const v
   L.b_rows = HN;
   L.slab_rows = d.N;
   L.k_splits = 1;
-  L.outs[0] = q;
-  L.outs[1] = k;
-  L.outs[2] = v;
-  L.outs[3] = gs;
-  L.out_rows = (long long)d.B * d.H * d.T;
   GemmParams p{};
   p.status = status;
   p.q = static_cast<__nv_bfloat16*>(q);

@@ -14,11 +14,10 @@
 //   dQ_i = dS K      (dS also written to TMEM as packed bf16: A operand from TMEM)
 // dK and dV stay in TMEM for the whole walk.  The softmax warps also add each
 // finished dQ_i tile (fp32) into the accumulator in global memory ([B,H,T,N],
-// zeroed by the caller) and finally write dK and dV.  For N <= 64 the dQ tile
-// is staged in swizzled shared memory and added by one TMA reduce-add per
-// 32-column box, which keeps the reductions off the load/store unit that the
-// P/dS tile stores need; for N = 128 (no room for the staging tile) the warps
-// issue vector red.global.add directly.
+// zeroed by the caller) and finally write dK and dV.  The dQ tile is staged in
+// swizzled shared memory (64 columns at a time: two rounds for N = 128) and
+// added by one TMA reduce-add per 32-column box, which keeps the reductions off
+// the load/store unit that the P/dS tile stores need.
 //
 // Warps (four warpgroups, registers rebalanced with setmaxnreg): warpgroup 0 =
 // warp 0 TMA, warp 1 MMA issue (warps 2, 3 idle); warpgroups 1-2 = softmax:
@@ -57,7 +56,7 @@ struct AttnBwdParams {
 
 struct AttnBwdMaps {
   CUtensorMap q, k, v, dO;
-  CUtensorMap dq;  // dq_acc as [B*H*T, N] fp32, 32x128 boxes, 128-byte swizzle (N <= 64)
+  CUtensorMap dq;  // dq_acc as [B*H*T, N] fp32, 32x128 boxes, 128-byte swizzle
 };
 
 template <int HD>
@@ -76,9 +75,10 @@ struct AttnBwdCfg {
   static constexpr uint32_t OFF_K = 0, OFF_V = TB, OFF_Q = 2 * TB, OFF_DO = OFF_Q + STAGES * TB;
   static constexpr uint32_t OFF_P = OFF_DO + STAGES * TB, OFF_DS = OFF_P + PT;
   static constexpr uint32_t OFF_LSE = OFF_DS + PT;
-  static constexpr bool TMA_DQ = OVERLAP;                      // dQ staged for a TMA reduce-add
-  static constexpr uint32_t OFF_DQ = OFF_LSE + STAGES * 1024;  // HD/32 boxes of [128 x 32] fp32
-  static constexpr uint32_t DQ_BYTES = TMA_DQ ? HD * 512 : 0;
+  static constexpr int DQ_COLS = HD < 64 ? HD : 64;             // dQ columns staged per round
+  static constexpr int DQ_ROUNDS = HD / DQ_COLS;                // rounds per dQ tile (2 for N = 128)
+  static constexpr uint32_t OFF_DQ = OFF_LSE + STAGES * 1024;   // DQ_COLS/32 boxes of [128 x 32] fp32
+  static constexpr uint32_t DQ_BYTES = DQ_COLS * 512;
   static constexpr uint32_t OFF_BAR = OFF_DQ + DQ_BYTES;
   static constexpr size_t SMEM = 1024 + OFF_BAR + 256;
 };
@@ -149,30 +149,15 @@ __device__ __forceinline__ void bwd_half_row(uint32_t s_addr, uint32_t dp_addr, 
   }
 }
 
-// Add row r of a dQ tile (all HD columns, scaled) into the fp32 accumulator row.
-template <int HD>
-__device__ __forceinline__ void dq_readout(uint32_t dq_addr, float* dqrow, float scale) {
+// Stage columns [c0, c0 + NC) of row r of a dQ tile (scaled) into the fp32
+// staging tile: NC/32 boxes of 128 rows x 128 bytes in the 128-byte swizzle the
+// TMA reduce-add unswizzles (16-byte unit u of row r at u ^ (r & 7)).
+template <int NC>
+__device__ __forceinline__ void dq_stage(uint32_t dq_addr, int c0, int r, uint32_t stg, float scale) {
 #pragma unroll
-  for (int c = 0; c < HD; c += 16) {
+  for (int c = 0; c < NC; c += 16) {
     uint32_t v[16];
-    tmem_load16(dq_addr + c, v);
-    float* dst = dqrow + c;
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      red_add_v4_f32(dst + 4 * j, __uint_as_float(v[4 * j]) * scale, __uint_as_float(v[4 * j + 1]) * scale,
-                     __uint_as_float(v[4 * j + 2]) * scale, __uint_as_float(v[4 * j + 3]) * scale);
-  }
-}
-
-// Stage row r of a dQ tile (all HD columns, scaled) into the fp32 staging tile:
-// HD/32 boxes of 128 rows x 128 bytes in the 128-byte swizzle the TMA
-// reduce-add unswizzles (16-byte unit u of row r at u ^ (r & 7)).
-template <int HD>
-__device__ __forceinline__ void dq_stage(uint32_t dq_addr, int r, uint32_t stg, float scale) {
-#pragma unroll
-  for (int c = 0; c < HD; c += 16) {
-    uint32_t v[16];
-    tmem_load16(dq_addr + c, v);
+    tmem_load16(dq_addr + c0 + c, v);
     const int col0 = c;
     const uint32_t row = stg + (col0 >> 5) * 16384 + r * 128;
 #pragma unroll
@@ -464,10 +449,10 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     reg_dealloc<72>();
     // ---------------- dQ read-out warps 12..15 ----------------
     // Row r of each finished dQ tile out of TMEM (dq_full), scaled, added into
-    // the fp32 accumulator: N <= 64 through the staging tile and one TMA
-    // reduce-add per 32-column box (the lead thread waits for all 128 writers,
-    // stg_full, and the tile is reused once the previous reduce-add has read it,
-    // stg_empty); N = 128 with vector red.global.add.
+    // the fp32 accumulator through the staging tile, 64 columns per round, and
+    // one TMA reduce-add per 32-column box (the lead thread waits for all 128
+    // writers, stg_full, and the tile is reused once the previous reduce-add
+    // has read it, stg_empty).
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
@@ -478,39 +463,39 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
       ok = __all_sync(0xffffffffu, mbar_wait(dq_full, k & 1, g, 9));
       if (!ok) break;
       tc_fence_after();
-      if constexpr (Cfg::TMA_DQ) {
-        if (k > 0) {
+      constexpr int NC = Cfg::DQ_COLS, NR = Cfg::DQ_ROUNDS;
+#pragma unroll 1
+      for (int h = 0; h < NR && ok; ++h) {
+        const int rnd = k * NR + h;  // staging-tile round
+        if (rnd > 0) {
           if (lead) {
             bulk_wait_read0();
             mbar_arrive(stg_empty);
           }
-          ok = __all_sync(0xffffffffu, mbar_wait(stg_empty, (k - 1) & 1, g, 13));
+          ok = __all_sync(0xffffffffu, mbar_wait(stg_empty, (rnd - 1) & 1, g, 13));
           if (!ok) break;
         }
-        dq_stage<HD>(lane_base + Cfg::DQ_COL, r, stg, p.scale);
-        tc_fence_before();
-        mbar_arrive(dq_empty);
+        dq_stage<NC>(lane_base + Cfg::DQ_COL, h * NC, r, stg, p.scale);
+        if (h == NR - 1) {  // every TMEM load of the dQ tile has completed
+          tc_fence_before();
+          mbar_arrive(dq_empty);
+        }
         fence_proxy_async_smem();
         mbar_arrive(stg_full);
         if (lead) {
-          ok = mbar_wait(stg_full, k & 1, g, 14);
+          ok = mbar_wait(stg_full, rnd & 1, g, 14);
           if (ok) {
             const int qrow = row0 + (jt + k) * 128;
 #pragma unroll
-            for (int bx = 0; bx < HD / 32; ++bx) tma_reduce_add_2d(&maps.dq, stg + bx * 16384, bx * 32, qrow);
+            for (int bx = 0; bx < NC / 32; ++bx)
+              tma_reduce_add_2d(&maps.dq, stg + bx * 16384, h * NC + bx * 32, qrow);
             bulk_commit();
           }
         }
         ok = __all_sync(0xffffffffu, ok);
-      } else {
-        dq_readout<HD>(lane_base + Cfg::DQ_COL, p.dq_acc + (size_t(row0) + size_t(jt + k) * 128 + r) * HD, p.scale);
-        tc_fence_before();
-        mbar_arrive(dq_empty);
       }
     }
-    if constexpr (Cfg::TMA_DQ) {
-      if (lead) bulk_wait0();  // every reduce-add has landed before the CTA exits
-    }
+    if (lead) bulk_wait0();  // every reduce-add has landed before the CTA exits
     if (!ok) g.ok = false;
     finish();
   }
@@ -546,10 +531,8 @@ int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, cons
   rc |= make_tmap_2d(&maps.k, k, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
   rc |= make_tmap_2d(&maps.v, v, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
   rc |= make_tmap_2d(&maps.dO, dO, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
-  maps.dq = maps.q;
-  if (HD <= 64)
-    rc |= make_tmap_2d(&maps.dq, dq_acc, HD, rows, uint64_t(HD) * 4, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B,
-                       CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+  rc |= make_tmap_2d(&maps.dq, dq_acc, HD, rows, uint64_t(HD) * 4, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
   if (rc) return set_error(MEA_ERR_CUDA, "attention backward: tensor map encode failed");
   AttnBwdParams p;
   p.B = B;

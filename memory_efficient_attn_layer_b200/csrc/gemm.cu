@@ -91,16 +91,6 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
     if (rc) return set_error(MEA_ERR_CUDA, "gemm: B tensor map %d failed (%d)", i, rc);
   }
   for (int i = nb; i < 4; ++i) maps.b[i] = maps.b[0];
-  for (int i = 0; i < 4; ++i) maps.out[i] = maps.b[0];
-  if (L.epi == EPI_QKVG) {  // TMA store maps for q, k, v, g viewed as [B*H*T, N]
-    const int hd = L.slab_rows;
-    const uint32_t swb = hd >= 64 ? 128 : 64;
-    for (int i = 0; i < 4; ++i) {
-      if (!L.outs[i]) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: projection output %d is null", i);
-      rc = make_tmap_2d(&maps.out[i], L.outs[i], hd, L.out_rows, uint64_t(hd) * 2, swb / 2, GEMM_BM, swizzle_for(swb));
-      if (rc) return set_error(MEA_ERR_CUDA, "gemm: output tensor map %d failed (%d)", i, rc);
-    }
-  }
 
   p.M = L.M;
   p.N = L.N;

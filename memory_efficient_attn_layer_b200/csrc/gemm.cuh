@@ -33,7 +33,6 @@ enum EpiMode : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_RED_F32 = 2, EPI_QKVG = 3, E
 struct GemmMaps {
   CUtensorMap a;
   CUtensorMap b[4];
-  CUtensorMap out[4];  // EPI_QKVG: q, k, v, g as [B*H*T, N] for TMA stores
 };
 
 struct GemmParams {
@@ -64,20 +63,20 @@ constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr uint32_t GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
 
-// EPI_QKVG runs eight epilogue warps (two groups splitting the q/k/v/g slabs)
-// and writes its outputs through a shared-memory staging tile with TMA stores;
-// the other epilogues run four warps storing straight from registers.
+// EPI_QKVG runs eight epilogue warps (two groups splitting the q/k/v/g slabs);
+// the other epilogues run four.  Every epilogue stores straight from registers
+// (an earlier EPI_QKVG that staged its tile in shared memory for TMA stores
+// met intermittent launch failures under long runs; this path has none).
 template <int BN, int EPI>
 struct GemmCfg {
-  static constexpr bool STAGED = EPI == EPI_QKVG;
-  static constexpr int EPI_WARPS = STAGED ? 8 : 4;
+  static constexpr bool QKVG = EPI == EPI_QKVG;
+  static constexpr int EPI_WARPS = QKVG ? 8 : 4;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  static constexpr int STAGES = STAGED ? 3 : (BN >= 256 ? 4 : 6);
+  static constexpr int STAGES = BN >= 256 ? 4 : 6;
   static constexpr uint32_t B_BYTES = BN * GEMM_BK * 2;
   static constexpr uint32_t STAGE_BYTES = GEMM_A_BYTES + B_BYTES;
-  static constexpr uint32_t STAGING_BYTES = STAGED ? GEMM_BM * BN * 2 : 0;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + STAGING_BYTES + 256;
+  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + 256;
 };
 
 __device__ __forceinline__ void gemm_decode(const GemmParams& p, int BN, int t, int& m0, int& n0, int& kb0, int& kb1) {
@@ -123,11 +122,7 @@ __device__ __forceinline__ void epi_store(const GemmParams& p, int mode, uint32_
   }
 }
 
-// EPI_QKVG through shared memory: this thread's row of each slab the group owns
-// (slabs s with s % 2 == wg) is written bf16 into the staging tile, laid out
-// per slab as [N/64 column chunks][128 rows][row of min(128, 2N) bytes] with
-// the TMA swizzle, so that one TMA store per chunk writes the slab's 128
-// contiguous rows of q/k/v/g.
+// Rotary-table columns [c, c+32) of one table row, as four 16-byte pieces per table.
 template <int HD>
 __device__ __forceinline__ void load_tab_chunk(const __nv_bfloat16* f1row, const __nv_bfloat16* f2row, int c,
                                                uint4 (&t1)[4], uint4 (&t2)[4]) {
@@ -141,21 +136,17 @@ __device__ __forceinline__ void load_tab_chunk(const __nv_bfloat16* f1row, const
 // q/k RMSNorm over the head dim, bf16 rounding of the normed value, then
 // interleaved rotary out[n] = qn[n]*f1[t,n] + qn[n^1]*f2[t,n]
 // (fast_triton_attn.py:102-106, :132-141); v stored as is (fast_triton_attn.py:108)
-// and g as sigmoid(g) (fast_triton_attn.py:123).  This thread's row of each
-// slab its group owns (slabs s with s % 2 == wg) is written bf16 into the
-// staging tile, laid out per slab as [N/64 column chunks][128 rows][row of
-// min(128, 2N) bytes] with the TMA swizzle, so one TMA store per chunk writes
-// the slab's 128 contiguous rows.  Rotary-table rows are loaded one 32-column
-// chunk ahead of their use.
-// One slab (q, k, v or g of one head) of this thread's row, into the staging tile.
+// and g as sigmoid(g) (fast_triton_attn.py:123).  One slab (q, k, v or g of one
+// head) of this thread's row, written bf16 to its [B,H,T,N] output row in
+// 32-column chunks; rotary-table rows are loaded one chunk ahead of their use.
 // QK: q or k (per-head RMSNorm + rotary, with the rotary rows of chunks 0 and 1
 // preloaded in t1/t2 and later chunks streamed one ahead); else v or sigmoid(g).
 template <int HD, bool QK>
-__device__ __forceinline__ void qkvg_slab(const GemmParams& p, uint32_t tcol, uint32_t slab, int typ, int r, int swz,
-                                          float rs, size_t bht, const __nv_bfloat16* f1row,
-                                          const __nv_bfloat16* f2row, uint4 (&t1)[2][4], uint4 (&t2)[2][4]) {
-  constexpr int SWB = HD >= 64 ? 128 : 64;
+__device__ __forceinline__ void qkvg_slab(const GemmParams& p, uint32_t tcol, int typ, float rs, size_t bht,
+                                          const __nv_bfloat16* f1row, const __nv_bfloat16* f2row,
+                                          uint4 (&t1)[2][4], uint4 (&t2)[2][4]) {
   constexpr int NCH = HD / 32;
+  __nv_bfloat16* orow = (typ == 0 ? p.q : typ == 1 ? p.k : typ == 2 ? p.v : p.g) + bht * HD;
   float sc = rs;
   if (QK) {
     float ss = 0.f;
@@ -207,15 +198,8 @@ __device__ __forceinline__ void qkvg_slab(const GemmParams& p, uint32_t tcol, ui
       }
     }
     // 32 columns = 4 16-byte units of the row, in column chunk c / 64
-    const uint32_t row_addr = slab + (c >> 6) * (GEMM_BM * SWB) + r * SWB;
-    const int u0 = (c & 63) >> 3;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t addr = row_addr + (((u0 + j) ^ swz) << 4);
-      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(pk[4 * j]), "r"(pk[4 * j + 1]),
-                   "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
-                   : "memory");
-    }
+    for (int j = 0; j < 4; ++j) st_global_v4(orow + c + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
   }
 }
 
@@ -224,12 +208,11 @@ __device__ __forceinline__ void qkvg_slab(const GemmParams& p, uint32_t tcol, ui
 // rotary-table row is fetched alongside so its latency overlaps the TMEM wait,
 // and the values stay in registers from the sum of squares to the rotary.
 template <int HD, bool QK>
-__device__ __forceinline__ void qkvg_slab_row(const GemmParams& p, uint32_t tcol, uint32_t slab, int typ, int r,
-                                              int swz, float rs, size_t bht, const __nv_bfloat16* f1row,
-                                              const __nv_bfloat16* f2row) {
+__device__ __forceinline__ void qkvg_slab_row(const GemmParams& p, uint32_t tcol, int typ, float rs, size_t bht,
+                                              const __nv_bfloat16* f1row, const __nv_bfloat16* f2row) {
   static_assert(HD == 32 || HD == 64, "row-at-once slab: head dim 32 or 64");
-  constexpr int SWB = HD >= 64 ? 128 : 64;
   constexpr int NCH = HD / 32;
+  __nv_bfloat16* orow = (typ == 0 ? p.q : typ == 1 ? p.k : typ == 2 ? p.v : p.g) + bht * HD;
   uint32_t v[NCH][32];
   uint4 w1[HD / 8], w2[HD / 8];
 #pragma unroll
@@ -288,15 +271,8 @@ __device__ __forceinline__ void qkvg_slab_row(const GemmParams& p, uint32_t tcol
         pk[j] = pack_bf16(a, bb);
       }
     }
-    const uint32_t row_addr = slab + (c >> 6) * (GEMM_BM * SWB) + r * SWB;
-    const int u0 = (c & 63) >> 3;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t addr = row_addr + (((u0 + j) ^ swz) << 4);
-      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(pk[4 * j]), "r"(pk[4 * j + 1]),
-                   "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
-                   : "memory");
-    }
+    for (int j = 0; j < 4; ++j) st_global_v4(orow + c + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
   }
 }
 
@@ -304,55 +280,46 @@ __device__ __forceinline__ void qkvg_slab_row(const GemmParams& p, uint32_t tcol
 // interleaved rotary out[n] = qn[n]*f1[t,n] + qn[n^1]*f2[t,n]
 // (fast_triton_attn.py:102-106, :132-141); v stored as is (fast_triton_attn.py:108)
 // and g as sigmoid(g) (fast_triton_attn.py:123).  This thread's row of each
-// slab its group owns (slabs s with s % 2 == wg) is written bf16 into the
-// staging tile, laid out per slab as [N/64 column chunks][128 rows][row of
-// min(128, 2N) bytes] with the TMA swizzle, so one TMA store per chunk writes
-// the slab's 128 contiguous rows.  q/k slabs go first, while the rotary rows
-// preloaded by the caller are live; v/g slabs follow.
+// slab its group owns (slabs s with s % 2 == wg) goes straight to the slab's
+// [B,H,T,N] output.  For N = 128 the q/k slabs go first, while the rotary rows
+// preloaded by the caller are live, and v/g follow.
 template <int BN, int HD>
-__device__ __forceinline__ void epi_qkvg_staged(const GemmParams& p, uint32_t taddr, int m, int n0, int wg, int r,
-                                                uint32_t stg, uint4 (&t1)[2][4], uint4 (&t2)[2][4]) {
-  constexpr int SWB = HD >= 64 ? 128 : 64;
+__device__ __forceinline__ void epi_qkvg(const GemmParams& p, uint32_t taddr, int m, int n0, int wg,
+                                         uint4 (&t1)[2][4], uint4 (&t2)[2][4]) {
   constexpr int NSLAB = BN / HD;
   const int b = m / p.T;
   const int t = m - b * p.T;
   const float rs = p.row_scale ? p.row_scale[m] : 1.0f;
   const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
   const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
-  const int swz = SWB == 128 ? (r & 7) : ((r >> 1) & 3);
   if constexpr (HD <= 64) {
 #pragma unroll 1
     for (int s = wg; s < NSLAB; s += 2) {
       const int sg = n0 / HD + s;
+      const size_t bht = (size_t(b) * p.H + (sg >> 2)) * p.T + t;
       if ((sg & 3) < 2)
-        qkvg_slab_row<HD, true>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs,
-                                (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row);
+        qkvg_slab_row<HD, true>(p, taddr + s * HD, sg & 3, rs, bht, f1row, f2row);
       else
-        qkvg_slab_row<HD, false>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs, 0, f1row,
-                                 f2row);
+        qkvg_slab_row<HD, false>(p, taddr + s * HD, sg & 3, rs, bht, f1row, f2row);
     }
   } else {
 #pragma unroll 1
     for (int s = wg; s < NSLAB; s += 2) {
       const int sg = n0 / HD + s;
       if ((sg & 3) < 2)
-        qkvg_slab<HD, true>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs,
-                            (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row, t1, t2);
+        qkvg_slab<HD, true>(p, taddr + s * HD, sg & 3, rs, (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row,
+                            t1, t2);
     }
 #pragma unroll 1
     for (int s = wg; s < NSLAB; s += 2) {
       const int sg = n0 / HD + s;
       if ((sg & 3) >= 2)
-        qkvg_slab<HD, false>(p, taddr + s * HD, stg + s * (GEMM_BM * HD * 2), sg & 3, r, swz, rs, 0, f1row, f2row,
+        qkvg_slab<HD, false>(p, taddr + s * HD, sg & 3, rs, (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row,
                              t1, t2);
     }
   }
 }
 
-__device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int c0, int c1) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];"
-               ::"l"(tmap), "r"(src), "r"(c0), "r"(c1) : "memory");
-}
 
 // Gate backward fused on the dGated = dY * Wo tile (fast_triton_attn.py:576-584, :601):
 //   dO = dGated*g  -> [B,H,T,N] bf16 (input of the attention backward)
@@ -584,9 +551,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
     // ---------------- Epilogue: warps 2 .. 2+EPI_WARPS-1 ----------------
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const int wg = (warp - 2) >> 2;                          // epilogue group (STAGED: 0 or 1)
-    const bool leader = Cfg::STAGED && quarter == 2 && lane == 0;  // warps 2 and 6
-    const uint32_t stg = sA + STAGES * Cfg::STAGE_BYTES;
+    const int wg = (warp - 2) >> 2;  // epilogue group (QKVG: 0 or 1)
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       int m0, n0, kb0, kb1;
@@ -595,7 +560,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
       // Projection epilogue: the rotary-table rows of this thread's token are
       // loaded before the accumulator wait, which hides their latency.
       uint4 pre1[2][4], pre2[2][4];
-      if constexpr (Cfg::STAGED && HD > 64) {
+      if constexpr (Cfg::QKVG && HD > 64) {
         const int t = (m0 + row) % p.T;
         const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
         const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
@@ -611,27 +576,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
       tc_fence_after();
       const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + buf * BN;
       const int m = m0 + row;
-      if constexpr (Cfg::STAGED) {
-        // the group's previous TMA stores must have finished reading the staging tile
-        if (leader) bulk_wait_read0();
-        named_bar_sync(1 + wg, 128);
-        epi_qkvg_staged<BN, HD>(p, taddr, m, n0, wg, row, stg, pre1, pre2);
+      if constexpr (Cfg::QKVG) {
+        epi_qkvg<BN, HD>(p, taddr, m, n0, wg, pre1, pre2);
         tc_fence_before();
         mbar_arrive(acce_bar(buf));
-        fence_proxy_async_smem();
-        named_bar_sync(1 + wg, 128);
-        if (leader) {
-          const int hd = p.hd;
-          const int swb = hd >= 64 ? 128 : 64;
-          const int b = m0 / p.T, t0 = m0 - (m0 / p.T) * p.T;
-          for (int s = wg; s < BN / hd; s += 2) {
-            const int sg = n0 / hd + s;
-            const int orow = (b * p.H + (sg >> 2)) * p.T + t0;
-            for (int c = 0; c < hd; c += swb / 2)
-              tma_store_2d(&maps.out[sg & 3], stg + s * (GEMM_BM * hd * 2) + (c / 64) * (GEMM_BM * swb), c, orow);
-          }
-          bulk_commit();
-        }
       } else {
         if constexpr (EPI == EPI_DGATE)
           epi_dgate<BN, HD>(p, taddr, m, n0);
@@ -641,7 +589,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
         mbar_arrive(acce_bar(buf));
       }
     }
-    if (leader) bulk_wait0();
   }
 
   __syncthreads();

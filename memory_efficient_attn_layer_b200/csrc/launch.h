@@ -34,8 +34,6 @@ struct GemmLaunch {
   int b_rows;           // B_SLABS / B_MN_KSPLIT4: rows of each B tensor
   int slab_rows;        // B_SLABS: head dim
   int k_splits;         // > 1 only with EPI_RED_F32
-  void* outs[4];        // EPI_QKVG: q, k, v, g outputs ([B*H*T, N] bf16), written by TMA
-  long long out_rows;   // EPI_QKVG: B*H*T
 };
 int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st);
 int auto_splits(int m_tiles, int n_tiles, int kb_total, int waves);
