@@ -63,20 +63,21 @@ constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr uint32_t GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
 
-// EPI_QKVG runs eight epilogue warps (two groups splitting the q/k/v/g slabs);
-// the other epilogues run four.  Every epilogue stores straight from registers
-// (an earlier EPI_QKVG that staged its tile in shared memory for TMA stores
-// met intermittent launch failures under long runs; this path has none).
+// EPI_QKVG runs eight epilogue warps (two groups splitting the q/k/v/g slabs)
+// that stage each slab in shared memory and copy it out with coalesced stores;
+// the other epilogues run four warps storing straight from registers.  Shared
+// memory: stage ring, then the staging tile, then the barriers.
 template <int BN, int EPI>
 struct GemmCfg {
   static constexpr bool QKVG = EPI == EPI_QKVG;
   static constexpr int EPI_WARPS = QKVG ? 8 : 4;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  static constexpr int STAGES = BN >= 256 ? 4 : 6;
+  static constexpr int STAGES = QKVG ? 3 : (BN >= 256 ? 4 : 6);
+  static constexpr uint32_t STAGING_BYTES = QKVG ? GEMM_BM * BN * 2 : 0;
   static constexpr uint32_t B_BYTES = BN * GEMM_BK * 2;
   static constexpr uint32_t STAGE_BYTES = GEMM_A_BYTES + B_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + 256;
+  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + STAGING_BYTES + 256;
 };
 
 __device__ __forceinline__ void gemm_decode(const GemmParams& p, int BN, int t, int& m0, int& n0, int& kb0, int& kb1) {
@@ -122,6 +123,36 @@ __device__ __forceinline__ void epi_store(const GemmParams& p, int mode, uint32_
   }
 }
 
+// Staging tile of one slab: 128 rows of 2*HD bytes; 16-byte unit u of row r sits
+// at u ^ (r & 7) within the row (u ^ (r & 3) for HD = 32), so that the row-per-
+// thread writes and the unit-per-thread copy-out both spread over the banks.
+template <int HD>
+__device__ __forceinline__ uint32_t stage_addr(uint32_t slab, int r, int u) {
+  constexpr int UPR = HD / 8;  // 16-byte units per row
+  constexpr int MASK = UPR >= 8 ? 7 : UPR - 1;
+  return slab + r * (HD * 2) + ((u ^ (r & MASK)) << 4);
+}
+template <int HD>
+__device__ __forceinline__ void stage_unit(uint32_t slab, int r, int u, const uint32_t* w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(stage_addr<HD>(slab, r, u)), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3])
+               : "memory");
+}
+// Copy a staged slab (128 consecutive rows of one [B,H,T,N] output) to global
+// memory: the group's 128 threads move consecutive 16-byte units.
+template <int HD>
+__device__ __forceinline__ void copy_out_slab(uint32_t slab, __nv_bfloat16* dst, int ti) {
+  constexpr int UPR = HD / 8;
+#pragma unroll 4
+  for (int i = ti; i < 128 * UPR; i += 128) {
+    const int r = i / UPR, u = i - (i / UPR) * UPR;
+    uint32_t w0, w1, w2, w3;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                 : "r"(stage_addr<HD>(slab, r, u)) : "memory");
+    st_global_v4(dst + size_t(i) * 8, w0, w1, w2, w3);
+  }
+}
+
 // Rotary-table columns [c, c+32) of one table row, as four 16-byte pieces per table.
 template <int HD>
 __device__ __forceinline__ void load_tab_chunk(const __nv_bfloat16* f1row, const __nv_bfloat16* f2row, int c,
@@ -142,11 +173,10 @@ __device__ __forceinline__ void load_tab_chunk(const __nv_bfloat16* f1row, const
 // QK: q or k (per-head RMSNorm + rotary, with the rotary rows of chunks 0 and 1
 // preloaded in t1/t2 and later chunks streamed one ahead); else v or sigmoid(g).
 template <int HD, bool QK>
-__device__ __forceinline__ void qkvg_slab(const GemmParams& p, uint32_t tcol, int typ, float rs, size_t bht,
-                                          const __nv_bfloat16* f1row, const __nv_bfloat16* f2row,
+__device__ __forceinline__ void qkvg_slab(const GemmParams& p, uint32_t tcol, uint32_t slab, int r, int typ, float rs,
+                                          size_t bht, const __nv_bfloat16* f1row, const __nv_bfloat16* f2row,
                                           uint4 (&t1)[2][4], uint4 (&t2)[2][4]) {
   constexpr int NCH = HD / 32;
-  __nv_bfloat16* orow = (typ == 0 ? p.q : typ == 1 ? p.k : typ == 2 ? p.v : p.g) + bht * HD;
   float sc = rs;
   if (QK) {
     float ss = 0.f;
@@ -199,7 +229,7 @@ __device__ __forceinline__ void qkvg_slab(const GemmParams& p, uint32_t tcol, in
     }
     // 32 columns = 4 16-byte units of the row, in column chunk c / 64
 #pragma unroll
-    for (int j = 0; j < 4; ++j) st_global_v4(orow + c + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+    for (int j = 0; j < 4; ++j) stage_unit<HD>(slab, r, c / 8 + j, pk + 4 * j);
   }
 }
 
@@ -208,11 +238,11 @@ __device__ __forceinline__ void qkvg_slab(const GemmParams& p, uint32_t tcol, in
 // rotary-table row is fetched alongside so its latency overlaps the TMEM wait,
 // and the values stay in registers from the sum of squares to the rotary.
 template <int HD, bool QK>
-__device__ __forceinline__ void qkvg_slab_row(const GemmParams& p, uint32_t tcol, int typ, float rs, size_t bht,
-                                              const __nv_bfloat16* f1row, const __nv_bfloat16* f2row) {
+__device__ __forceinline__ void qkvg_slab_row(const GemmParams& p, uint32_t tcol, uint32_t slab, int r, int typ,
+                                              float rs, size_t bht, const __nv_bfloat16* f1row,
+                                              const __nv_bfloat16* f2row) {
   static_assert(HD == 32 || HD == 64, "row-at-once slab: head dim 32 or 64");
   constexpr int NCH = HD / 32;
-  __nv_bfloat16* orow = (typ == 0 ? p.q : typ == 1 ? p.k : typ == 2 ? p.v : p.g) + bht * HD;
   uint32_t v[NCH][32];
   uint4 w1[HD / 8], w2[HD / 8];
 #pragma unroll
@@ -272,7 +302,7 @@ __device__ __forceinline__ void qkvg_slab_row(const GemmParams& p, uint32_t tcol
       }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) st_global_v4(orow + c + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+    for (int j = 0; j < 4; ++j) stage_unit<HD>(slab, r, c / 8 + j, pk + 4 * j);
   }
 }
 
@@ -284,39 +314,58 @@ __device__ __forceinline__ void qkvg_slab_row(const GemmParams& p, uint32_t tcol
 // [B,H,T,N] output.  For N = 128 the q/k slabs go first, while the rotary rows
 // preloaded by the caller are live, and v/g follow.
 template <int BN, int HD>
-__device__ __forceinline__ void epi_qkvg(const GemmParams& p, uint32_t taddr, int m, int n0, int wg,
-                                         uint4 (&t1)[2][4], uint4 (&t2)[2][4]) {
+__device__ __forceinline__ void epi_qkvg(const GemmParams& p, uint32_t taddr, int m, int n0, int wg, int r, int ti,
+                                         uint32_t stg, uint4 (&t1)[2][4], uint4 (&t2)[2][4]) {
   constexpr int NSLAB = BN / HD;
+  constexpr uint32_t SLAB_BYTES = GEMM_BM * HD * 2;
   const int b = m / p.T;
   const int t = m - b * p.T;
   const float rs = p.row_scale ? p.row_scale[m] : 1.0f;
   const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
   const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
+  // the group's previous copy-out has read the staging tile
+  named_bar_sync(1 + wg, 128);
   if constexpr (HD <= 64) {
 #pragma unroll 1
     for (int s = wg; s < NSLAB; s += 2) {
       const int sg = n0 / HD + s;
       const size_t bht = (size_t(b) * p.H + (sg >> 2)) * p.T + t;
       if ((sg & 3) < 2)
-        qkvg_slab_row<HD, true>(p, taddr + s * HD, sg & 3, rs, bht, f1row, f2row);
+        qkvg_slab_row<HD, true>(p, taddr + s * HD, stg + s * SLAB_BYTES, r, sg & 3, rs, bht, f1row, f2row);
       else
-        qkvg_slab_row<HD, false>(p, taddr + s * HD, sg & 3, rs, bht, f1row, f2row);
+        qkvg_slab_row<HD, false>(p, taddr + s * HD, stg + s * SLAB_BYTES, r, sg & 3, rs, bht, f1row, f2row);
     }
   } else {
 #pragma unroll 1
     for (int s = wg; s < NSLAB; s += 2) {
       const int sg = n0 / HD + s;
       if ((sg & 3) < 2)
-        qkvg_slab<HD, true>(p, taddr + s * HD, sg & 3, rs, (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row,
-                            t1, t2);
+        qkvg_slab<HD, true>(p, taddr + s * HD, stg + s * SLAB_BYTES, r, sg & 3, rs,
+                            (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row, t1, t2);
     }
 #pragma unroll 1
     for (int s = wg; s < NSLAB; s += 2) {
       const int sg = n0 / HD + s;
       if ((sg & 3) >= 2)
-        qkvg_slab<HD, false>(p, taddr + s * HD, sg & 3, rs, (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row,
-                             t1, t2);
+        qkvg_slab<HD, false>(p, taddr + s * HD, stg + s * SLAB_BYTES, r, sg & 3, rs,
+                             (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row, t1, t2);
     }
+  }
+}
+
+// Copy-out of the slabs staged by epi_qkvg (after the group's barrier).
+template <int BN, int HD>
+__device__ __forceinline__ void epi_qkvg_copy_out(const GemmParams& p, int m0, int n0, int wg, int ti, uint32_t stg) {
+  constexpr int NSLAB = BN / HD;
+  const int b = m0 / p.T, t0 = m0 - (m0 / p.T) * p.T;
+  named_bar_sync(1 + wg, 128);
+#pragma unroll 1
+  for (int s = wg; s < NSLAB; s += 2) {
+    const int sg = n0 / HD + s;
+    const int typ = sg & 3;
+    __nv_bfloat16* out = (typ == 0 ? p.q : typ == 1 ? p.k : typ == 2 ? p.v : p.g) +
+                         ((size_t(b) * p.H + (sg >> 2)) * p.T + t0) * HD;
+    copy_out_slab<HD>(stg + s * (GEMM_BM * HD * 2), out, ti);
   }
 }
 
@@ -406,7 +455,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sA = smem_u32(smem);
   const uint32_t sB = sA + STAGES * GEMM_A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  // barriers after the stage ring and the staging tile
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::STAGING_BYTES);
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
@@ -552,6 +602,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int wg = (warp - 2) >> 2;  // epilogue group (QKVG: 0 or 1)
+    const int ti = (warp - 2 - 4 * wg) * 32 + lane;  // thread index within the group
+    const uint32_t stg = sA + STAGES * Cfg::STAGE_BYTES;
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       int m0, n0, kb0, kb1;
@@ -577,9 +629,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
       const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + buf * BN;
       const int m = m0 + row;
       if constexpr (Cfg::QKVG) {
-        epi_qkvg<BN, HD>(p, taddr, m, n0, wg, pre1, pre2);
+        epi_qkvg<BN, HD>(p, taddr, m, n0, wg, row, ti, stg, pre1, pre2);
         tc_fence_before();
         mbar_arrive(acce_bar(buf));
+        epi_qkvg_copy_out<BN, HD>(p, m0, n0, wg, ti, stg);
       } else {
         if constexpr (EPI == EPI_DGATE)
           epi_dgate<BN, HD>(p, taddr, m, n0);
