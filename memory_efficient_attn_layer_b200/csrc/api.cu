@@ -94,13 +94,12 @@ struct Carve {
 };
 
 struct FwdWs {
-  size_t xn, rx, q, k, v, gs, gated, bound, total;
+  size_t rx, q, k, v, gs, gated, bound, total;
 };
 static FwdWs fwd_layout(const mea_block_dims& d) {
   const size_t M = size_t(d.B) * d.T, HN = size_t(d.H) * d.N;
   FwdWs w;
   Carve c;
-  w.xn = c.take(M * d.C * 2);
   w.rx = c.take(M * 4);
   w.q = c.take(M * HN * 2);
   w.k = c.take(M * HN * 2);
@@ -143,9 +142,12 @@ static BwdWs bwd_layout(const mea_block_dims& d) {
 // ---------------------------------------------------------------------------
 // Building blocks
 // ---------------------------------------------------------------------------
-static int qkvg(const mea_block_dims& d, const void* xn, const void* wq, const void* wk, const void* wv,
-                const void* wg, const void* f1, const void* f2, void* q, void* k, void* v, void* gs, float* rq,
-                float* rk, int* status, cudaStream_t st) {
+// Fused q/k/v/g projection.  `a` is x_n, or x itself with `row_scale` = the
+// input RMSNorm's inverse RMS per row (the norm applied to the accumulator rows
+// in the epilogue: x_n W^T = diag(r) x W^T).
+static int qkvg(const mea_block_dims& d, const void* a, const float* row_scale, const void* wq, const void* wk,
+                const void* wv, const void* wg, const void* f1, const void* f2, void* q, void* k, void* v, void* gs,
+                float* rq, float* rk, int* status, cudaStream_t st) {
   const int HN = d.H * d.N;
   GemmLaunch L{};
   L.M = d.B * d.T;
@@ -155,7 +157,7 @@ static int qkvg(const mea_block_dims& d, const void* xn, const void* wq, const v
   L.amode = A_K;
   L.bmode = B_SLABS;
   L.epi = EPI_QKVG;
-  L.a = xn;
+  L.a = a;
   L.lda = d.C;
   L.b[0] = wq;
   L.b[1] = wk;
@@ -176,7 +178,7 @@ static int qkvg(const mea_block_dims& d, const void* xn, const void* wq, const v
   p.ldf = d.N;
   p.rq = rq;
   p.rk = rk;
-  p.row_scale = nullptr;
+  p.row_scale = row_scale;
   p.T = d.T;
   p.H = d.H;
   p.hd = d.N;
@@ -354,8 +356,11 @@ int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, co
   auto st = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
   const int M = d->B * d->T, HN = d->H * d->N;
-  MEA_STAGE(ST_FWD_NORM, run_rmsnorm_fwd(M, d->C, d->eps, x, ws + w.xn, reinterpret_cast<float*>(ws + w.rx), st));
-  MEA_STAGE(ST_FWD_QKVG, qkvg(*d, ws + w.xn, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, nullptr,
+  // Input RMSNorm fused into the projection: only the inverse RMS per row is
+  // computed here; the GEMM runs on x and scales its accumulator rows.
+  float* rx = reinterpret_cast<float*>(ws + w.rx);
+  MEA_STAGE(ST_FWD_NORM, run_rmsnorm_fwd(M, d->C, d->eps, x, nullptr, rx, st));
+  MEA_STAGE(ST_FWD_QKVG, qkvg(*d, x, rx, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, nullptr,
                nullptr, status, st));
   {
     // Scores are bounded through the per-head norm and the rotary tables, so
@@ -412,7 +417,10 @@ int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, c
 
   // Recompute: input norm, projections (+ inverse RMS of q/k), attention (+ O).
   MEA_STAGE(ST_BWD_NORM, run_rmsnorm_fwd(M, C, d->eps, x, ws + w.xn, rx, st));
-  MEA_STAGE(ST_BWD_QKVG, qkvg(*d, ws + w.xn, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, rq, rk,
+  // Same projection as the forward (x with the row scale), so the recomputed
+  // q/k/v/g match the forward's bit for bit and the saved LSE stays exact;
+  // x_n (written above) serves the weight and input gradients.
+  MEA_STAGE(ST_BWD_QKVG, qkvg(*d, x, rx, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, rq, rk,
                status, st));
   // The recompute takes the forward's LSE as its exp2 reference: P comes out
   // normalised, the same P the attention backward rebuilds.
@@ -481,7 +489,8 @@ int mea_qkvg_forward(const mea_block_dims* d, const void* xn, const void* wq, co
                      const void* wg, const void* factor1, const void* factor2, void* q, void* k, void* v, void* gs,
                      float* rq, float* rk, int* status, void* stream) {
   MEA_TRY(validate(d));
-  return qkvg(*d, xn, wq, wk, wv, wg, factor1, factor2, q, k, v, gs, rq, rk, status, static_cast<cudaStream_t>(stream));
+  return qkvg(*d, xn, nullptr, wq, wk, wv, wg, factor1, factor2, q, k, v, gs, rq, rk, status,
+              static_cast<cudaStream_t>(stream));
 }
 
 int mea_attention_forward(int B, int H, int T, int N, const void* q, const void* k, const void* v, const void* gs,
