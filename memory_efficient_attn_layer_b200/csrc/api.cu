@@ -169,13 +169,14 @@ static int qkvg(const mea_block_dims& d, const void* a, const float* row_scale, 
   L.k_splits = 1;
   GemmParams p{};
   p.status = status;
-  p.q = static_cast<__nv_bfloat16*>(q);
-  p.k = static_cast<__nv_bfloat16*>(k);
-  p.v = static_cast<__nv_bfloat16*>(v);
-  p.g = static_cast<__nv_bfloat16*>(gs);
-  p.f1 = static_cast<const __nv_bfloat16*>(f1);
-  p.f2 = static_cast<const __nv_bfloat16*>(f2);
-  p.ldf = d.N;
+  L.out[0] = q;
+  L.out[1] = k;
+  L.out[2] = v;
+  L.out[3] = gs;
+  L.in[0] = f1;
+  L.in[1] = f2;
+  L.ldin = d.N;
+  L.in_rows = d.T_max;
   p.rq = rq;
   p.rk = rk;
   p.row_scale = row_scale;
@@ -204,11 +205,11 @@ static int gate_bwd(const mea_block_dims& d, const void* dy, const void* wo, con
   L.k_splits = 1;
   GemmParams p{};
   p.status = status;
-  p.o_in = static_cast<const __nv_bfloat16*>(o);
-  p.gs_in = static_cast<const __nv_bfloat16*>(gs);
-  p.do_out = static_cast<__nv_bfloat16*>(dO);
-  p.dg_out = static_cast<__nv_bfloat16*>(dg);
-  p.ld_dg = ld_dg;
+  L.in[0] = o;
+  L.in[1] = gs;
+  L.out[0] = dO;
+  L.out[1] = dg;
+  L.ldo = ld_dg;
   p.delta = delta;
   p.T = d.T;
   p.H = d.H;
@@ -234,8 +235,8 @@ static int weight_grad(int Mp, int Np, int tokens, const void* a, long long lda,
   L.k_splits = auto_splits(Mp / GEMM_BM, Np / L.bn, tokens / GEMM_BK, 8);
   GemmParams p{};
   p.status = status;
-  p.out = out;
-  p.ldo = Np;
+  L.out[0] = out;
+  L.ldo = Np;
   return run_gemm(L, p, st);
 }
 
@@ -384,10 +385,10 @@ int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, co
   L.b[0] = wo;
   L.ldb = HN;
   L.k_splits = 1;
+  L.out[0] = y;
+  L.ldo = d->C;
   GemmParams p{};
   p.status = status;
-  p.out = y;
-  p.ldo = d->C;
   StageScope scope_(ST_FWD_OPROJ, st);
   return run_gemm(L, p, st);
 }
@@ -464,10 +465,10 @@ int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, c
     L.ldb = C;
     L.b_rows = HN;
     L.k_splits = 1;
+    L.out[0] = ws + w.dxn;
+    L.ldo = C;
     GemmParams p{};
     p.status = status;
-    p.out = ws + w.dxn;
-    p.ldo = C;
     MEA_STAGE(ST_BWD_DX, run_gemm(L, p, st));
   }
   MEA_STAGE(ST_BWD_NORM_BWD, run_rmsnorm_bwd(M, C, ws + w.dxn, x, rx, dx, st));
@@ -518,10 +519,10 @@ int mea_gemm(int M, int N, int K, const void* a, long long lda, int a_mn, const 
   if (accumulate && L.amode != A_MN) L.k_splits = 1;  // the reducing epilogue is built for A_MN x B_MN only
   if (accumulate && (L.amode != A_MN || L.bmode != B_MN))
     return set_error(MEA_ERR_INVALID_ARGUMENT, "mea_gemm: accumulate needs a_mn = b_mn = 1");
+  L.out[0] = out;
+  L.ldo = ldo;
   GemmParams p{};
   p.status = status;
-  p.out = out;
-  p.ldo = ldo;
   return run_gemm(L, p, static_cast<cudaStream_t>(stream));
 }
 

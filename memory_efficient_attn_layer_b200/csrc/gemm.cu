@@ -1,4 +1,4 @@
-// Host-side set-up and dispatch of the tcgen05 GEMM (gemm.cuh).
+// Host-side set-up and dispatch of the CTA-pair tcgen05 GEMM (gemm.cuh).
 #include <cstdio>
 
 #include "gemm.cuh"
@@ -7,18 +7,48 @@
 
 namespace mea {
 
+// Persistent grid: one 2-CTA cluster per SM pair that can hold one, at most one
+// per work unit.
 template <int BN, int AM, int BMD, int EPI, int HD>
 static int launch_gemm_t(const GemmMaps& maps, const GemmParams& p, cudaStream_t st) {
-  using Cfg = GemmCfg<BN, EPI>;
+  using Cfg = GemmCfg<BN, EPI, HD>;
   auto kern = gemm_kernel<BN, AM, BMD, EPI, HD>;
   if (!smem_attr_set(reinterpret_cast<const void*>(kern), int(Cfg::SMEM)))
     return set_error(MEA_ERR_CUDA, "cudaFuncSetAttribute(gemm) failed");
-  const int ntiles = p.m_tiles * p.n_tiles * p.k_splits;
-  const int grid = ntiles < num_sms() ? ntiles : num_sms();
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(maps, p);
-  char what[96];
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static int max_pairs[64] = {0};  // per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& mp = max_pairs[dev & 63];
+  if (mp <= 0) {
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    mp = n;
+  }
+  const int units = p.m_pairs * p.n_tiles * p.k_splits;
+  cfg.gridDim = dim3(2 * (units < mp ? units : mp));
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
+  char what[112];
   snprintf(what, sizeof(what), "gemm_kernel<%d,%d,%d,%d,%d> M=%d N=%d K=%d splits=%d", BN, AM, BMD, EPI, HD, p.M, p.N,
            p.K, p.k_splits);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(MEA_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  }
   return check_launch(what);
 }
 
@@ -36,7 +66,6 @@ static int launch_gemm_t(const GemmMaps& maps, const GemmParams& p, cudaStream_t
 static int dispatch(int bn, int am, int bmd, int epi, const GemmMaps& maps, const GemmParams& p, cudaStream_t st) {
   // forward: fused projections, o_proj
   MEA_GEMM_CASE_HD(256, A_K, B_SLABS, EPI_QKVG)
-  MEA_GEMM_CASE_HD(128, A_K, B_SLABS, EPI_QKVG)
   MEA_GEMM_CASE(256, A_K, B_K, EPI_BF16)
   MEA_GEMM_CASE(128, A_K, B_K, EPI_BF16)
   // backward: dGated (+ gate bwd), dx_normed, weight gradients
@@ -55,10 +84,18 @@ static int dispatch(int bn, int am, int bmd, int epi, const GemmMaps& maps, cons
   MEA_GEMM_CASE(128, A_K, B_MN, EPI_F32)
   MEA_GEMM_CASE(256, A_MN, B_K, EPI_F32)
   MEA_GEMM_CASE(128, A_MN, B_K, EPI_F32)
-  return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: no kernel for bn=%d amode=%d bmode=%d epi=%d", bn, am, bmd, epi);
+  return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: no kernel for bn=%d amode=%d bmode=%d epi=%d hd=%d", bn, am, bmd,
+                   epi, p.hd);
 }
 #undef MEA_GEMM_CASE
 #undef MEA_GEMM_CASE_HD
+
+// Map over a [rows, hd] bf16 tensor with boxes of 32 rows x min(hd, 64) columns,
+// swizzled to match the epilogue's staging layout.
+static int hd_map(CUtensorMap* m, const void* base, uint64_t rows, int hd, uint64_t pitch_elems, uint64_t cols) {
+  const uint32_t box_w = hd < 64 ? uint32_t(hd) : 64u;
+  return make_tmap_2d(m, base, cols, rows, pitch_elems * 2, box_w, 32, swizzle_for(box_w * 2));
+}
 
 int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
   const int bn = L.bn;
@@ -69,19 +106,19 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
   memset(&maps, 0, sizeof(maps));
   const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
   int rc;
-  // A operand: K-major [M rows, K] or MN-major [K rows, M]
+  // A operand (this CTA's 128 rows): K-major [M rows, K] or MN-major [K rows, M]
   if (L.amode == A_K)
     rc = make_tmap_2d(&maps.a, L.a, L.K, L.M, uint64_t(L.lda) * 2, 64, 128, sw);
   else
     rc = make_tmap_2d(&maps.a, L.a, L.M, L.K, uint64_t(L.lda) * 2, 64, 64, sw);
   if (rc) return set_error(MEA_ERR_CUDA, "gemm: A tensor map failed (%d)", rc);
-  // B operand
+  // B operand (this CTA's bn/2 columns)
   const int nb = (L.bmode == B_K || L.bmode == B_MN) ? 1 : 4;
   for (int i = 0; i < nb; ++i) {
     const void* src = L.b[i];
     if (!src) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: B tensor %d is null", i);
     if (L.bmode == B_K)
-      rc = make_tmap_2d(&maps.b[i], src, L.K, L.N, uint64_t(L.ldb) * 2, 64, bn, sw);
+      rc = make_tmap_2d(&maps.b[i], src, L.K, L.N, uint64_t(L.ldb) * 2, 64, bn / 2, sw);
     else if (L.bmode == B_MN)
       rc = make_tmap_2d(&maps.b[i], src, L.N, L.K, uint64_t(L.ldb) * 2, 64, 64, sw);
     else if (L.bmode == B_SLABS)
@@ -92,10 +129,44 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
   }
   for (int i = nb; i < 4; ++i) maps.b[i] = maps.b[0];
 
+  // Epilogue maps
+  if (L.epi == EPI_BF16 || L.epi == EPI_F32 || L.epi == EPI_RED_F32) {
+    if (!L.out[0]) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: output is null");
+    if (L.epi == EPI_BF16)
+      rc = make_tmap_2d(&maps.out[0], L.out[0], L.N, L.M, uint64_t(L.ldo) * 2, 64, 32, sw);
+    else
+      rc = make_tmap_2d(&maps.out[0], L.out[0], L.N, L.M, uint64_t(L.ldo) * 4, 32, 32, sw,
+                        CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+    if (rc) return set_error(MEA_ERR_CUDA, "gemm: output tensor map failed (%d)", rc);
+  } else {
+    const int hd = p.hd;
+    if (hd != 32 && hd != 64 && hd != 128) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: head dim %d", hd);
+    const uint64_t bht = uint64_t(L.M) * p.H;  // B*H*T rows of a [B,H,T,N] tensor
+    const int nout = L.epi == EPI_QKVG ? 4 : 1;
+    for (int i = 0; i < nout; ++i) {
+      if (!L.out[i]) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: epilogue output %d is null", i);
+      if ((rc = hd_map(&maps.out[i], L.out[i], bht, hd, hd, hd)))
+        return set_error(MEA_ERR_CUDA, "gemm: epilogue output map %d failed (%d)", i, rc);
+    }
+    if (L.epi == EPI_DGATE) {
+      if (!L.out[1]) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: dg output is null");
+      if ((rc = hd_map(&maps.out[1], L.out[1], uint64_t(L.M), hd, uint64_t(L.ldo), uint64_t(p.H) * hd)))
+        return set_error(MEA_ERR_CUDA, "gemm: dg output map failed (%d)", rc);
+    }
+    for (int i = 0; i < 2; ++i) {
+      if (!L.in[i]) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: epilogue input %d is null", i);
+      if (L.epi == EPI_QKVG)
+        rc = hd_map(&maps.in[i], L.in[i], uint64_t(L.in_rows), hd, uint64_t(L.ldin), hd);
+      else
+        rc = hd_map(&maps.in[i], L.in[i], bht, hd, hd, hd);
+      if (rc) return set_error(MEA_ERR_CUDA, "gemm: epilogue input map %d failed (%d)", i, rc);
+    }
+  }
+
   p.M = L.M;
   p.N = L.N;
   p.K = L.K;
-  p.m_tiles = L.M / GEMM_BM;
+  p.m_pairs = (L.M / GEMM_BM + 1) / 2;
   p.n_tiles = L.N / bn;
   p.kb_total = L.K / GEMM_BK;
   int splits = L.k_splits < 1 ? 1 : L.k_splits;
@@ -106,18 +177,20 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
   p.b_kb_per_src = L.b_rows / GEMM_BK;
   if (p.k_splits > 1 && L.epi != EPI_RED_F32)
     return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: split-K needs the reducing epilogue");
-  if (L.bmode == B_SLABS && (L.slab_rows % 8 || bn % L.slab_rows))
-    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: slab rows %d must divide %d", L.slab_rows, bn);
+  if (L.bmode == B_SLABS && (L.slab_rows % 8 || bn % (2 * L.slab_rows)))
+    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: slab rows %d must divide %d", L.slab_rows, bn / 2);
   if (L.bmode == B_MN_KSPLIT4 && (L.b_rows % GEMM_BK || 4 * L.b_rows != L.K))
     return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: K must be 4 x rows of each B tensor");
+  if ((L.epi == EPI_QKVG || L.epi == EPI_DGATE) && (p.T % GEMM_BM || L.M % p.T))
+    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: per-head epilogue needs T %% 128 == 0 and M %% T == 0");
   return dispatch(bn, L.amode, L.bmode, L.epi, maps, p, st);
 }
 
 // Split count for a long-K GEMM with few output tiles: about `waves` work
-// units per SM, at least 8 k-blocks per unit.
+// units per SM pair, at least 8 k-blocks per unit.
 int auto_splits(int m_tiles, int n_tiles, int kb_total, int waves) {
-  const int tiles = m_tiles * n_tiles;
-  int s = (num_sms() * waves + tiles - 1) / tiles;
+  const int units = ((m_tiles + 1) / 2) * n_tiles;
+  int s = ((num_sms() / 2) * waves + units - 1) / units;
   if (s > kb_total / 8) s = kb_total / 8;
   return s < 1 ? 1 : s;
 }

@@ -1,24 +1,36 @@
-// Persistent warp-specialised tcgen05 GEMM for sm_100a.
+// Persistent warp-specialised tcgen05 GEMM for sm_100a on CTA pairs.
 //
 //   D[M, N] = sum_k A[m, k] * B[n, k]      (bf16 operands, fp32 accumulate in TMEM)
 //
-// One CTA per SM walks a static list of 128 x BN output tiles (optionally split
-// along K).  Warp 0 issues TMA loads into a STAGES-deep shared-memory ring,
-// warp 1 issues tcgen05.mma from one elected lane into one of two TMEM
-// accumulators (double-buffered, so the epilogue of tile i overlaps the
-// mainloop of tile i+1), and warps 2..5 run the epilogue (one TMEM lane = one
-// output row per thread).  Operands may be K-major or MN-major in global
-// memory; both are staged with 128-byte swizzle and described to the tensor
-// core with the matching smem descriptor, so no transposes are ever written.
+// The grid is a set of 2-CTA clusters, one CTA per SM.  Each pair walks a
+// static list of 256 x BN output tiles (optionally split along K): every CTA
+// stages its own 128 rows of A and its own BN/2 columns of B, and the pair's
+// leader issues one tcgen05.mma.cta_group::2 of M = 256 per 16-deep k-step,
+// which reads both CTAs' shared memory and leaves each CTA's 128 accumulator
+// rows in its own TMEM.  Per SM this halves the B traffic through shared
+// memory, whose bandwidth (TMA writes plus tensor-core reads) is what bounds a
+// 128 x BN single-CTA tile at K = 512.
+//
+// Roles per CTA: warp 0 issues the TMA loads into a STAGES-deep ring (counted
+// on the leader's "full" barrier), warp 1 of the leader issues the MMAs into
+// one of two TMEM accumulators (double-buffered, so the epilogue of tile i
+// overlaps the mainloop of tile i+1), and the epilogue warps (one TMEM lane =
+// one output row per thread) read the accumulator, release it to the leader,
+// and write their results through a swizzled shared-memory staging tile with
+// TMA stores, so that no epilogue access to global memory is row-per-thread.
+// Operands may be K-major or MN-major in global memory; both are staged with
+// 128-byte swizzle and described to the tensor core with the matching smem
+// descriptor, so no transposes are ever written.
 //
 // Epilogues carry the block's elementwise work so it never makes its own pass
 // over HBM:
-//   EPI_QKVG  : per-head q/k RMSNorm + interleaved rotary, v copy, sigmoid(g),
-//               scatter to [B, H, T, N]   (fast_triton_attn.py:102-144)
+//   EPI_QKVG  : row scale (the fused input RMSNorm), per-head q/k RMSNorm +
+//               interleaved rotary, v copy, sigmoid(g), [B, H, T, N] outputs
+//               (fast_triton_attn.py:102-144); rotary-table rows come in by TMA
 //   EPI_DGATE : gate backward (dO = dGated*g, dg_pre = dGated*O*g(1-g)) and
 //               delta = rowsum(dO*O) for the attention backward
-//               (fast_triton_attn.py:581-584, :601)
-//   EPI_BF16 / EPI_F32 / EPI_RED_F32 : plain stores / split-K fp32 reduction.
+//               (fast_triton_attn.py:581-584, :601); O and g rows come in by TMA
+//   EPI_BF16 / EPI_F32 / EPI_RED_F32 : plain stores / split-K fp32 TMA reduce-add.
 #pragma once
 #include <cuda.h>
 
@@ -30,444 +42,479 @@ enum AMode : int { A_K = 0, A_MN = 1 };
 enum BMode : int { B_K = 0, B_MN = 1, B_SLABS = 2, B_MN_KSPLIT4 = 3 };
 enum EpiMode : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_RED_F32 = 2, EPI_QKVG = 3, EPI_DGATE = 4 };
 
+// out: EPI_BF16/F32/RED_F32 out[0] = D; EPI_QKVG out[0..3] = q, k, v, sigmoid(g)
+// ([B*H*T, N] views); EPI_DGATE out[0] = dO ([B*H*T, N]), out[1] = dg_pre
+// ([M, H*N] view of the g slot).  in: EPI_QKVG the rotary tables f1, f2
+// ([T_max, N]); EPI_DGATE O and sigmoid(g) ([B*H*T, N]).
 struct GemmMaps {
   CUtensorMap a;
   CUtensorMap b[4];
+  CUtensorMap out[4];
+  CUtensorMap in[2];
 };
 
 struct GemmParams {
   int M, N, K;
-  int m_tiles, n_tiles, k_splits, kb_per_split, kb_total;
+  int m_pairs, n_tiles, k_splits, kb_per_split, kb_total;
   int b_kb_per_src;  // B_MN_KSPLIT4: k-blocks taken from each of the 4 B tensors
   int slab_rows;     // B_SLABS: rows of one slab (= head dim)
   int* status;
-  // EPI_BF16 / EPI_F32 / EPI_RED_F32: D[m, n] -> out[m * ldo + n]
-  void* out;
-  long long ldo;
   // EPI_QKVG
-  __nv_bfloat16 *q, *k, *v, *g;
-  const __nv_bfloat16 *f1, *f2;
-  long long ldf;
   float *rq, *rk;
   const float* row_scale;
   int T, H, hd;
   float eps;
   // EPI_DGATE
-  const __nv_bfloat16 *o_in, *gs_in;
-  __nv_bfloat16 *do_out, *dg_out;
-  long long ld_dg;
   float* delta;
 };
 
-constexpr int GEMM_BM = 128;
+constexpr int GEMM_BM = 128;  // rows per CTA; a pair covers 256
 constexpr int GEMM_BK = 64;
 constexpr uint32_t GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
+constexpr uint32_t GEMM_SMEM_LIMIT = 232448;              // 227 KB opt-in per block
 
-// EPI_QKVG runs eight epilogue warps (two groups splitting the q/k/v/g slabs)
-// that stage each slab in shared memory and copy it out with coalesced stores;
-// the other epilogues run four warps storing straight from registers.  Shared
-// memory: stage ring, then the staging tile, then the barriers.
-template <int BN, int EPI>
+// Shared memory: A ring, B ring, epilogue staging (per warp), epilogue inputs
+// (rotary tables per TMEM lane quarter, or O / sigmoid(g) buffers per warp),
+// barriers.  Every region starts on a 1024-byte boundary (128-byte swizzle
+// atoms).  The ring takes whatever the epilogue leaves, up to 8 stages.
+template <int BN, int EPI, int HD>
 struct GemmCfg {
   static constexpr bool QKVG = EPI == EPI_QKVG;
+  static constexpr bool DGATE = EPI == EPI_DGATE;
   static constexpr int EPI_WARPS = QKVG ? 8 : 4;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  static constexpr int STAGES = QKVG ? 3 : (BN >= 256 ? 4 : 6);
-  static constexpr uint32_t STAGING_BYTES = QKVG ? GEMM_BM * BN * 2 : 0;
-  static constexpr uint32_t B_BYTES = BN * GEMM_BK * 2;
+  static constexpr uint32_t B_BYTES = (BN / 2) * GEMM_BK * 2;
   static constexpr uint32_t STAGE_BYTES = GEMM_A_BYTES + B_BYTES;
+  // DGATE: O / sigmoid(g) input buffers per warp (double-buffered below N = 128)
+  static constexpr int IN_BUFS = DGATE ? (HD >= 128 ? 1 : 2) : 0;
+  static constexpr uint32_t WARP_STG = QKVG ? 32u * BN
+                                       : EPI == EPI_BF16 ? 64u * BN
+                                       : DGATE ? 128u * HD
+                                               : 32u * (BN < 128 ? BN : 128) * 4;
+  static constexpr uint32_t STAGING = EPI_WARPS * WARP_STG;
+  static constexpr uint32_t INPUTS = QKVG ? 512u * HD : DGATE ? 4u * IN_BUFS * 128u * HD : 0;
+  static constexpr uint32_t FIXED = 1024 + STAGING + INPUTS + 256;
+  static constexpr int STAGES_FIT = int((GEMM_SMEM_LIMIT - FIXED) / STAGE_BYTES);
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + STAGING_BYTES + 256;
+  static constexpr size_t SMEM = FIXED + size_t(STAGES) * STAGE_BYTES;
+  static_assert(STAGES >= 3, "GEMM: shared memory leaves fewer than 3 pipeline stages");
+  static_assert(WARP_STG % 1024 == 0 && INPUTS % 1024 == 0, "GEMM: 1024-byte regions");
 };
 
-__device__ __forceinline__ void gemm_decode(const GemmParams& p, int BN, int t, int& m0, int& n0, int& kb0, int& kb1) {
-  const int mn = p.m_tiles * p.n_tiles;
-  const int split = t / mn;
-  const int r = t - split * mn;
+// Work unit u -> pair row base m0 (256 rows), column base n0, k-block range.
+__device__ __forceinline__ void gemm_decode(const GemmParams& p, int BN, int u, int& m0, int& n0, int& kb0, int& kb1) {
+  const int mn = p.m_pairs * p.n_tiles;
+  const int split = u / mn;
+  const int r = u - split * mn;
   const int mt = r / p.n_tiles;
   const int nt = r - mt * p.n_tiles;
-  m0 = mt * GEMM_BM;
+  m0 = mt * 2 * GEMM_BM;
   n0 = nt * BN;
   kb0 = split * p.kb_per_split;
   kb1 = min(kb0 + p.kb_per_split, p.kb_total);
 }
 
 // ---------------------------------------------------------------------------
-// Epilogues.  `taddr` is this warp's TMEM lane block + accumulator column 0;
-// `m` the output row this thread owns.
+// Staging geometry.  A box is 32 rows (one warp's TMEM lane quarter) of a tile
+// 64 elements wide (128-byte rows, 128-byte swizzle: 16-byte unit u of row r at
+// u ^ (r & 7)) or 32 bf16 wide (64-byte rows, 64-byte swizzle: unit u at
+// u ^ ((r >> 1) & 3)) -- the layouts TMA reads and writes for those swizzle
+// modes.  With one row per lane, a warp's 16-byte accesses of one unit column
+// touch every bank exactly four times (the minimum for 512 bytes).
 // ---------------------------------------------------------------------------
-template <int BN>
-__device__ __forceinline__ void epi_store(const GemmParams& p, int mode, uint32_t taddr, int m, int n0) {
-  for (int c = 0; c < BN; c += 32) {
-    uint32_t r[32];
-    tmem_load32(taddr + c, r);
-    if (mode == EPI_BF16) {
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(m) * p.ldo + n0 + c;
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        st_global_v4(dst + 8 * j, pack_bf16(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1])),
-                     pack_bf16(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3])),
-                     pack_bf16(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5])),
-                     pack_bf16(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7])));
-    } else if (mode == EPI_F32) {
-      float* dst = reinterpret_cast<float*>(p.out) + size_t(m) * p.ldo + n0 + c;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) st_global_v4(dst + 4 * j, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-    } else {
-      float* dst = reinterpret_cast<float*>(p.out) + size_t(m) * p.ldo + n0 + c;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        red_add_v4_f32(dst + 4 * j, __uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                       __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-    }
-  }
+__device__ __forceinline__ uint32_t swz128(uint32_t box, int r, int u) { return box + r * 128 + ((u ^ (r & 7)) << 4); }
+__device__ __forceinline__ uint32_t swz64(uint32_t box, int r, int u) {
+  return box + r * 64 + ((u ^ ((r >> 1) & 3)) << 4);
 }
-
-// Staging tile of one slab: 128 rows of 2*HD bytes; 16-byte unit u of row r sits
-// at u ^ (r & 7) within the row (u ^ (r & 3) for HD = 32), so that the row-per-
-// thread writes and the unit-per-thread copy-out both spread over the banks.
+// Unit u of row r in a 32-row tile HD bf16 wide (boxes of 64 columns, 4 KB each).
 template <int HD>
-__device__ __forceinline__ uint32_t stage_addr(uint32_t slab, int r, int u) {
-  constexpr int UPR = HD / 8;  // 16-byte units per row
-  constexpr int MASK = UPR >= 8 ? 7 : UPR - 1;
-  return slab + r * (HD * 2) + ((u ^ (r & MASK)) << 4);
+__device__ __forceinline__ uint32_t hd_unit(uint32_t tile, int r, int u) {
+  if constexpr (HD == 32) return swz64(tile, r, u);
+  else return swz128(tile + (u >> 3) * 4096, r, u & 7);
 }
-template <int HD>
-__device__ __forceinline__ void stage_unit(uint32_t slab, int r, int u, const uint32_t* w) {
-  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(stage_addr<HD>(slab, r, u)), "r"(w[0]), "r"(w[1]),
-               "r"(w[2]), "r"(w[3])
+__device__ __forceinline__ void sts_v4(uint32_t addr, const uint32_t* w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
                : "memory");
 }
-// Copy a staged slab (128 consecutive rows of one [B,H,T,N] output) to global
-// memory: the group's 128 threads move consecutive 16-byte units.
-template <int HD>
-__device__ __forceinline__ void copy_out_slab(uint32_t slab, __nv_bfloat16* dst, int ti) {
-  constexpr int UPR = HD / 8;
-#pragma unroll 4
-  for (int i = ti; i < 128 * UPR; i += 128) {
-    const int r = i / UPR, u = i - (i / UPR) * UPR;
-    uint32_t w0, w1, w2, w3;
-    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
-                 : "r"(stage_addr<HD>(slab, r, u)) : "memory");
-    st_global_v4(dst + size_t(i) * 8, w0, w1, w2, w3);
-  }
+__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void tmem_wait_ld_tied2x32(uint32_t (&a)[32], uint32_t (&b)[32]) {
+  tmem_wait_ld_tied(a);
+  asm volatile("" : "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]),
+               "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15]),
+               "+r"(b[16]), "+r"(b[17]), "+r"(b[18]), "+r"(b[19]), "+r"(b[20]), "+r"(b[21]), "+r"(b[22]),
+               "+r"(b[23]), "+r"(b[24]), "+r"(b[25]), "+r"(b[26]), "+r"(b[27]), "+r"(b[28]), "+r"(b[29]),
+               "+r"(b[30]), "+r"(b[31])::"memory");
 }
 
-// Rotary-table columns [c, c+32) of one table row, as four 16-byte pieces per table.
-template <int HD>
-__device__ __forceinline__ void load_tab_chunk(const __nv_bfloat16* f1row, const __nv_bfloat16* f2row, int c,
-                                               uint4 (&t1)[4], uint4 (&t2)[4]) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    t1[j] = *reinterpret_cast<const uint4*>(f1row + c + 8 * j);
-    t2[j] = *reinterpret_cast<const uint4*>(f2row + c + 8 * j);
-  }
+// Hand this warp's share of an accumulator buffer back to the pair's MMA issuer.
+__device__ __forceinline__ void release_acc(uint32_t acce_cl, int lane) {
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive_cluster(acce_cl);
+}
+// Before a warp rewrites its staging tile: its previous TMA stores have read it.
+__device__ __forceinline__ void staging_acquire(int lane) {
+  if (lane == 0) bulk_wait_read0();
+  __syncwarp();
+}
+// After a warp's st.shared of a staging tile: visible to the TMA (async proxy).
+__device__ __forceinline__ void staging_publish() {
+  fence_proxy_async_smem();
+  __syncwarp();
 }
 
-// q/k RMSNorm over the head dim, bf16 rounding of the normed value, then
-// interleaved rotary out[n] = qn[n]*f1[t,n] + qn[n^1]*f2[t,n]
-// (fast_triton_attn.py:102-106, :132-141); v stored as is (fast_triton_attn.py:108)
-// and g as sigmoid(g) (fast_triton_attn.py:123).  One slab (q, k, v or g of one
-// head) of this thread's row, written bf16 to its [B,H,T,N] output row in
-// 32-column chunks; rotary-table rows are loaded one chunk ahead of their use.
-// QK: q or k (per-head RMSNorm + rotary, with the rotary rows of chunks 0 and 1
-// preloaded in t1/t2 and later chunks streamed one ahead); else v or sigmoid(g).
-template <int HD, bool QK>
-__device__ __forceinline__ void qkvg_slab(const GemmParams& p, uint32_t tcol, uint32_t slab, int r, int typ, float rs,
-                                          size_t bht, const __nv_bfloat16* f1row, const __nv_bfloat16* f2row,
-                                          uint4 (&t1)[2][4], uint4 (&t2)[2][4]) {
-  constexpr int NCH = HD / 32;
-  float sc = rs;
-  if (QK) {
-    float ss = 0.f;
+// ---------------------------------------------------------------------------
+// Epilogues.  `taddr` is this warp's TMEM lane quarter + accumulator column 0;
+// `row0` the output row of lane 0, `stg` this warp's staging tile.
+// ---------------------------------------------------------------------------
+template <int BN>
+__device__ __forceinline__ void epi_bf16(const GemmMaps& maps, uint32_t taddr, uint32_t stg, int lane, int row0, int n0,
+                                         uint32_t acce_cl) {
+  staging_acquire(lane);
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 64) {
+    uint32_t r0[32], r1[32];
+    tmem_ld32(taddr + c, r0);
+    tmem_ld32(taddr + c + 32, r1);
+    tmem_wait_ld_tied2x32(r0, r1);
+    const uint32_t box = stg + (c >> 6) * 4096;
 #pragma unroll
-    for (int ci = 0; ci < NCH; ++ci) {
-      uint32_t v[32];
-      tmem_load32(tcol + 32 * ci, v);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float x = __uint_as_float(v[j]) * rs;
-        ss = fmaf(x, x, ss);
-      }
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t* r = j < 4 ? r0 + 8 * j : r1 + 8 * (j - 4);
+      const uint32_t w[4] = {pack_bf16(__uint_as_float(r[0]), __uint_as_float(r[1])),
+                             pack_bf16(__uint_as_float(r[2]), __uint_as_float(r[3])),
+                             pack_bf16(__uint_as_float(r[4]), __uint_as_float(r[5])),
+                             pack_bf16(__uint_as_float(r[6]), __uint_as_float(r[7]))};
+      sts_v4(swz128(box, lane, j), w);
     }
-    const float inv = rsqrtf(ss / float(HD) + p.eps);
-    float* rdst = typ == 0 ? p.rq : p.rk;
-    if (rdst) rdst[bht] = inv;
-    sc = rs * inv;
   }
+  release_acc(acce_cl, lane);
+  staging_publish();
+  if (lane == 0) {
 #pragma unroll
-  for (int ci = 0; ci < NCH; ++ci) {
-    const int c = 32 * ci;
-    if (QK && ci >= 1 && ci + 1 < NCH) load_tab_chunk<HD>(f1row, f2row, c + 32, t1[(ci + 1) & 1], t2[(ci + 1) & 1]);
-    uint32_t v[32];
-    tmem_load32(tcol + c, v);
-    uint32_t pk[16];
-    if (QK) {
+    for (int bx = 0; bx < BN / 64; ++bx) tma_store_2d(&maps.out[0], stg + bx * 4096, n0 + 64 * bx, row0);
+    bulk_commit();
+  }
+}
+
+// fp32 output (RED: TMA reduce-add into it), 128 columns per staging round.
+template <int BN, bool RED>
+__device__ __forceinline__ void epi_f32(const GemmMaps& maps, uint32_t taddr, uint32_t stg, int lane, int row0, int n0,
+                                        uint32_t acce_cl) {
+  constexpr int CH = BN < 128 ? BN : 128;
+#pragma unroll 1
+  for (int h = 0; h < BN; h += CH) {
+    staging_acquire(lane);
+#pragma unroll 1
+    for (int c = 0; c < CH; c += 32) {
+      uint32_t r[32];
+      tmem_load32(taddr + h + c, r);
+      const uint32_t box = stg + (c >> 5) * 4096;
 #pragma unroll
-      for (int v4 = 0; v4 < 4; ++v4) {
-        const uint32_t w1[4] = {t1[ci & 1][v4].x, t1[ci & 1][v4].y, t1[ci & 1][v4].z, t1[ci & 1][v4].w};
-        const uint32_t w2[4] = {t2[ci & 1][v4].x, t2[ci & 1][v4].y, t2[ci & 1][v4].z, t2[ci & 1][v4].w};
+      for (int j = 0; j < 8; ++j) sts_v4(swz128(box, lane, j), r + 4 * j);
+    }
+    if (h + CH >= BN) release_acc(acce_cl, lane);
+    staging_publish();
+    if (lane == 0) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = v4 * 4 + e;
-          const float qa = round_bf16(__uint_as_float(v[2 * j]) * sc);
-          const float qb = round_bf16(__uint_as_float(v[2 * j + 1]) * sc);
-          pk[j] = pack_bf16(qa * bf16_lo(w1[e]) + qb * bf16_lo(w2[e]), qb * bf16_hi(w1[e]) + qa * bf16_hi(w2[e]));
-        }
+      for (int bx = 0; bx < CH / 32; ++bx) {
+        if (RED) tma_reduce_add_2d(&maps.out[0], stg + bx * 4096, n0 + h + 32 * bx, row0);
+        else tma_store_2d(&maps.out[0], stg + bx * 4096, n0 + h + 32 * bx, row0);
       }
+      bulk_commit();
+    }
+  }
+}
+
+// q or k slab of this lane's row: per-head RMSNorm over the head dim, bf16
+// rounding of the normed value, then interleaved rotary
+//   out[n] = qn[n]*f1[t,n] + qn[n^1]*f2[t,n]      (fast_triton_attn.py:102-106, :132-141)
+// with the rotary-table row read from the quarter's table tile.  `rs` is the
+// row's input-norm scale (1 when the GEMM input is already normalised).
+template <int HD>
+__device__ __forceinline__ void qk_slab(const GemmParams& p, uint32_t tcol, uint32_t slab, uint32_t tab, int lane,
+                                        int typ, float rs, size_t bht, bool valid) {
+  constexpr int NCH = HD / 32;
+  constexpr uint32_t TAB_BYTES = 32 * HD * 2;
+  uint32_t v[HD <= 64 ? NCH : 1][32];
+  float ss0 = 0.f, ss1 = 0.f;
+  if constexpr (HD <= 64) {
+    tmem_ld32(tcol, v[0]);
+    if constexpr (NCH == 2) {
+      tmem_ld32(tcol + 32, v[NCH - 1]);
+      tmem_wait_ld_tied2x32(v[0], v[NCH - 1]);
     } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float a = __uint_as_float(v[2 * j]) * rs;
-        float bb = __uint_as_float(v[2 * j + 1]) * rs;
-        if (typ == 3) {
-          a = __fdividef(1.0f, 1.0f + __expf(-a));
-          bb = __fdividef(1.0f, 1.0f + __expf(-bb));
-        }
-        pk[j] = pack_bf16(a, bb);
-      }
+      tmem_wait_ld_tied(v[0]);
     }
-    // 32 columns = 4 16-byte units of the row, in column chunk c / 64
-#pragma unroll
-    for (int j = 0; j < 4; ++j) stage_unit<HD>(slab, r, c / 8 + j, pk + 4 * j);
-  }
-}
-
-// The same for head dims <= 64, with one TMEM round trip per slab: the whole
-// row of the slab is loaded at once (both 32-column chunks in flight), the
-// rotary-table row is fetched alongside so its latency overlaps the TMEM wait,
-// and the values stay in registers from the sum of squares to the rotary.
-template <int HD, bool QK>
-__device__ __forceinline__ void qkvg_slab_row(const GemmParams& p, uint32_t tcol, uint32_t slab, int r, int typ,
-                                              float rs, size_t bht, const __nv_bfloat16* f1row,
-                                              const __nv_bfloat16* f2row) {
-  static_assert(HD == 32 || HD == 64, "row-at-once slab: head dim 32 or 64");
-  constexpr int NCH = HD / 32;
-  uint32_t v[NCH][32];
-  uint4 w1[HD / 8], w2[HD / 8];
-#pragma unroll
-  for (int ci = 0; ci < NCH; ++ci) tmem_ld32(tcol + 32 * ci, v[ci]);
-  if (QK) {
-#pragma unroll
-    for (int j = 0; j < HD / 8; ++j) {
-      w1[j] = __ldg(reinterpret_cast<const uint4*>(f1row) + j);
-      w2[j] = __ldg(reinterpret_cast<const uint4*>(f2row) + j);
-    }
-  }
-#pragma unroll
-  for (int ci = 0; ci < NCH; ++ci) tmem_wait_ld_tied(v[ci]);
-  float sc = rs;
-  if (QK) {
-    float ss0 = 0.f, ss1 = 0.f;
 #pragma unroll
     for (int ci = 0; ci < NCH; ++ci)
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
-        const float x0 = __uint_as_float(v[ci][j]) * rs, x1 = __uint_as_float(v[ci][j + 1]) * rs;
+        const float x0 = __uint_as_float(v[ci][j]), x1 = __uint_as_float(v[ci][j + 1]);
         ss0 = fmaf(x0, x0, ss0);
         ss1 = fmaf(x1, x1, ss1);
       }
-    const float inv = rsqrtf((ss0 + ss1) / float(HD) + p.eps);
-    float* rdst = typ == 0 ? p.rq : p.rk;
-    if (rdst) rdst[bht] = inv;
-    sc = rs * inv;
-  }
-#pragma unroll
-  for (int ci = 0; ci < NCH; ++ci) {
-    const int c = 32 * ci;
-    uint32_t pk[16];
-    if (QK) {
-#pragma unroll
-      for (int v4 = 0; v4 < 4; ++v4) {
-        const uint4 a1 = w1[ci * 4 + v4], a2 = w2[ci * 4 + v4];
-        const uint32_t x1[4] = {a1.x, a1.y, a1.z, a1.w}, x2[4] = {a2.x, a2.y, a2.z, a2.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = v4 * 4 + e;
-          const float qa = round_bf16(__uint_as_float(v[ci][2 * j]) * sc);
-          const float qb = round_bf16(__uint_as_float(v[ci][2 * j + 1]) * sc);
-          pk[j] = pack_bf16(qa * bf16_lo(x1[e]) + qb * bf16_lo(x2[e]), qb * bf16_hi(x1[e]) + qa * bf16_hi(x2[e]));
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float a = __uint_as_float(v[ci][2 * j]) * rs;
-        float bb = __uint_as_float(v[ci][2 * j + 1]) * rs;
-        if (typ == 3) {
-          a = __fdividef(1.0f, 1.0f + __expf(-a));
-          bb = __fdividef(1.0f, 1.0f + __expf(-bb));
-        }
-        pk[j] = pack_bf16(a, bb);
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) stage_unit<HD>(slab, r, c / 8 + j, pk + 4 * j);
-  }
-}
-
-// q/k RMSNorm over the head dim, bf16 rounding of the normed value, then
-// interleaved rotary out[n] = qn[n]*f1[t,n] + qn[n^1]*f2[t,n]
-// (fast_triton_attn.py:102-106, :132-141); v stored as is (fast_triton_attn.py:108)
-// and g as sigmoid(g) (fast_triton_attn.py:123).  This thread's row of each
-// slab its group owns (slabs s with s % 2 == wg) goes straight to the slab's
-// [B,H,T,N] output.  For N = 128 the q/k slabs go first, while the rotary rows
-// preloaded by the caller are live, and v/g follow.
-template <int BN, int HD>
-__device__ __forceinline__ void epi_qkvg(const GemmParams& p, uint32_t taddr, int m, int n0, int wg, int r, int ti,
-                                         uint32_t stg, uint4 (&t1)[2][4], uint4 (&t2)[2][4]) {
-  constexpr int NSLAB = BN / HD;
-  constexpr uint32_t SLAB_BYTES = GEMM_BM * HD * 2;
-  const int b = m / p.T;
-  const int t = m - b * p.T;
-  const float rs = p.row_scale ? p.row_scale[m] : 1.0f;
-  const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
-  const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
-  // the group's previous copy-out has read the staging tile
-  named_bar_sync(1 + wg, 128);
-  if constexpr (HD <= 64) {
-#pragma unroll 1
-    for (int s = wg; s < NSLAB; s += 2) {
-      const int sg = n0 / HD + s;
-      const size_t bht = (size_t(b) * p.H + (sg >> 2)) * p.T + t;
-      if ((sg & 3) < 2)
-        qkvg_slab_row<HD, true>(p, taddr + s * HD, stg + s * SLAB_BYTES, r, sg & 3, rs, bht, f1row, f2row);
-      else
-        qkvg_slab_row<HD, false>(p, taddr + s * HD, stg + s * SLAB_BYTES, r, sg & 3, rs, bht, f1row, f2row);
-    }
   } else {
 #pragma unroll 1
-    for (int s = wg; s < NSLAB; s += 2) {
-      const int sg = n0 / HD + s;
-      if ((sg & 3) < 2)
-        qkvg_slab<HD, true>(p, taddr + s * HD, stg + s * SLAB_BYTES, r, sg & 3, rs,
-                            (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row, t1, t2);
+    for (int ci = 0; ci < NCH; ++ci) {
+      uint32_t w[32];
+      tmem_load32(tcol + 32 * ci, w);
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const float x0 = __uint_as_float(w[j]), x1 = __uint_as_float(w[j + 1]);
+        ss0 = fmaf(x0, x0, ss0);
+        ss1 = fmaf(x1, x1, ss1);
+      }
     }
-#pragma unroll 1
-    for (int s = wg; s < NSLAB; s += 2) {
-      const int sg = n0 / HD + s;
-      if ((sg & 3) >= 2)
-        qkvg_slab<HD, false>(p, taddr + s * HD, stg + s * SLAB_BYTES, r, sg & 3, rs,
-                             (size_t(b) * p.H + (sg >> 2)) * p.T + t, f1row, f2row, t1, t2);
+  }
+  const float inv = rsqrtf((ss0 + ss1) * (rs * rs) / float(HD) + p.eps);
+  if (valid) {
+    float* rdst = typ == 0 ? p.rq : p.rk;
+    if (rdst) rdst[bht] = inv;
+  }
+  const float sc = rs * inv;
+#pragma unroll
+  for (int ci = 0; ci < NCH; ++ci) {
+    uint32_t wbuf[32];
+    const uint32_t* w;
+    if constexpr (HD <= 64) {
+      w = v[ci];
+    } else {
+      tmem_load32(tcol + 32 * ci, wbuf);
+      w = wbuf;
+    }
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+      const int u = 4 * ci + j4;
+      const uint4 a1 = lds_v4(hd_unit<HD>(tab, lane, u));
+      const uint4 a2 = lds_v4(hd_unit<HD>(tab + TAB_BYTES, lane, u));
+      const uint32_t x1[4] = {a1.x, a1.y, a1.z, a1.w}, x2[4] = {a2.x, a2.y, a2.z, a2.w};
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = 8 * j4 + 2 * e;
+        const float qa = round_bf16(__uint_as_float(w[j]) * sc);
+        const float qb = round_bf16(__uint_as_float(w[j + 1]) * sc);
+        pk[e] = pack_bf16(qa * bf16_lo(x1[e]) + qb * bf16_lo(x2[e]), qb * bf16_hi(x1[e]) + qa * bf16_hi(x2[e]));
+      }
+      sts_v4(hd_unit<HD>(slab, lane, u), pk);
     }
   }
 }
 
-// Copy-out of the slabs staged by epi_qkvg (after the group's barrier).
-template <int BN, int HD>
-__device__ __forceinline__ void epi_qkvg_copy_out(const GemmParams& p, int m0, int n0, int wg, int ti, uint32_t stg) {
-  constexpr int NSLAB = BN / HD;
-  const int b = m0 / p.T, t0 = m0 - (m0 / p.T) * p.T;
-  named_bar_sync(1 + wg, 128);
+// v slab (stored as is, fast_triton_attn.py:108) or g slab (sigmoid, :123).
+template <int HD>
+__device__ __forceinline__ void vg_slab(uint32_t tcol, uint32_t slab, int lane, bool sig, float rs) {
 #pragma unroll 1
-  for (int s = wg; s < NSLAB; s += 2) {
+  for (int ci = 0; ci < HD / 32; ++ci) {
+    uint32_t w[32];
+    tmem_load32(tcol + 32 * ci, w);
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = 8 * j4 + 2 * e;
+        float a = __uint_as_float(w[j]) * rs;
+        float b = __uint_as_float(w[j + 1]) * rs;
+        if (sig) {
+          a = __fdividef(1.0f, 1.0f + __expf(-a));
+          b = __fdividef(1.0f, 1.0f + __expf(-b));
+        }
+        pk[e] = pack_bf16(a, b);
+      }
+      sts_v4(hd_unit<HD>(slab, lane, 4 * ci + j4), pk);
+    }
+  }
+}
+
+// Projection epilogue of one tile for this warp: its group's slabs (s % 2 ==
+// wg) of its 32 rows, staged per slab and written by TMA to the slab's
+// [B,H,T,N] output.  q/k slabs wait for the quarter's rotary-table tile.
+template <int BN, int HD>
+__device__ __forceinline__ void epi_qkvg(const GemmMaps& maps, const GemmParams& p, uint32_t taddr, uint32_t stg,
+                                         uint32_t tab, uint32_t tab_full, uint32_t tab_empty, uint32_t tab_par,
+                                         int lane, int wg, int mq, int n0, uint32_t acce_cl, Guard& g) {
+  constexpr int NJ = BN / HD / 2;
+  constexpr uint32_t SLAB_BYTES = 32 * HD * 2;
+  const int b = mq / p.T;
+  const int tq = mq - b * p.T;  // token of lane 0
+  const int m = mq + lane;
+  const bool valid = m < p.M;
+  const float rs = p.row_scale ? __ldg(p.row_scale + (valid ? m : p.M - 1)) : 1.0f;
+  staging_acquire(lane);
+  bool any_qk = false;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int s = wg + 2 * j;
     const int sg = n0 / HD + s;
     const int typ = sg & 3;
-    __nv_bfloat16* out = (typ == 0 ? p.q : typ == 1 ? p.k : typ == 2 ? p.v : p.g) +
-                         ((size_t(b) * p.H + (sg >> 2)) * p.T + t0) * HD;
-    copy_out_slab<HD>(stg + s * (GEMM_BM * HD * 2), out, ti);
+    if (typ < 2) {
+      if (!any_qk) {
+        bool ok = mbar_wait(tab_full, tab_par, g, 7);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) g.ok = false;
+        any_qk = true;
+      }
+      const size_t bht = (size_t(b) * p.H + (sg >> 2)) * p.T + tq + lane;
+      qk_slab<HD>(p, taddr + s * HD, stg + j * SLAB_BYTES, tab, lane, typ, rs, bht, valid);
+    } else {
+      vg_slab<HD>(taddr + s * HD, stg + j * SLAB_BYTES, lane, typ == 3, rs);
+    }
+  }
+  if (any_qk) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tab_empty);
+  }
+  release_acc(acce_cl, lane);
+  staging_publish();
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int sg = n0 / HD + wg + 2 * j;
+      const int row = (b * p.H + (sg >> 2)) * p.T + tq;
+#pragma unroll
+      for (int bx = 0; bx < (HD + 63) / 64; ++bx)
+        tma_store_2d(&maps.out[sg & 3], stg + j * SLAB_BYTES + bx * 4096, 64 * bx, row);
+    }
+    bulk_commit();
   }
 }
 
-
-// Gate backward fused on the dGated = dY * Wo tile (fast_triton_attn.py:576-584, :601):
+// Gate backward on the dGated = dY * Wo tile, head by head (fast_triton_attn.py:576-584, :601):
 //   dO = dGated*g  -> [B,H,T,N] bf16 (input of the attention backward)
 //   dg_pre = dGated*O*g*(1-g) -> the g slot of the projection-gradient buffer
 //   delta = rowsum(dO*O) per (b,h,t)  (the attention backward's D term)
-template <int BN, int HD>
-__device__ __forceinline__ void epi_dgate(const GemmParams& p, uint32_t taddr, int m, int n0) {
-  constexpr int hd = HD;
-  const int b = m / p.T;
-  const int t = m - b * p.T;
-  constexpr int nslab = BN / hd;
-  constexpr int nch = hd / 32;
-#pragma unroll 1
-  for (int s = 0; s < nslab; ++s) {
-    const int head = n0 / hd + s;
-    const size_t bht = (size_t(b) * p.H + head) * p.T + t;
-    const __nv_bfloat16* orow = p.o_in + bht * hd;
-    const __nv_bfloat16* grow = p.gs_in + bht * hd;
-    __nv_bfloat16* dorow = p.do_out + bht * hd;
-    __nv_bfloat16* dgrow = p.dg_out + size_t(m) * p.ld_dg + size_t(head) * hd;
-    float dsum = 0.f;
-    // O and sigmoid(g) of the row are loaded one 32-column chunk ahead of their use.
-    uint4 ob[2][4], gb[2][4];
+// O and sigmoid(g) of each head come in by TMA into per-warp buffers, two heads
+// ahead (one for N = 128), so their latency overlaps the mainloop and the
+// previous head.  `hc` counts this warp's heads across tiles (buffer phases).
+template <int BN, int HD, int IN_BUFS>
+__device__ __forceinline__ void dgate_issue(const GemmMaps& maps, uint32_t inb, uint32_t in_bar, int b, int H, int T,
+                                            int tq, int head) {
+  constexpr uint32_t TILE = 32 * HD * 2;
+  const int row = (b * H + head) * T + tq;
+  mbar_expect_tx(in_bar, 2 * TILE);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      ob[0][j] = *reinterpret_cast<const uint4*>(orow + 8 * j);
-      gb[0][j] = *reinterpret_cast<const uint4*>(grow + 8 * j);
-    }
-#pragma unroll
-    for (int ci = 0; ci < nch; ++ci) {
-      const int c = 32 * ci;
-      const int cur = ci & 1;
-      if (ci + 1 < nch) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          ob[cur ^ 1][j] = *reinterpret_cast<const uint4*>(orow + c + 32 + 8 * j);
-          gb[cur ^ 1][j] = *reinterpret_cast<const uint4*>(grow + c + 32 + 8 * j);
-        }
-      }
-      uint32_t r[32];
-      tmem_load32(taddr + s * hd + c, r);
-      uint32_t pd[16], pg[16];
-#pragma unroll
-      for (int v4 = 0; v4 < 4; ++v4) {
-        const uint4 ov = ob[cur][v4];
-        const uint4 gv = gb[cur][v4];
-        const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
-        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = v4 * 4 + e;
-          const float o0 = bf16_lo(ow[e]), o1 = bf16_hi(ow[e]);
-          const float g0 = bf16_lo(gw[e]), g1 = bf16_hi(gw[e]);
-          const float d0 = __uint_as_float(r[2 * j]), d1 = __uint_as_float(r[2 * j + 1]);
-          const float do0 = round_bf16(d0 * g0), do1 = round_bf16(d1 * g1);
-          dsum = fmaf(do0, o0, dsum);
-          dsum = fmaf(do1, o1, dsum);
-          pd[j] = pack_bf16(do0, do1);
-          pg[j] = pack_bf16(d0 * o0 * g0 * (1.0f - g0), d1 * o1 * g1 * (1.0f - g1));
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        st_global_v4(dorow + c + 8 * j, pd[4 * j], pd[4 * j + 1], pd[4 * j + 2], pd[4 * j + 3]);
-        st_global_v4(dgrow + c + 8 * j, pg[4 * j], pg[4 * j + 1], pg[4 * j + 2], pg[4 * j + 3]);
-      }
-    }
-    p.delta[bht] = dsum;
+  for (int bx = 0; bx < (HD + 63) / 64; ++bx) {
+    tma_load_2d(inb + bx * 4096, &maps.in[0], in_bar, 64 * bx, row);
+    tma_load_2d(inb + TILE + bx * 4096, &maps.in[1], in_bar, 64 * bx, row);
   }
 }
 
+template <int BN, int HD, int IN_BUFS>
+__device__ __forceinline__ void epi_dgate(const GemmMaps& maps, const GemmParams& p, uint32_t taddr, uint32_t stg,
+                                          uint32_t inb0, uint32_t in_bar0, uint32_t& hc, int lane, int mq, int n0,
+                                          uint32_t acce_cl, Guard& g) {
+  constexpr int NH = BN / HD;
+  constexpr uint32_t TILE = 32 * HD * 2;
+  const int b = mq / p.T;
+  const int tq = mq - b * p.T;
+  const bool valid = mq + lane < p.M;
+  const uint32_t hc0 = hc;
+#pragma unroll 1
+  for (int s = 0; s < NH; ++s, ++hc) {
+    const int head = n0 / HD + s;
+    const uint32_t buf = IN_BUFS == 2 ? (hc & 1) : 0;
+    const uint32_t par = IN_BUFS == 2 ? ((hc >> 1) & 1) : (hc & 1);
+    const uint32_t inb = inb0 + buf * 2 * TILE;
+    const uint32_t in_bar = in_bar0 + 8 * buf;
+    // this head's inputs were issued ahead (the first heads of the tile by the caller)
+    bool ok = mbar_wait(in_bar, par, g, 8);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) {
+      g.ok = false;
+      break;
+    }
+    staging_acquire(lane);
+    float dsum = 0.f;
+#pragma unroll 1
+    for (int ci = 0; ci < HD / 32; ++ci) {
+      uint32_t r[32];
+      tmem_load32(taddr + s * HD + 32 * ci, r);
+#pragma unroll
+      for (int j4 = 0; j4 < 4; ++j4) {
+        const int u = 4 * ci + j4;
+        const uint4 ov = lds_v4(hd_unit<HD>(inb, lane, u));
+        const uint4 gv = lds_v4(hd_unit<HD>(inb + TILE, lane, u));
+        const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
+        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+        uint32_t pd[4], pg[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = 8 * j4 + 2 * e;
+          const float o0 = bf16_lo(ow[e]), o1 = bf16_hi(ow[e]);
+          const float g0 = bf16_lo(gw[e]), g1 = bf16_hi(gw[e]);
+          const float d0 = __uint_as_float(r[j]), d1 = __uint_as_float(r[j + 1]);
+          const float do0 = round_bf16(d0 * g0), do1 = round_bf16(d1 * g1);
+          dsum = fmaf(do0, o0, dsum);
+          dsum = fmaf(do1, o1, dsum);
+          pd[e] = pack_bf16(do0, do1);
+          pg[e] = pack_bf16(d0 * o0 * g0 * (1.0f - g0), d1 * o1 * g1 * (1.0f - g1));
+        }
+        sts_v4(hd_unit<HD>(stg, lane, u), pd);
+        sts_v4(hd_unit<HD>(stg + TILE, lane, u), pg);
+      }
+    }
+    if (valid) p.delta[(size_t(b) * p.H + head) * p.T + tq + lane] = dsum;
+    if (s == NH - 1) release_acc(acce_cl, lane);
+    staging_publish();  // also orders this warp's reads of the input buffer before its refill
+    if (lane == 0) {
+      const int row = (b * p.H + head) * p.T + tq;
+#pragma unroll
+      for (int bx = 0; bx < (HD + 63) / 64; ++bx) {
+        tma_store_2d(&maps.out[0], stg + bx * 4096, 64 * bx, row);
+        tma_store_2d(&maps.out[1], stg + TILE + bx * 4096, head * HD + 64 * bx, mq);
+      }
+      bulk_commit();
+      if (s + IN_BUFS < NH) dgate_issue<BN, HD, IN_BUFS>(maps, inb, in_bar, b, p.H, p.T, tq, head + IN_BUFS);
+    }
+  }
+  hc = hc0 + NH;
+}
+
 // ---------------------------------------------------------------------------
-// The kernel
+// The kernel (launched as 2-CTA clusters)
 // ---------------------------------------------------------------------------
 // HD: head dim for the per-head epilogues (EPI_QKVG, EPI_DGATE), 0 otherwise.
 template <int BN, int AM, int BMD, int EPI, int HD>
-__global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
-  using Cfg = GemmCfg<BN, EPI>;
+__global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
+    gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
+  using Cfg = GemmCfg<BN, EPI, HD>;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr uint32_t IDESC = idesc_bf16(GEMM_BM, BN, AM == A_MN ? 1u : 0u, (BMD == B_MN || BMD == B_MN_KSPLIT4) ? 1u : 0u);
-  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  constexpr uint32_t IDESC =
+      idesc_bf16(2 * GEMM_BM, BN, AM == A_MN ? 1u : 0u, (BMD == B_MN || BMD == B_MN_KSPLIT4) ? 1u : 0u);
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+  constexpr int HB = BN / 2;  // B columns staged by each CTA
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sA = smem_u32(smem);
   const uint32_t sB = sA + STAGES * GEMM_A_BYTES;
-  // barriers after the stage ring and the staging tile
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::STAGING_BYTES);
+  const uint32_t sStg = sB + STAGES * Cfg::B_BYTES;
+  const uint32_t sIn = sStg + Cfg::STAGING;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::STAGING + Cfg::INPUTS);
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
   auto accf_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
   auto acce_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + 2 + b); };
   const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  // QKVG: table full/empty per lane quarter; DGATE: input buffers per epilogue warp
+  auto aux_bar = [&](int i) { return bar0 + 8u * (2 * STAGES + 5 + i); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 13);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int ntiles = p.m_tiles * p.n_tiles * p.k_splits;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int nunits = p.m_pairs * p.n_tiles * p.k_splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -476,9 +523,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf_bar(b), 1);
-      mbar_init(acce_bar(b), 32 * Cfg::EPI_WARPS);
+      mbar_init(acce_bar(b), 2 * Cfg::EPI_WARPS);  // every epilogue warp of both CTAs
     }
     mbar_init(drain_bar, 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(aux_bar(i), 1);
+      mbar_init(aux_bar(4 + i), Cfg::QKVG ? 2 : 1);
+    }
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -486,55 +537,62 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
     for (int i = 0; i < 4; ++i) tma_prefetch_desc(&maps.b[i]);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  // Both CTAs' barriers are initialised before any cross-CTA copy, commit or arrive.
+  cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   Guard g(p.status, KID_GEMM);
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer (both CTAs) ----------------
     if (elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
       int last_par[STAGES];
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
-      for (int t = blockIdx.x; t < ntiles && g.ok; t += gridDim.x) {
+      for (int u = pair; u < nunits && g.ok; u += npairs) {
         int m0, n0, kb0, kb1;
-        gemm_decode(p, BN, t, m0, n0, kb0, kb1);
+        gemm_decode(p, BN, u, m0, n0, kb0, kb1);
+        const int mc = m0 + int(rank) * GEMM_BM;  // this CTA's rows
+        const int nc = n0 + int(rank) * HB;       // this CTA's B columns
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, g, 1)) break;
-          const uint32_t fb = full_bar(stage);
-          mbar_expect_tx(fb, Cfg::STAGE_BYTES);
+          // both CTAs' copies count on the leader's barrier; the leader expects their sum
+          if (rank == 0) mbar_expect_tx(full_bar(stage), 2 * Cfg::STAGE_BYTES);
+          const uint32_t fb = mapa_shared(full_bar(stage), 0);
           const uint32_t a_dst = sA + stage * GEMM_A_BYTES;
           const uint32_t b_dst = sB + stage * Cfg::B_BYTES;
           if (AM == A_K) {
-            tma_load_2d(a_dst, &maps.a, fb, kb * GEMM_BK, m0);
+            tma_load_2d_pair(a_dst, &maps.a, fb, kb * GEMM_BK, mc);
           } else {
-            tma_load_2d(a_dst, &maps.a, fb, m0, kb * GEMM_BK);
-            tma_load_2d(a_dst + 8192, &maps.a, fb, m0 + 64, kb * GEMM_BK);
+            tma_load_2d_pair(a_dst, &maps.a, fb, mc, kb * GEMM_BK);
+            tma_load_2d_pair(a_dst + 8192, &maps.a, fb, mc + 64, kb * GEMM_BK);
           }
           if (BMD == B_K) {
-            tma_load_2d(b_dst, &maps.b[0], fb, kb * GEMM_BK, n0);
+            tma_load_2d_pair(b_dst, &maps.b[0], fb, kb * GEMM_BK, nc);
           } else if (BMD == B_MN) {
 #pragma unroll
-            for (int i = 0; i < BN / 64; ++i) tma_load_2d(b_dst + 8192 * i, &maps.b[0], fb, n0 + 64 * i, kb * GEMM_BK);
+            for (int i = 0; i < HB / 64; ++i)
+              tma_load_2d_pair(b_dst + 8192 * i, &maps.b[0], fb, nc + 64 * i, kb * GEMM_BK);
           } else if (BMD == B_SLABS) {
-            const int nsl = BN / p.slab_rows;
-            for (int s = 0; s < nsl; ++s) {
-              const int sg = n0 / p.slab_rows + s;
-              tma_load_2d(b_dst + s * p.slab_rows * 128, &maps.b[sg & 3], fb, kb * GEMM_BK, (sg >> 2) * p.slab_rows);
+            const int half = BN / p.slab_rows / 2;  // slabs staged by each CTA
+            for (int s = 0; s < half; ++s) {
+              const int sg = nc / p.slab_rows + s;
+              tma_load_2d_pair(b_dst + s * p.slab_rows * 128, &maps.b[sg & 3], fb, kb * GEMM_BK,
+                               (sg >> 2) * p.slab_rows);
             }
           } else {
             const int src = kb / p.b_kb_per_src;
             const int kr = (kb - src * p.b_kb_per_src) * GEMM_BK;
 #pragma unroll
-            for (int i = 0; i < BN / 64; ++i) tma_load_2d(b_dst + 8192 * i, &maps.b[src], fb, n0 + 64 * i, kr);
+            for (int i = 0; i < HB / 64; ++i)
+              tma_load_2d_pair(b_dst + 8192 * i, &maps.b[src], fb, nc + 64 * i, kr);
           }
           last_par[stage] = int(phase);
           if (++stage == STAGES) {
@@ -543,30 +601,32 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
           }
         }
       }
+      // Tail: every stage's last fill has been released by the MMA (the commits
+      // that arrive on this CTA's empty barriers have landed).
+      for (int s = 0; s < STAGES; ++s)
+        if (last_par[s] >= 0 && g.ok) mbar_wait(empty_bar(s), uint32_t(last_par[s]), g, 6);
       if (!g.ok) {
-        // Abort: let every copy this thread issued land before the CTA exits.
+        // Abort: let the copies in flight land (the leader's full barriers count
+        // both CTAs' bytes) and the MMA's releases arrive, with short bounded waits.
         for (int s = 0; s < STAGES; ++s)
-          if (last_par[s] >= 0) mbar_drain(full_bar(s), uint32_t(last_par[s]));
-      } else {
-        // Tail: wait for the MMA warp's release (tcgen05.commit) of every stage's
-        // last fill, so no asynchronous arrive targets this CTA's shared memory
-        // after it exits.
-        for (int s = 0; s < STAGES; ++s)
-          if (last_par[s] >= 0) mbar_wait(empty_bar(s), uint32_t(last_par[s]), g, 6);
+          if (last_par[s] >= 0) {
+            if (rank == 0) mbar_drain(full_bar(s), uint32_t(last_par[s]));
+            mbar_drain(empty_bar(s), uint32_t(last_par[s]));
+          }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (elect_one()) {
+    // ---------------- MMA issuer (leader CTA) ----------------
+    if (rank == 0 && elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool any = false;
-      for (int t = blockIdx.x; t < ntiles && g.ok; t += gridDim.x, ++it) {
+      for (int u = pair; u < nunits && g.ok; u += npairs, ++it) {
         int m0, n0, kb0, kb1;
-        gemm_decode(p, BN, t, m0, n0, kb0, kb1);
+        gemm_decode(p, BN, u, m0, n0, kb0, kb1);
         const int buf = it & 1;
-        if (!mbar_wait(acce_bar(buf), ((it >> 1) & 1) ^ 1, g, 2)) break;
+        if (!mbar_wait_cluster(acce_bar(buf), ((it >> 1) & 1) ^ 1, g, 2)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -580,44 +640,67 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
                                           : smem_desc(a_base + 2048 * k, 8192, 1024, SW_128B);
             const uint64_t bd = (BMD == B_K || BMD == B_SLABS) ? smem_desc(b_base + 32 * k, 16, 1024, SW_128B)
                                                                 : smem_desc(b_base + 2048 * k, 8192, 1024, SW_128B);
-            mma_ss(d, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+            mma_ss_pair(d, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           any = true;
-          mma_commit(empty_bar(stage));
+          mma_commit_pair(empty_bar(stage), 0x3);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!g.ok) break;
-        mma_commit(accf_bar(buf));
+        mma_commit_pair(accf_bar(buf), 0x3);
       }
       if (!g.ok && any) {
-        mma_commit(drain_bar);
+        mma_commit_pair(drain_bar, 0x1);
         mbar_drain(drain_bar, 0);
       }
     }
   } else {
-    // ---------------- Epilogue: warps 2 .. 2+EPI_WARPS-1 ----------------
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const int wg = (warp - 2) >> 2;  // epilogue group (QKVG: 0 or 1)
-    const int ti = (warp - 2 - 4 * wg) * 32 + lane;  // thread index within the group
-    const uint32_t stg = sA + STAGES * Cfg::STAGE_BYTES;
+    // ---------------- Epilogue: warps 2 .. 2+EPI_WARPS-1 (both CTAs) ----------------
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    const int wg = (warp - 2) >> 2;
+    const uint32_t stg = sStg + (warp - 2) * Cfg::WARP_STG;
+    const uint32_t acce_cl0 = mapa_shared(acce_bar(0), 0);
+    const uint32_t acce_cl1 = mapa_shared(acce_bar(1), 0);
+    // QKVG: the quarter's rotary-table tile (f1 then f2), loaded by the group-0 warp
+    const uint32_t tab = sIn + quarter * (Cfg::QKVG ? 2 * 32 * HD * 2 : 0);
+    uint32_t tab_par = 0;
+    // DGATE: this warp's input buffers and their barriers
+    const uint32_t inb = sIn + (warp - 2) * (Cfg::DGATE ? Cfg::IN_BUFS * 128 * HD : 0);
+    const uint32_t in_bar = aux_bar(Cfg::DGATE ? 2 * (warp - 2) : 0);
+    uint32_t hc = 0;
     int it = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+    for (int u = pair; u < nunits; u += npairs, ++it) {
       int m0, n0, kb0, kb1;
-      gemm_decode(p, BN, t, m0, n0, kb0, kb1);
+      gemm_decode(p, BN, u, m0, n0, kb0, kb1);
       const int buf = it & 1;
-      // Projection epilogue: the rotary-table rows of this thread's token are
-      // loaded before the accumulator wait, which hides their latency.
-      uint4 pre1[2][4], pre2[2][4];
-      if constexpr (Cfg::QKVG && HD > 64) {
-        const int t = (m0 + row) % p.T;
-        const __nv_bfloat16* f1row = p.f1 + size_t(t) * p.ldf;
-        const __nv_bfloat16* f2row = p.f2 + size_t(t) * p.ldf;
-        load_tab_chunk<HD>(f1row, f2row, 0, pre1[0], pre2[0]);
-        if (HD > 32) load_tab_chunk<HD>(f1row, f2row, 32, pre1[1], pre2[1]);
+      const int mq = m0 + int(rank) * GEMM_BM + quarter * 32;  // row of lane 0
+      if constexpr (Cfg::QKVG) {
+        // rotary rows of this tile: requested before the accumulator wait
+        const bool need_tab = ((n0 / HD + wg) & 3) < 2 || (BN / HD > 2);
+        const int tq = mq - (mq / p.T) * p.T;
+        if (need_tab && wg == 0 && lane == 0 && mbar_wait(aux_bar(4 + quarter), tab_par ^ 1, g, 9)) {
+          mbar_expect_tx(aux_bar(quarter), 2 * 32 * HD * 2);
+#pragma unroll
+          for (int bx = 0; bx < (HD + 63) / 64; ++bx) {
+            tma_load_2d(tab + bx * 4096, &maps.in[0], aux_bar(quarter), 64 * bx, tq);
+            tma_load_2d(tab + 32 * HD * 2 + bx * 4096, &maps.in[1], aux_bar(quarter), 64 * bx, tq);
+          }
+        }
+      }
+      if constexpr (Cfg::DGATE) {
+        // the tile's first heads: requested before the accumulator wait
+        if (lane == 0) {
+          const int b = mq / p.T, tq = mq - b * p.T;
+#pragma unroll
+          for (int i = 0; i < Cfg::IN_BUFS && i < BN / HD; ++i) {
+            const uint32_t hb = Cfg::IN_BUFS == 2 ? ((hc + i) & 1) : 0;
+            dgate_issue<BN, HD, Cfg::IN_BUFS>(maps, inb + hb * 2 * 32 * HD * 2, in_bar + 8 * hb, b, p.H, p.T, tq,
+                                              n0 / HD + i);
+          }
+        }
       }
       bool ok = mbar_wait(accf_bar(buf), (it >> 1) & 1, g, 4);
       ok = __all_sync(0xffffffffu, ok);
@@ -627,27 +710,34 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1) gemm_kernel(cons
       }
       tc_fence_after();
       const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + buf * BN;
-      const int m = m0 + row;
+      const uint32_t acce_cl = buf ? acce_cl1 : acce_cl0;
       if constexpr (Cfg::QKVG) {
-        epi_qkvg<BN, HD>(p, taddr, m, n0, wg, row, ti, stg, pre1, pre2);
-        tc_fence_before();
-        mbar_arrive(acce_bar(buf));
-        epi_qkvg_copy_out<BN, HD>(p, m0, n0, wg, ti, stg);
+        const bool need_tab = ((n0 / HD + wg) & 3) < 2 || (BN / HD > 2);
+        epi_qkvg<BN, HD>(maps, p, taddr, stg, tab, aux_bar(quarter), aux_bar(4 + quarter), tab_par, lane, wg, mq, n0,
+                         acce_cl, g);
+        if (need_tab) tab_par ^= 1;
+      } else if constexpr (Cfg::DGATE) {
+        epi_dgate<BN, HD, Cfg::IN_BUFS>(maps, p, taddr, stg, inb, in_bar, hc, lane, mq, n0, acce_cl, g);
+      } else if constexpr (EPI == EPI_BF16) {
+        epi_bf16<BN>(maps, taddr, stg, lane, mq, n0, acce_cl);
       } else {
-        if constexpr (EPI == EPI_DGATE)
-          epi_dgate<BN, HD>(p, taddr, m, n0);
-        else
-          epi_store<BN>(p, EPI, taddr, m, n0);
-        tc_fence_before();
-        mbar_arrive(acce_bar(buf));
+        epi_f32<BN, EPI == EPI_RED_F32>(maps, taddr, stg, lane, mq, n0, acce_cl);
       }
+      if (!g.ok) break;
     }
+    // every TMA store / reduce of this warp has completed before the CTA exits
+    if (lane == 0) bulk_wait0();
+    __syncwarp();
   }
 
   __syncthreads();
+  // No CTA of the pair leaves (or frees TMEM) while the other may still use its
+  // shared memory or barriers.
+  tc_fence_before();
+  cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
   }
 }
 

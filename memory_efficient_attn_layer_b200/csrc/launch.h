@@ -34,6 +34,17 @@ struct GemmLaunch {
   int b_rows;           // B_SLABS / B_MN_KSPLIT4: rows of each B tensor
   int slab_rows;        // B_SLABS: head dim
   int k_splits;         // > 1 only with EPI_RED_F32
+  // Epilogue tensors (run_gemm builds their TMA maps):
+  //   EPI_BF16 / EPI_F32 / EPI_RED_F32: out[0] = D [M, N], row pitch ldo elements
+  //   EPI_QKVG : out[0..3] = q, k, v, sigmoid(g) [B*H*T, hd]; in[0..1] = rotary
+  //              tables [in_rows, hd] with row pitch ldin
+  //   EPI_DGATE: out[0] = dO [B*H*T, hd]; out[1] = dg_pre [M, H*hd] with row
+  //              pitch ldo; in[0..1] = O, sigmoid(g) [B*H*T, hd]
+  void* out[4];
+  long long ldo;
+  const void* in[2];
+  long long ldin;
+  int in_rows;
 };
 int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st);
 int auto_splits(int m_tiles, int n_tiles, int kb_total, int waves);
