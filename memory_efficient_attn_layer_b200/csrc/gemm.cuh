@@ -143,14 +143,6 @@ __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
                : "memory");
   return v;
 }
-__device__ __forceinline__ void tmem_wait_ld_tied2x32(uint32_t (&a)[32], uint32_t (&b)[32]) {
-  tmem_wait_ld_tied(a);
-  asm volatile("" : "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]),
-               "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15]),
-               "+r"(b[16]), "+r"(b[17]), "+r"(b[18]), "+r"(b[19]), "+r"(b[20]), "+r"(b[21]), "+r"(b[22]),
-               "+r"(b[23]), "+r"(b[24]), "+r"(b[25]), "+r"(b[26]), "+r"(b[27]), "+r"(b[28]), "+r"(b[29]),
-               "+r"(b[30]), "+r"(b[31])::"memory");
-}
 
 // Hand this warp's share of an accumulator buffer back to the pair's MMA issuer.
 __device__ __forceinline__ void release_acc(uint32_t acce_cl, int lane) {

@@ -322,6 +322,19 @@ __device__ __forceinline__ void tmem_wait_ld_tied(uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_wait_ld_tied2(uint32_t (&a)[16], uint32_t (&b)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(a[0]),"+r"(a[1]),"+r"(a[2]),"+r"(a[3]),"+r"(a[4]),"+r"(a[5]),"+r"(a[6]),"+r"(a[7]),"+r"(a[8]),"+r"(a[9]),"+r"(a[10]),"+r"(a[11]),"+r"(a[12]),"+r"(a[13]),"+r"(a[14]),"+r"(a[15]), "+r"(b[0]),"+r"(b[1]),"+r"(b[2]),"+r"(b[3]),"+r"(b[4]),"+r"(b[5]),"+r"(b[6]),"+r"(b[7]),"+r"(b[8]),"+r"(b[9]),"+r"(b[10]),"+r"(b[11]),"+r"(b[12]),"+r"(b[13]),"+r"(b[14]),"+r"(b[15]) :: "memory");
 }
+// Ties registers filled by an earlier tcgen05.ld to the point of this call (after
+// a tcgen05.wait::ld), so that no use is scheduled above the wait.
+__device__ __forceinline__ void reg_tie(uint32_t (&b)[32]) {
+  asm volatile("" : "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]),
+               "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15]),
+               "+r"(b[16]), "+r"(b[17]), "+r"(b[18]), "+r"(b[19]), "+r"(b[20]), "+r"(b[21]), "+r"(b[22]),
+               "+r"(b[23]), "+r"(b[24]), "+r"(b[25]), "+r"(b[26]), "+r"(b[27]), "+r"(b[28]), "+r"(b[29]),
+               "+r"(b[30]), "+r"(b[31])::"memory");
+}
+__device__ __forceinline__ void tmem_wait_ld_tied2x32(uint32_t (&a)[32], uint32_t (&b)[32]) {
+  tmem_wait_ld_tied(a);
+  reg_tie(b);
+}
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),"r"(r[1]),"r"(r[2]),"r"(r[3]),"r"(r[4]),"r"(r[5]),"r"(r[6]),"r"(r[7]) : "memory");
 }
