@@ -23,6 +23,7 @@ as one coalesced fp32 bucket (memory_efficient_attn_layer_b200.dp).
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -239,7 +240,7 @@ def run_gpu(args, cfg, rank, world, device):
     import torch.distributed as dist
 
     from memory_efficient_attn_layer_b200 import FusedAttentionFunction, _lib
-    from memory_efficient_attn_layer_b200.dp import allreduce_grads
+    from memory_efficient_attn_layer_b200.dp import allreduce_grads, overlap_grad_allreduce
 
     B, T, C, H, N = (cfg[k] for k in ("B", "T", "C", "H", "N"))
     tokens_rank = B * T
@@ -266,10 +267,19 @@ def run_gpu(args, cfg, rank, world, device):
             return eager_block(inp, ws, yarn, H, N)
         return FusedAttentionFunction.apply(inp, *ws, yarn.factor1, yarn.factor2, H, N, 1e-6)
 
+    # Our block exchanges its weight gradients inside its own backward (the
+    # all-reduce of each part starts as soon as the library marks it final);
+    # the comparators exchange theirs after the backward.
+    overlap = world > 1 and not eager
+
+    def exchange_ctx():
+        return overlap_grad_allreduce() if overlap else contextlib.nullcontext()
+
     def step(inp, grad):
-        y = fwd(inp)
-        y.backward(grad)
-        if world > 1:
+        with exchange_ctx():
+            y = fwd(inp)
+            y.backward(grad)
+        if world > 1 and not overlap:
             allreduce_grads(ws)
         for w in ws:
             w.grad = None
@@ -350,11 +360,12 @@ def run_gpu(args, cfg, rank, world, device):
         if i + 1 < n:
             e2e_copy(i + 1)
         comp.wait_event(copied[b])
-        y = fwd(xbuf[b])
-        loss = (y * dybuf[b]).sum(dtype=torch.float32)
-        loss.backward()
+        with exchange_ctx():
+            y = fwd(xbuf[b])
+            loss = (y * dybuf[b]).sum(dtype=torch.float32)
+            loss.backward()
         consumed[b].record(comp)
-        if world > 1:
+        if world > 1 and not overlap:
             allreduce_grads(ws)
         for w in ws:
             w.grad = None
@@ -392,6 +403,8 @@ def run_gpu(args, cfg, rank, world, device):
         "data": "synthetic: x, dy ~ N(0,1); weights ~ U(+-0.5/sqrt(C)) replicated; rotary tables for N, T",
         "config": {"workload": cfg["name"], "B_per_gpu": B, "global_batch": B * world, "T": T, "C": C, "H": H,
                    "N": N, "parallelism": f"dp{world}" if world > 1 else "single",
+                   "grad_exchange": ("nccl all-reduce overlapped with the backward" if overlap else
+                                     "nccl all-reduce after the backward") if world > 1 else None,
                    "l2": f"inputs larger than L2 (x is {2 * B * T * C / 1e6:.0f} MB per GPU), no flush"},
     }
     if eager:

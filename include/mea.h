@@ -80,6 +80,23 @@ int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, c
                        float* dfactor1, float* dfactor2, float* dweights_f32, void* workspace,
                        size_t workspace_bytes, int* status, void* stream);
 
+/* mea_block_backward for data-parallel training: no counterpart in the
+ * reference, whose weight gradients are exchanged after the backward.  Same
+ * arguments, plus two CUDA events (cudaEvent_t, may be NULL) recorded on
+ * `stream` as soon as the fp32 gradients in dweights_f32 are final: ev_dwo_ready
+ * after the o_proj gradient [C, H*N] (early in the backward, before the
+ * attention backward), ev_dw_ready after the q/k/v/g gradients [4*H*N, C]
+ * (before the input-gradient GEMM).  A caller can start its all-reduce of each
+ * part on another stream at those events, overlapping the rest of the
+ * backward.  dwq .. dwo may be NULL (no bf16 copy written); dweights_f32 must
+ * then be non-NULL. */
+int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                          const void* wg, const void* wo, const void* factor1, const void* factor2,
+                          const float* lse2, const void* dy, void* dx, void* dwq, void* dwk, void* dwv, void* dwg,
+                          void* dwo, float* dfactor1, float* dfactor2, float* dweights_f32, void* workspace,
+                          size_t workspace_bytes, int* status, void* stream, void* ev_dwo_ready,
+                          void* ev_dw_ready);
+
 /* ---------------------------------------------------------------- kernel level */
 
 /* rms_norm_kernel / rms_norm_kernel_recompute (fast_triton_attn.py:12-34, :181-210):

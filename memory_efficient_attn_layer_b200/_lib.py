@@ -46,6 +46,8 @@ SIGNATURES = {
     "mea_backward_workspace_size": (_S, [_D]),
     "mea_block_backward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                 _P, _S, _P, _P]),
+    "mea_block_backward_ex": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                   _P, _P, _S, _P, _P, _P, _P]),
     "mea_rmsnorm_forward": (_I, [_I, _I, _F, _P, _P, _P, _P]),
     "mea_qkvg_forward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "mea_attention_forward": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),

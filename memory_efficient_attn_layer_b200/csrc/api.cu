@@ -299,6 +299,13 @@ struct StageScope {
     MEA_TRY(expr);                 \
   } while (0)
 
+static int record_event(void* ev, cudaStream_t st) {
+  if (!ev) return MEA_OK;
+  if (cudaEventRecord(static_cast<cudaEvent_t>(ev), st) != cudaSuccess)
+    return set_error(MEA_ERR_CUDA, "cudaEventRecord failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return MEA_OK;
+}
+
 static int memset_async(void* p, size_t bytes, cudaStream_t st) {
   if (!p || !bytes) return MEA_OK;
   if (cudaMemsetAsync(p, 0, bytes, st) != cudaSuccess) return set_error(MEA_ERR_CUDA, "cudaMemsetAsync failed");
@@ -398,7 +405,21 @@ int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, c
                        const void* dy, void* dx, void* dwq, void* dwk, void* dwv, void* dwg, void* dwo,
                        float* dfactor1, float* dfactor2, float* dweights_f32, void* workspace,
                        size_t workspace_bytes, int* status, void* stream) {
+  return mea_block_backward_ex(d, x, wq, wk, wv, wg, wo, factor1, factor2, lse2, dy, dx, dwq, dwk, dwv, dwg, dwo,
+                               dfactor1, dfactor2, dweights_f32, workspace, workspace_bytes, status, stream, nullptr,
+                               nullptr);
+}
+
+int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                          const void* wg, const void* wo, const void* factor1, const void* factor2,
+                          const float* lse2, const void* dy, void* dx, void* dwq, void* dwk, void* dwv, void* dwg,
+                          void* dwo, float* dfactor1, float* dfactor2, float* dweights_f32, void* workspace,
+                          size_t workspace_bytes, int* status, void* stream, void* ev_dwo_ready,
+                          void* ev_dw_ready) {
   MEA_TRY(validate(d));
+  const bool want_bf16 = dwq || dwk || dwv || dwg || dwo;
+  if (!want_bf16 && !dweights_f32)
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "backward: no weight-gradient output (bf16 or fp32) given");
   const BwdWs w = bwd_layout(*d);
   if (!workspace || workspace_bytes < w.total)
     return set_error(MEA_ERR_WORKSPACE, "backward workspace needs %zu bytes, got %zu", w.total, workspace_bytes);
@@ -436,6 +457,7 @@ int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, c
   }
   // o_proj backward: dWo = dY^T gated; dGated = dY Wo with the gate backward fused.
   MEA_STAGE(ST_BWD_DWO, weight_grad(C, HN, M, dy, C, ws + w.gated, HN, dwo32, status, st));
+  MEA_TRY(record_event(ev_dwo_ready, st));
   MEA_STAGE(ST_BWD_DGATE, gate_bwd(*d, dy, wo, ws + w.o, ws + w.gs, ws + w.dO, dacc + size_t(3) * HN * 2, ld_dacc, delta, status,
                    st));
   // Attention backward: dq (fp32 accumulate), dk, dv -> v slot of dacc.
@@ -446,6 +468,7 @@ int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, c
                                d->N, dacc, ld_dacc, dfactor1, dfactor2, st));
   // Projection weight gradients: [4HN, C] = dacc^T xn.
   MEA_STAGE(ST_BWD_DW, weight_grad(4 * HN, C, M, dacc, ld_dacc, ws + w.xn, C, dw32, status, st));
+  MEA_TRY(record_event(ev_dw_ready, st));
   // dx_normed = dacc [Wq; Wk; Wv; Wg]
   {
     GemmLaunch L{};
@@ -474,11 +497,9 @@ int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, c
   MEA_STAGE(ST_BWD_NORM_BWD, run_rmsnorm_bwd(M, C, ws + w.dxn, x, rx, dx, st));
   const size_t wsz = size_t(HN) * C;
   StageScope cast_scope(ST_BWD_CAST, st);
-  MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32, dwq, st));
-  MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32 + wsz, dwk, st));
-  MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32 + 2 * wsz, dwv, st));
-  MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32 + 3 * wsz, dwg, st));
-  MEA_TRY(run_cast_f32_bf16((long long)wsz, dwo32, dwo, st));
+  void* dst[5] = {dwq, dwk, dwv, dwg, dwo};
+  for (int i = 0; i < 5; ++i)
+    if (dst[i]) MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32 + i * wsz, dst[i], st));
   return MEA_OK;
 }
 

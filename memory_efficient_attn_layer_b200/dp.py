@@ -2,14 +2,29 @@
 
 The block's batch shards across ranks by sequence (one process per GPU); the
 only exchange is the all-reduce of the five weight gradients (Wq, Wk, Wv, Wg,
-Wo) after each backward.  They are exchanged as one coalesced fp32 bucket (one
-collective instead of five, and no bf16 rounding inside the sum), then written
-back to each ``.grad`` in its own dtype.  The rotary tables are buffers, not
+Wo).  They are exchanged in fp32 (no bf16 rounding inside the sum) and written
+back to each gradient in its own dtype.  The rotary tables are buffers, not
 parameters, so their gradients are not exchanged.
+
+Two ways to run it:
+
+* ``allreduce_grads(params)`` after ``loss.backward()``: one coalesced fp32
+  bucket, one collective, nothing overlapped.
+* ``with overlap_grad_allreduce(group): y = block(x); ...; loss.backward()``:
+  every ``FusedAttentionFunction`` forward run inside the context tags its
+  node, and that node's backward exchanges its own weight gradients while the
+  rest of its backward still runs.  The library records an event as soon as
+  the fp32 o_proj gradient is final (before the attention backward) and
+  another when the q/k/v/g gradients are (before the input-gradient GEMM);
+  the all-reduce of each part starts at its event on a side stream, and the
+  caller's stream waits for the exchange only where the backward returns.  The
+  gradients handed back to autograd are already the group mean (or sum), so
+  ``allreduce_grads`` must not be called for those weights as well.
 """
 from __future__ import annotations
 
-from typing import Iterable, Optional
+import contextlib
+from typing import Callable, Iterable, Optional
 
 import torch
 import torch.distributed as dist
@@ -36,3 +51,68 @@ def allreduce_grads(params: Iterable[torch.Tensor], group: Optional[dist.Process
         n = g.numel()
         g.copy_(bucket[off:off + n].view_as(g))
         off += n
+
+
+def reduce_weight_grads(buf: torch.Tensor, n_qkvg: int, group: Optional[dist.ProcessGroup] = None,
+                        average: bool = True, before_qkvg: Optional[Callable[[], None]] = None) -> None:
+    """All-reduce the block's fp32 weight-gradient buffer in the order the
+    backward finishes it: ``buf[n_qkvg:]`` (Wo) first, then ``buf[:n_qkvg]``
+    (Wq, Wk, Wv, Wg), with ``before_qkvg`` run between the two (the overlapped
+    path makes the side stream wait for the second readiness event there).
+    Every rank issues the same two collectives in the same order."""
+    dist.all_reduce(buf[n_qkvg:], group=group)
+    if before_qkvg is not None:
+        before_qkvg()
+    dist.all_reduce(buf[:n_qkvg], group=group)
+    if average and dist.get_world_size(group) > 1:
+        buf.div_(dist.get_world_size(group))
+
+
+_SIDE_STREAMS = {}
+
+
+def side_stream(device: torch.device) -> "torch.cuda.Stream":
+    """The per-device stream the overlapped exchange runs on.  High priority:
+    the collective's kernels are scheduled ahead of the block's own grids as
+    SMs free up."""
+    s = _SIDE_STREAMS.get(device.index)
+    if s is None:
+        s = torch.cuda.Stream(device=device, priority=-1)
+        _SIDE_STREAMS[device.index] = s
+    return s
+
+
+class GradExchange:
+    """Settings of one overlapped exchange context."""
+
+    def __init__(self, group: Optional[dist.ProcessGroup] = None, average: bool = True):
+        self.group = group
+        self.average = average
+
+
+_ACTIVE: Optional[GradExchange] = None
+
+
+def active_exchange() -> Optional[GradExchange]:
+    """The exchange a forward run now should tag its node with (None outside
+    an ``overlap_grad_allreduce`` context or with a group of one rank)."""
+    ex = _ACTIVE
+    if ex is None or not dist.is_available() or not dist.is_initialized():
+        return None
+    if dist.get_world_size(ex.group) <= 1:
+        return None
+    return ex
+
+
+@contextlib.contextmanager
+def overlap_grad_allreduce(group: Optional[dist.ProcessGroup] = None, average: bool = True):
+    """Forwards of the block run inside this context exchange their weight
+    gradients across ``group`` during their own backward (see the module
+    docstring).  The backward itself may run after the context has closed."""
+    global _ACTIVE
+    prev = _ACTIVE
+    _ACTIVE = GradExchange(group, average)
+    try:
+        yield _ACTIVE
+    finally:
+        _ACTIVE = prev

@@ -16,6 +16,7 @@ import os
 import torch
 
 from . import _lib
+from . import dp as _dp
 
 _CHECK_STATUS = os.environ.get("MEA_CHECK_STATUS", "0") == "1"
 
@@ -73,6 +74,7 @@ class FusedAttentionFunction(torch.autograd.Function):
             _lib.read_status(x.device)
         ctx.save_for_backward(x, *weights, factor1, factor2, lse)
         ctx.H, ctx.N, ctx.eps = int(H), int(N), float(eps)
+        ctx.exchange = _dp.active_exchange()
         return y
 
     @staticmethod
@@ -90,16 +92,47 @@ class FusedAttentionFunction(torch.autograd.Function):
         ws_bytes = L.mea_backward_workspace_size(ctypes.byref(dims))
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         status = _lib.status_buffer(x.device)
-        _lib.check(L.mea_block_backward(
-            ctypes.byref(dims), _lib.ptr(x), _lib.ptr(wq), _lib.ptr(wk), _lib.ptr(wv), _lib.ptr(wg), _lib.ptr(wo),
-            _lib.ptr(factor1), _lib.ptr(factor2), _lib.ptr(lse), _lib.ptr(dy), _lib.ptr(dx),
-            *[_lib.ptr(d) for d in dws], _lib.ptr(df1), _lib.ptr(df2), None, _lib.ptr(ws), ws_bytes,
-            _lib.ptr(status), _lib.stream_ptr(x.device)))
+        args = (ctypes.byref(dims), _lib.ptr(x), _lib.ptr(wq), _lib.ptr(wk), _lib.ptr(wv), _lib.ptr(wg),
+                _lib.ptr(wo), _lib.ptr(factor1), _lib.ptr(factor2), _lib.ptr(lse), _lib.ptr(dy), _lib.ptr(dx))
+        ex = ctx.exchange
+        if ex is None:
+            _lib.check(L.mea_block_backward(
+                *args, *[_lib.ptr(d) for d in dws], _lib.ptr(df1), _lib.ptr(df2), None, _lib.ptr(ws), ws_bytes,
+                _lib.ptr(status), _lib.stream_ptr(x.device)))
+        else:
+            _exchange_backward(L, args, dws, df1, df2, ws, ws_bytes, status, x, ex)
         if _CHECK_STATUS:
             _lib.read_status(x.device)
         gf1 = df1.to(factor1.dtype) if want_df else None
         gf2 = df2.to(factor2.dtype) if want_df else None
         return (dx, *dws, gf1, gf2, None, None, None)
+
+
+def _exchange_backward(L, args, dws, df1, df2, ws, ws_bytes, status, x, ex):
+    """Backward whose fp32 weight gradients are all-reduced across the exchange's
+    group on a side stream, each part from the moment the library marks it
+    final; the bf16 gradients are written from the reduced buffer on that
+    stream, and the caller's stream waits for it before anything after the
+    backward runs."""
+    main = torch.cuda.current_stream(x.device)
+    side = _dp.side_stream(x.device)
+    n_w = dws[0].numel()
+    dw32 = torch.empty(5 * n_w, dtype=torch.float32, device=x.device)
+    ev_dwo, ev_dw = torch.cuda.Event(), torch.cuda.Event()
+    ev_dwo.record(main)  # creates the events; the library records them again at the right points
+    ev_dw.record(main)
+    _lib.check(L.mea_block_backward_ex(
+        *args, None, None, None, None, None, _lib.ptr(df1), _lib.ptr(df2), _lib.ptr(dw32), _lib.ptr(ws), ws_bytes,
+        _lib.ptr(status), _lib.stream_ptr(x.device), ev_dwo._as_parameter_, ev_dw._as_parameter_))
+    dw32.record_stream(side)
+    for d in dws:
+        d.record_stream(side)
+    with torch.cuda.stream(side):
+        side.wait_event(ev_dwo)
+        _dp.reduce_weight_grads(dw32, 4 * n_w, ex.group, ex.average, before_qkvg=lambda: side.wait_event(ev_dw))
+        for i, d in enumerate(dws):
+            d.copy_(dw32[i * n_w:(i + 1) * n_w].view_as(d))
+    main.wait_stream(side)
 
 
 def fused_attn(x, q_proj, k_proj, v_proj, g_proj, o_proj, yarn_module, H, N, eps=1e-6):

@@ -9,7 +9,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from memory_efficient_attn_layer_b200.dp import allreduce_grads
+from memory_efficient_attn_layer_b200.dp import active_exchange, allreduce_grads, overlap_grad_allreduce, reduce_weight_grads
 
 
 def _free_port():
@@ -64,3 +64,50 @@ def test_allreduce_grads_two_ranks(average):
         for r in range(world):
             assert torch.equal(results[r][i], want), (i, r)
     assert results[0][5] is None and results[1][5] is None
+
+
+def _reduce_worker(rank, world, port, average, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        buf = torch.randn(5 * 12, generator=torch.Generator().manual_seed(7 + rank))
+        marks = []
+        # the second collective may only start after the callback (the overlapped
+        # path's wait on the q/k/v/g readiness event)
+        reduce_weight_grads(buf, 4 * 12, average=average, before_qkvg=lambda: marks.append("qkvg"))
+        with overlap_grad_allreduce(average=average) as ex:
+            tagged = active_exchange() is ex
+        q.put((rank, buf, marks, tagged))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("average", [True, False])
+def test_reduce_weight_grads_two_ranks(average):
+    """The overlapped exchange's collectives: o_proj part, callback, q/k/v/g part,
+    sum or mean over the group; forwards inside the context get tagged."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_reduce_worker, args=(r, world, port, average, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {r: rest for r, *rest in (q.get(timeout=120) for _ in range(world))}
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = sum(torch.randn(60, generator=torch.Generator().manual_seed(7 + r)) for r in range(world))
+    if average:
+        want = want / world
+    for r in range(world):
+        buf, marks, tagged = results[r]
+        assert torch.allclose(buf, want, rtol=0, atol=1e-6)
+        assert marks == ["qkvg"] and tagged
+
+
+def test_no_exchange_outside_context_or_without_group():
+    assert active_exchange() is None
+    with overlap_grad_allreduce():
+        assert active_exchange() is None  # no process group: nothing to exchange

@@ -1,6 +1,7 @@
 """GPU, 2 ranks: the data-parallel path end to end.  Each rank runs the block
-on its half of the batch and the five weight gradients are exchanged with
-allreduce_grads over NCCL (sum); they must equal one GPU's full-batch weight
+on its half of the batch and the five weight gradients are exchanged over NCCL
+(sum), either with allreduce_grads after the backward or overlapped with the
+backward (overlap_grad_allreduce); they must equal one GPU's full-batch weight
 gradients (cosine > 0.9999; bf16 gradients summed in fp32).  Skipped with fewer
 than two GPUs."""
 import os
@@ -26,7 +27,9 @@ def _inputs():
     return make_inputs(SHAPE["B"], SHAPE["T"], SHAPE["C"], SHAPE["H"], SHAPE["N"], seed=41)
 
 
-def _weight_grads(inp, dev, lo, hi):
+def _weight_grads(inp, dev, lo, hi, exchange=None):
+    import contextlib
+
     from memory_efficient_attn_layer_b200 import FusedAttentionFunction
 
     leaves = [inp[k].to(device=dev, dtype=torch.bfloat16).contiguous() for k in ("wq", "wk", "wv", "wg", "wo")]
@@ -35,17 +38,18 @@ def _weight_grads(inp, dev, lo, hi):
     x = inp["x"][lo:hi].to(device=dev, dtype=torch.bfloat16).contiguous()
     f1 = inp["f1"].to(device=dev, dtype=torch.bfloat16).contiguous()
     f2 = inp["f2"].to(device=dev, dtype=torch.bfloat16).contiguous()
-    y = FusedAttentionFunction.apply(x, *leaves, f1, f2, SHAPE["H"], SHAPE["N"], 1e-6)
-    y.backward(inp["dy"][lo:hi].to(device=dev, dtype=torch.bfloat16))
+    with exchange if exchange is not None else contextlib.nullcontext():
+        y = FusedAttentionFunction.apply(x, *leaves, f1, f2, SHAPE["H"], SHAPE["N"], 1e-6)
+        y.backward(inp["dy"][lo:hi].to(device=dev, dtype=torch.bfloat16))
     return leaves
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, overlap, q):
     import datetime
 
     import torch.distributed as dist
 
-    from memory_efficient_attn_layer_b200.dp import allreduce_grads
+    from memory_efficient_attn_layer_b200.dp import allreduce_grads, overlap_grad_allreduce
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -56,22 +60,26 @@ def _rank(rank, world, port, q):
     try:
         inp = _inputs()
         per = SHAPE["B"] // world
-        leaves = _weight_grads(inp, dev, rank * per, (rank + 1) * per)
-        allreduce_grads(leaves, average=False)
+        if overlap:
+            leaves = _weight_grads(inp, dev, rank * per, (rank + 1) * per, overlap_grad_allreduce(average=False))
+        else:
+            leaves = _weight_grads(inp, dev, rank * per, (rank + 1) * per)
+            allreduce_grads(leaves, average=False)
         torch.cuda.synchronize(dev)
         q.put((rank, [w.grad.float().cpu() for w in leaves]))
     finally:
         dist.destroy_process_group()
 
 
-def test_dp_two_ranks_match_full_batch():
+@pytest.mark.parametrize("overlap", [False, True])
+def test_dp_two_ranks_match_full_batch(overlap):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, overlap, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=300) for _ in range(world))
