@@ -81,13 +81,17 @@ template <int BN, int EPI, int HD>
 struct GemmCfg {
   static constexpr bool QKVG = EPI == EPI_QKVG;
   static constexpr bool DGATE = EPI == EPI_DGATE;
-  static constexpr int EPI_WARPS = QKVG ? 8 : 4;
+  // EPI_QKVG: QK_GROUPS groups of four warps (one per TMEM lane quarter), group
+  // g taking the slabs s with s % QK_GROUPS == g: one slab per warp and tile for
+  // N <= 64 (16 warps), one of the two for N = 128 (8 warps).
+  static constexpr int QK_GROUPS = QKVG ? (HD >= 128 ? 2 : 4) : 1;
+  static constexpr int EPI_WARPS = 4 * QK_GROUPS;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr uint32_t B_BYTES = (BN / 2) * GEMM_BK * 2;
   static constexpr uint32_t STAGE_BYTES = GEMM_A_BYTES + B_BYTES;
   // DGATE: O / sigmoid(g) input buffers per warp (double-buffered below N = 128)
   static constexpr int IN_BUFS = DGATE ? (HD >= 128 ? 1 : 2) : 0;
-  static constexpr uint32_t WARP_STG = QKVG ? 32u * BN
+  static constexpr uint32_t WARP_STG = QKVG ? 64u * BN / QK_GROUPS
                                        : EPI == EPI_BF16 ? 64u * BN
                                        : DGATE ? 128u * HD
                                                : 32u * (BN < 128 ? BN : 128) * 4;
@@ -326,14 +330,15 @@ __device__ __forceinline__ void vg_slab(uint32_t tcol, uint32_t slab, int lane, 
   }
 }
 
-// Projection epilogue of one tile for this warp: its group's slabs (s % 2 ==
+// Projection epilogue of one tile for this warp: its group's slabs (s % G ==
 // wg) of its 32 rows, staged per slab and written by TMA to the slab's
 // [B,H,T,N] output.  q/k slabs wait for the quarter's rotary-table tile.
 template <int BN, int HD>
 __device__ __forceinline__ void epi_qkvg(const GemmMaps& maps, const GemmParams& p, uint32_t taddr, uint32_t stg,
                                          uint32_t tab, uint32_t tab_full, uint32_t tab_empty, uint32_t tab_par,
                                          int lane, int wg, int mq, int n0, uint32_t acce_cl, Guard& g) {
-  constexpr int NJ = BN / HD / 2;
+  constexpr int G = HD >= 128 ? 2 : 4;  // warp groups splitting the slabs (GemmCfg::QK_GROUPS)
+  constexpr int NJ = BN / HD / G;
   constexpr uint32_t SLAB_BYTES = 32 * HD * 2;
   const int b = mq / p.T;
   const int tq = mq - b * p.T;  // token of lane 0
@@ -344,7 +349,7 @@ __device__ __forceinline__ void epi_qkvg(const GemmMaps& maps, const GemmParams&
   bool any_qk = false;
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
-    const int s = wg + 2 * j;
+    const int s = wg + G * j;
     const int sg = n0 / HD + s;
     const int typ = sg & 3;
     if (typ < 2) {
@@ -369,7 +374,7 @@ __device__ __forceinline__ void epi_qkvg(const GemmMaps& maps, const GemmParams&
   if (lane == 0) {
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
-      const int sg = n0 / HD + wg + 2 * j;
+      const int sg = n0 / HD + wg + G * j;
       const int row = (b * p.H + (sg >> 2)) * p.T + tq;
 #pragma unroll
       for (int bx = 0; bx < (HD + 63) / 64; ++bx)
@@ -671,7 +676,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
       const int mq = m0 + int(rank) * GEMM_BM + quarter * 32;  // row of lane 0
       if constexpr (Cfg::QKVG) {
         // rotary rows of this tile: requested before the accumulator wait
-        const bool need_tab = ((n0 / HD + wg) & 3) < 2 || (BN / HD > 2);
+        const bool need_tab = ((n0 / HD) & 3) < 2 || (BN / HD > 2);  // the tile has q/k slabs
         const int tq = mq - (mq / p.T) * p.T;
         if (need_tab && wg == 0 && lane == 0 && mbar_wait(aux_bar(4 + quarter), tab_par ^ 1, g, 9)) {
           mbar_expect_tx(aux_bar(quarter), 2 * 32 * HD * 2);
@@ -704,7 +709,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
       const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + buf * BN;
       const uint32_t acce_cl = buf ? acce_cl1 : acce_cl0;
       if constexpr (Cfg::QKVG) {
-        const bool need_tab = ((n0 / HD + wg) & 3) < 2 || (BN / HD > 2);
+        const bool need_tab = ((n0 / HD) & 3) < 2 || (BN / HD > 2);  // the tile has q/k slabs
         epi_qkvg<BN, HD>(maps, p, taddr, stg, tab, aux_bar(quarter), aux_bar(4 + quarter), tab_par, lane, wg, mq, n0,
                          acce_cl, g);
         if (need_tab) tab_par ^= 1;

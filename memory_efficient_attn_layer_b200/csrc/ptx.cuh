@@ -228,8 +228,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   return r;
 }
 // Arrive on an mbarrier of any CTA of the cluster (address from mapa_shared).
+// Default (CTA-scope release) semantics: used to hand TMEM back to the pair's
+// MMA issuer, which the tcgen05 fences around the arrive and the wait order;
+// no shared-memory data is published through it.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cl_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
   uint32_t done;
