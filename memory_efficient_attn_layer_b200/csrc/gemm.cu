@@ -186,13 +186,27 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
   return dispatch(bn, L.amode, L.bmode, L.epi, maps, p, st);
 }
 
-// Split count for a long-K GEMM with few output tiles: about `waves` work
-// units per SM pair, at least 8 k-blocks per unit.
+// Split count for a long-K GEMM with few output tiles.  Each CTA pair runs
+// ceil(splits * tiles / pairs) work units of kb_total / splits k-blocks; a unit
+// also costs about six k-blocks' time of its own (pipeline fill and its fp32
+// reduce-add epilogue, overlapped only with a following unit).  The split
+// count minimising that makespan wins; ties go to fewer splits (less
+// reduce-add traffic).  `waves` caps the units per pair.
 int auto_splits(int m_tiles, int n_tiles, int kb_total, int waves) {
   const int units = ((m_tiles + 1) / 2) * n_tiles;
-  int s = ((num_sms() / 2) * waves + units - 1) / units;
-  if (s > kb_total / 8) s = kb_total / 8;
-  return s < 1 ? 1 : s;
+  const int pairs = num_sms() / 2;
+  int best_s = 1;
+  double best = 1e30;
+  for (int sp = 1; sp <= kb_total / 8; ++sp) {
+    const int per_pair = (sp * units + pairs - 1) / pairs;
+    if (per_pair > waves) break;
+    const double cost = per_pair * (double(kb_total) / sp + 6.0);
+    if (cost < best - 1e-6) {
+      best = cost;
+      best_s = sp;
+    }
+  }
+  return best_s;
 }
 
 }  // namespace mea

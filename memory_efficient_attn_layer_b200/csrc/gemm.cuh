@@ -85,19 +85,23 @@ struct GemmCfg {
   // g taking the slabs s with s % QK_GROUPS == g: one slab per warp and tile for
   // N <= 64 (16 warps), one of the two for N = 128 (8 warps).
   static constexpr int QK_GROUPS = QKVG ? (HD >= 128 ? 2 : 4) : 1;
-  static constexpr int EPI_WARPS = 4 * QK_GROUPS;
+  // EPI_DGATE: DG_GROUPS groups of four warps, group g taking the heads s with
+  // s % DG_GROUPS == g; each warp streams its heads through two in-place buffers.
+  static constexpr int DG_GROUPS = DGATE ? (HD >= 128 ? 1 : 2) : 1;
+  static constexpr int EPI_WARPS = 4 * QK_GROUPS * DG_GROUPS;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr uint32_t B_BYTES = (BN / 2) * GEMM_BK * 2;
   static constexpr uint32_t STAGE_BYTES = GEMM_A_BYTES + B_BYTES;
-  // DGATE: O / sigmoid(g) input buffers per warp (double-buffered below N = 128)
-  static constexpr int IN_BUFS = DGATE ? (HD >= 128 ? 1 : 2) : 0;
   static constexpr uint32_t WARP_STG = QKVG ? 64u * BN / QK_GROUPS
                                        : EPI == EPI_BF16 ? 64u * BN
-                                       : DGATE ? 128u * HD
+                                       : DGATE ? 0u
                                                : 32u * (BN < 128 ? BN : 128) * 4;
   static constexpr uint32_t STAGING = EPI_WARPS * WARP_STG;
-  static constexpr uint32_t INPUTS = QKVG ? 512u * HD : DGATE ? 4u * IN_BUFS * 128u * HD : 0;
-  static constexpr uint32_t FIXED = 1024 + STAGING + INPUTS + 256;
+  // DGATE: per warp two buffers of one head's O and sigmoid(g) rows (32 x HD
+  // each), overwritten in place by dO and dg_pre and stored from there.
+  static constexpr uint32_t INPUTS = QKVG ? 512u * HD : DGATE ? EPI_WARPS * 2u * 128u * HD : 0;
+  static constexpr int AUX_BARS = 16;
+  static constexpr uint32_t FIXED = 1024 + STAGING + INPUTS + 512;
   static constexpr int STAGES_FIT = int((GEMM_SMEM_LIMIT - FIXED) / STAGE_BYTES);
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -384,95 +388,103 @@ __device__ __forceinline__ void epi_qkvg(const GemmMaps& maps, const GemmParams&
   }
 }
 
-// Gate backward on the dGated = dY * Wo tile, head by head (fast_triton_attn.py:576-584, :601):
+// Gate backward on the dGated = dY * Wo tile (fast_triton_attn.py:576-584, :601):
 //   dO = dGated*g  -> [B,H,T,N] bf16 (input of the attention backward)
 //   dg_pre = dGated*O*g*(1-g) -> the g slot of the projection-gradient buffer
 //   delta = rowsum(dO*O) per (b,h,t)  (the attention backward's D term)
-// O and sigmoid(g) of each head come in by TMA into per-warp buffers, two heads
-// ahead (one for N = 128), so their latency overlaps the mainloop and the
-// previous head.  `hc` counts this warp's heads across tiles (buffer phases).
-template <int BN, int HD, int IN_BUFS>
-__device__ __forceinline__ void dgate_issue(const GemmMaps& maps, uint32_t inb, uint32_t in_bar, int b, int H, int T,
+// Each warp streams the heads s (s % G == its group) of its 32 rows through two
+// buffers: O and sigmoid(g) of a head come in by TMA, are overwritten in place
+// by dO and dg_pre (each lane reads and then writes the same 16-byte units of
+// its own row) and go out by TMA from there.  The next head's load (of this
+// tile, or the first of the warp's next tile) is issued while this head is
+// processed.  `hc` counts the warp's heads (buffer hc & 1, phase (hc >> 1) & 1).
+template <int HD>
+__device__ __forceinline__ void dgate_issue(const GemmMaps& maps, uint32_t buf, uint32_t bar, int b, int H, int T,
                                             int tq, int head) {
   constexpr uint32_t TILE = 32 * HD * 2;
   const int row = (b * H + head) * T + tq;
-  mbar_expect_tx(in_bar, 2 * TILE);
+  mbar_expect_tx(bar, 2 * TILE);
 #pragma unroll
   for (int bx = 0; bx < (HD + 63) / 64; ++bx) {
-    tma_load_2d(inb + bx * 4096, &maps.in[0], in_bar, 64 * bx, row);
-    tma_load_2d(inb + TILE + bx * 4096, &maps.in[1], in_bar, 64 * bx, row);
+    tma_load_2d(buf + bx * 4096, &maps.in[0], bar, 64 * bx, row);
+    tma_load_2d(buf + TILE + bx * 4096, &maps.in[1], bar, 64 * bx, row);
   }
 }
 
-template <int BN, int HD, int IN_BUFS>
-__device__ __forceinline__ void epi_dgate(const GemmMaps& maps, const GemmParams& p, uint32_t taddr, uint32_t stg,
-                                          uint32_t inb0, uint32_t in_bar0, uint32_t& hc, int lane, int mq, int n0,
-                                          uint32_t acce_cl, Guard& g) {
-  constexpr int NH = BN / HD;
+template <int BN, int HD, int G>
+__device__ __forceinline__ void epi_dgate(const GemmMaps& maps, const GemmParams& p, uint32_t taddr, uint32_t inb,
+                                          uint32_t in_bar, uint32_t& hc, int lane, int wg, int mq, int n0,
+                                          bool has_next, int next_mq, int next_n0, uint32_t acce_cl, Guard& g) {
+  constexpr int NJ = BN / HD / G;
   constexpr uint32_t TILE = 32 * HD * 2;
   const int b = mq / p.T;
   const int tq = mq - b * p.T;
   const bool valid = mq + lane < p.M;
-  const uint32_t hc0 = hc;
 #pragma unroll 1
-  for (int s = 0; s < NH; ++s, ++hc) {
-    const int head = n0 / HD + s;
-    const uint32_t buf = IN_BUFS == 2 ? (hc & 1) : 0;
-    const uint32_t par = IN_BUFS == 2 ? ((hc >> 1) & 1) : (hc & 1);
-    const uint32_t inb = inb0 + buf * 2 * TILE;
-    const uint32_t in_bar = in_bar0 + 8 * buf;
-    // this head's inputs were issued ahead (the first heads of the tile by the caller)
-    bool ok = mbar_wait(in_bar, par, g, 8);
+  for (int j = 0; j < NJ; ++j, ++hc) {
+    const int head = n0 / HD + wg + G * j;
+    const uint32_t buf = inb + (hc & 1) * 2 * TILE;
+    const uint32_t bar = in_bar + 8 * (hc & 1);
+    // The other buffer's last store has read it: refill it with the next head.
+    staging_acquire(lane);
+    if (lane == 0) {
+      const uint32_t nbuf = inb + ((hc + 1) & 1) * 2 * TILE, nbar = in_bar + 8 * ((hc + 1) & 1);
+      if (j + 1 < NJ) {
+        dgate_issue<HD>(maps, nbuf, nbar, b, p.H, p.T, tq, head + G);
+      } else if (has_next) {
+        const int nb = next_mq / p.T;
+        dgate_issue<HD>(maps, nbuf, nbar, nb, p.H, p.T, next_mq - nb * p.T, next_n0 / HD + wg);
+      }
+    }
+    bool ok = mbar_wait(bar, (hc >> 1) & 1, g, 8);
     ok = __all_sync(0xffffffffu, ok);
     if (!ok) {
       g.ok = false;
       break;
     }
-    staging_acquire(lane);
     float dsum = 0.f;
 #pragma unroll 1
     for (int ci = 0; ci < HD / 32; ++ci) {
       uint32_t r[32];
-      tmem_load32(taddr + s * HD + 32 * ci, r);
+      tmem_load32(taddr + (wg + G * j) * HD + 32 * ci, r);
 #pragma unroll
       for (int j4 = 0; j4 < 4; ++j4) {
         const int u = 4 * ci + j4;
-        const uint4 ov = lds_v4(hd_unit<HD>(inb, lane, u));
-        const uint4 gv = lds_v4(hd_unit<HD>(inb + TILE, lane, u));
+        const uint32_t ao = hd_unit<HD>(buf, lane, u), ag = hd_unit<HD>(buf + TILE, lane, u);
+        const uint4 ov = lds_v4(ao);
+        const uint4 gv = lds_v4(ag);
         const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
         const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
         uint32_t pd[4], pg[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int j = 8 * j4 + 2 * e;
+          const int jj = 8 * j4 + 2 * e;
           const float o0 = bf16_lo(ow[e]), o1 = bf16_hi(ow[e]);
           const float g0 = bf16_lo(gw[e]), g1 = bf16_hi(gw[e]);
-          const float d0 = __uint_as_float(r[j]), d1 = __uint_as_float(r[j + 1]);
+          const float d0 = __uint_as_float(r[jj]), d1 = __uint_as_float(r[jj + 1]);
           const float do0 = round_bf16(d0 * g0), do1 = round_bf16(d1 * g1);
           dsum = fmaf(do0, o0, dsum);
           dsum = fmaf(do1, o1, dsum);
           pd[e] = pack_bf16(do0, do1);
           pg[e] = pack_bf16(d0 * o0 * g0 * (1.0f - g0), d1 * o1 * g1 * (1.0f - g1));
         }
-        sts_v4(hd_unit<HD>(stg, lane, u), pd);
-        sts_v4(hd_unit<HD>(stg + TILE, lane, u), pg);
+        sts_v4(ao, pd);
+        sts_v4(ag, pg);
       }
     }
     if (valid) p.delta[(size_t(b) * p.H + head) * p.T + tq + lane] = dsum;
-    if (s == NH - 1) release_acc(acce_cl, lane);
-    staging_publish();  // also orders this warp's reads of the input buffer before its refill
+    if (j == NJ - 1) release_acc(acce_cl, lane);
+    staging_publish();
     if (lane == 0) {
       const int row = (b * p.H + head) * p.T + tq;
 #pragma unroll
       for (int bx = 0; bx < (HD + 63) / 64; ++bx) {
-        tma_store_2d(&maps.out[0], stg + bx * 4096, 64 * bx, row);
-        tma_store_2d(&maps.out[1], stg + TILE + bx * 4096, head * HD + 64 * bx, mq);
+        tma_store_2d(&maps.out[0], buf + bx * 4096, 64 * bx, row);
+        tma_store_2d(&maps.out[1], buf + TILE + bx * 4096, head * HD + 64 * bx, mq);
       }
       bulk_commit();
-      if (s + IN_BUFS < NH) dgate_issue<BN, HD, IN_BUFS>(maps, inb, in_bar, b, p.H, p.T, tq, head + IN_BUFS);
     }
   }
-  hc = hc0 + NH;
 }
 
 // ---------------------------------------------------------------------------
@@ -504,7 +516,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
   const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
   // QKVG: table full/empty per lane quarter; DGATE: input buffers per epilogue warp
   auto aux_bar = [&](int i) { return bar0 + 8u * (2 * STAGES + 5 + i); };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 13);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5 + Cfg::AUX_BARS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -523,10 +535,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
       mbar_init(acce_bar(b), 2 * Cfg::EPI_WARPS);  // every epilogue warp of both CTAs
     }
     mbar_init(drain_bar, 1);
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(aux_bar(i), 1);
-      mbar_init(aux_bar(4 + i), Cfg::QKVG ? 2 : 1);
-    }
+    for (int i = 0; i < Cfg::AUX_BARS; ++i) mbar_init(aux_bar(i), (Cfg::QKVG && i >= 4 && i < 8) ? 2 : 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -664,10 +673,20 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
     // QKVG: the quarter's rotary-table tile (f1 then f2), loaded by the group-0 warp
     const uint32_t tab = sIn + quarter * (Cfg::QKVG ? 2 * 32 * HD * 2 : 0);
     uint32_t tab_par = 0;
-    // DGATE: this warp's input buffers and their barriers
-    const uint32_t inb = sIn + (warp - 2) * (Cfg::DGATE ? Cfg::IN_BUFS * 128 * HD : 0);
+    // DGATE: this warp's two head buffers and their barriers; the first head of
+    // the warp's first tile is requested before the loop
+    const uint32_t inb = sIn + (warp - 2) * (Cfg::DGATE ? 2 * 128 * HD : 0);
     const uint32_t in_bar = aux_bar(Cfg::DGATE ? 2 * (warp - 2) : 0);
     uint32_t hc = 0;
+    if constexpr (Cfg::DGATE) {
+      if (lane == 0 && pair < nunits) {
+        int m0, n0, kb0, kb1;
+        gemm_decode(p, BN, pair, m0, n0, kb0, kb1);
+        const int mq = m0 + int(rank) * GEMM_BM + quarter * 32;
+        const int b = mq / p.T;
+        dgate_issue<HD>(maps, inb, in_bar, b, p.H, p.T, mq - b * p.T, n0 / HD + wg);
+      }
+    }
     int it = 0;
     for (int u = pair; u < nunits; u += npairs, ++it) {
       int m0, n0, kb0, kb1;
@@ -687,18 +706,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
           }
         }
       }
-      if constexpr (Cfg::DGATE) {
-        // the tile's first heads: requested before the accumulator wait
-        if (lane == 0) {
-          const int b = mq / p.T, tq = mq - b * p.T;
-#pragma unroll
-          for (int i = 0; i < Cfg::IN_BUFS && i < BN / HD; ++i) {
-            const uint32_t hb = Cfg::IN_BUFS == 2 ? ((hc + i) & 1) : 0;
-            dgate_issue<BN, HD, Cfg::IN_BUFS>(maps, inb + hb * 2 * 32 * HD * 2, in_bar + 8 * hb, b, p.H, p.T, tq,
-                                              n0 / HD + i);
-          }
-        }
-      }
       bool ok = mbar_wait(accf_bar(buf), (it >> 1) & 1, g, 4);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
@@ -714,7 +721,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
                          acce_cl, g);
         if (need_tab) tab_par ^= 1;
       } else if constexpr (Cfg::DGATE) {
-        epi_dgate<BN, HD, Cfg::IN_BUFS>(maps, p, taddr, stg, inb, in_bar, hc, lane, mq, n0, acce_cl, g);
+        const bool has_next = u + npairs < nunits;
+        int nm0 = 0, nn0 = 0;
+        if (has_next) gemm_decode(p, BN, u + npairs, nm0, nn0, kb0, kb1);
+        epi_dgate<BN, HD, Cfg::DG_GROUPS>(maps, p, taddr, inb, in_bar, hc, lane, wg, mq, n0, has_next,
+                                          nm0 + int(rank) * GEMM_BM + quarter * 32, nn0, acce_cl, g);
       } else if constexpr (EPI == EPI_BF16) {
         epi_bf16<BN>(maps, taddr, stg, lane, mq, n0, acce_cl);
       } else {
