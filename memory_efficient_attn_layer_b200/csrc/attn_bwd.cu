@@ -107,10 +107,11 @@ __device__ __forceinline__ void st_tile_row16(uint32_t tile, int r, int c, const
 template <bool DIAG>
 __device__ __forceinline__ void bwd_chunk(const uint32_t (&sv)[16], const uint32_t (&dp)[16], int c, int cbase, int r,
                                           float2 scale2, float2 bias2, float dl, uint32_t (&pk)[32], uint32_t (&dsk)[32]) {
+  const float2 dl2 = make_float2(dl, dl);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const float2 t = ffma2(make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), scale2, bias2);
-    const float2 pp = exp2_pair(t, (kPolyPairs >> e) & 1);
+    const float2 pp = exp2_pair(t, (kPolyPairsBwd >> e) & 1);
     float p0 = pp.x, p1 = pp.y;
     if (DIAG) {  // key column > query row: masked
       const int c0 = 16 * (cbase + c) + 2 * e;
@@ -118,7 +119,9 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t (&sv)[16], const uint32
       p1 = c0 + 1 > r ? 0.f : p1;
     }
     pk[8 * c + e] = pack_bf16(p0, p1);
-    dsk[8 * c + e] = pack_bf16(p0 * (__uint_as_float(dp[2 * e]) - dl), p1 * (__uint_as_float(dp[2 * e + 1]) - dl));
+    const float2 ds = fmul2(make_float2(p0, p1),
+                            fsub2(make_float2(__uint_as_float(dp[2 * e]), __uint_as_float(dp[2 * e + 1])), dl2));
+    dsk[8 * c + e] = pack_bf16(ds.x, ds.y);
   }
 }
 

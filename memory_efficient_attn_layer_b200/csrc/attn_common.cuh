@@ -10,9 +10,17 @@
 namespace mea {
 
 // Pairs of each 16-score softmax chunk whose exp2 runs as a polynomial on the
-// FMA pipe (bit e = pair e, exp2_poly2); the rest use MUFU ex2.  Three of eight
-// roughly balances the two pipes.
-constexpr uint32_t kPolyPairs = 0x4A;
+// FMA pipe (bit e = pair e, exp2_poly2); the rest use MUFU ex2.  The forward's
+// softmax does little else on the FMA pipe, the backward's also forms dS there,
+// so each balances the two pipes with its own share.
+#ifndef MEA_POLY_FWD
+#define MEA_POLY_FWD 0x4A
+#endif
+#ifndef MEA_POLY_BWD
+#define MEA_POLY_BWD 0x4A
+#endif
+constexpr uint32_t kPolyPairsFwd = MEA_POLY_FWD;
+constexpr uint32_t kPolyPairsBwd = MEA_POLY_BWD;
 
 // exp2 of a pair, on the FMA pipe when `poly` (argument clamped at -127, where
 // the result is negligible next to the row's largest term) else on MUFU.

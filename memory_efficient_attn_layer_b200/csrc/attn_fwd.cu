@@ -112,7 +112,7 @@ __device__ __forceinline__ void exp_chunk(const uint32_t (&v)[16], uint32_t sb, 
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const float2 t = ffma2(make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), scale2, bias2);
-    const float2 pp = exp2_pair(t, (kPolyPairs >> e) & 1);
+    const float2 pp = exp2_pair(t, (kPolyPairsFwd >> e) & 1);
     float p0 = pp.x, p1 = pp.y;
     if (DIAG) {
       const int c0 = 16 * c + 2 * e;
@@ -161,7 +161,7 @@ __device__ __forceinline__ float exp_row_regs(uint32_t sb, int r, float sl2, flo
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const float2 t = ffma2(make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), scale2, bias2);
-      const float2 pp = exp2_pair(t, (kPolyPairs >> e) & 1);
+      const float2 pp = exp2_pair(t, (kPolyPairsFwd >> e) & 1);
       float p0 = pp.x, p1 = pp.y;
       if (DIAG) {
         const int c0 = 16 * c + 2 * e;
