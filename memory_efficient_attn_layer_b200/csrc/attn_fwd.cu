@@ -189,6 +189,46 @@ __device__ __forceinline__ float exp_row_regs(uint32_t sb, int r, float sl2, flo
   return (acc0.x + acc0.y) + (acc1.x + acc1.y);
 }
 
+// P = exp2(s * sl2 - m) of key columns [64*hh, 64*hh + 64) of query row r into
+// registers (packed bf16 pairs, columns 64*hh + [2i, 2i+2) in pk[i]); returns
+// this half's share of the row sum.  Every TMEM load has completed on return.
+template <bool DIAG>
+__device__ __forceinline__ float exp_half_regs(uint32_t sb, int hh, int r, float sl2, float neg_m, uint32_t (&pk)[32]) {
+  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+  const float2 scale2 = make_float2(sl2, sl2), bias2 = make_float2(neg_m, neg_m);
+  uint32_t a[16], b[16];
+  auto chunk = [&](const uint32_t(&v)[16], int c) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float2 t = ffma2(make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), scale2, bias2);
+      const float2 pp = exp2_pair(t, (kPolyPairsFwd >> e) & 1);
+      float p0 = pp.x, p1 = pp.y;
+      if (DIAG) {
+        const int c0 = 64 * hh + 16 * c + 2 * e;
+        p0 = c0 > r ? 0.f : p0;
+        p1 = c0 + 1 > r ? 0.f : p1;
+      }
+      if (e & 1)
+        acc1 = fadd2(acc1, make_float2(p0, p1));
+      else
+        acc0 = fadd2(acc0, make_float2(p0, p1));
+      pk[8 * c + e] = pack_bf16(p0, p1);
+    }
+  };
+  tmem_ld16(sb + 64 * hh, a);
+  tmem_wait_ld_tied(a);
+#pragma unroll
+  for (int c = 0; c < 4; c += 2) {
+    tmem_ld16(sb + 64 * hh + 16 * (c + 1), b);
+    chunk(a, c);
+    tmem_wait_ld_tied(b);
+    if (c + 2 < 4) tmem_ld16(sb + 64 * hh + 16 * (c + 2), a);
+    chunk(b, c + 1);
+    if (c + 2 < 4) tmem_wait_ld_tied(a);
+  }
+  return (acc0.x + acc0.y) + (acc1.x + acc1.y);
+}
+
 template <int HD>
 __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ AttnFwdMaps maps, const AttnFwdParams p) {
   using Cfg = AttnFwdCfg<HD>;
@@ -196,6 +236,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
   constexpr int KS = Cfg::KS, VS = Cfg::VS;
   constexpr uint32_t TB = Cfg::TILE_BYTES;
   constexpr uint32_t IDESC_S = idesc_bf16(128, 128, 0, 0);
+  constexpr uint32_t IDESC_SH = idesc_bf16(128, 64, 0, 0);  // (SEP_P) one 64-key half of S
   constexpr uint32_t IDESC_O = idesc_bf16(128, HD, 0, 1);
 
   extern __shared__ uint8_t smem_raw[];
@@ -214,9 +255,13 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
   const uint32_t p_full = s_full + 8;
   const uint32_t o_bar = s_full + 16;
   const uint32_t drain_bar = s_full + 24;
-  const uint32_t s_empty = s_full + 32;  // (SEP_P) softmax has read S_j
+  const uint32_t s_empty = s_full + 32;  // (SEP_P) softmax has read the key half [0, 64) of S_j
   const uint32_t pv_done = s_full + 40;  // (SEP_P) PV_j has completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7 + 2 * KS + 2 * VS);
+  // (SEP_P) S_j is computed in two 64-key halves: s_full / s_empty for keys
+  // [0, 64), s_full_b / s_empty_b for [64, 128)
+  const uint32_t s_full_b = s_full + 48;
+  const uint32_t s_empty_b = s_full + 56;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9 + 2 * KS + 2 * VS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -246,6 +291,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     mbar_init(drain_bar, 1);
     mbar_init(s_empty, 128);
     mbar_init(pv_done, 1);
+    mbar_init(s_full_b, 1);
+    mbar_init(s_empty_b, 128);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -317,17 +364,33 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         mma_commit(s_full);
       };
       if constexpr (Cfg::SEP_P) {
+        // S_j in two 64-key halves, each committed to its own barrier, so that the
+        // half [0, 64) of S_{j+1} runs while the softmax warps work on keys
+        // [64, 128) of S_j, and the other half while they start on S_{j+1}.
+        auto issue_half = [&](int j, int hf) {
+          const int sk = j % KS;
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk)
+            mma_ss(tmem + Cfg::S_COL + 64 * hf, Tile::kmajor(sQ, 128, kk),
+                   Tile::kmajor(sK + sk * TB + hf * 64 * Tile::SWB, 128, kk), IDESC_SH, kk > 0 ? 1u : 0u);
+          if (hf) mma_commit(k_empty(sk));
+          mma_commit(hf ? s_full_b : s_full);
+        };
         if (mbar_wait(q_full, 0, g, 5) && mbar_wait(k_full(0), 0, g, 2)) {
           tc_fence_after();
-          issue_s(0);
+          issue_half(0, 0);
+          issue_half(0, 1);
           any = true;
           for (int j = 0; j < nkv; ++j) {
             const int sv = j % VS;
-            if (j + 1 < nkv) {  // S_{j+1} as soon as S_j has been read
+            if (j + 1 < nkv) {  // each half of S_{j+1} as soon as that half of S_j has been read
               if (!mbar_wait(s_empty, j & 1, g, 10)) break;
               if (!mbar_wait(k_full((j + 1) % KS), ((j + 1) / KS) & 1, g, 2)) break;
               tc_fence_after();
-              issue_s(j + 1);
+              issue_half(j + 1, 0);
+              if (!mbar_wait(s_empty_b, j & 1, g, 16)) break;
+              tc_fence_after();
+              issue_half(j + 1, 1);
             }
             if (!mbar_wait(p_full, j & 1, g, 3)) break;
             if (!mbar_wait(v_full(sv), (j / VS) & 1, g, 4)) break;
@@ -393,6 +456,10 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     float m_run = -INFINITY, l_run = 0.f;  // m_run in scaled log2 units
     bool ok = true;
     if constexpr (Cfg::SEP_P) {
+      // S_j arrives in two 64-key halves; each half is released (s_empty,
+      // s_empty_b) as soon as its exponentials are done, and its bf16 P
+      // columns are written right away (once PV_{j-1} has consumed the
+      // previous P).
       const uint32_t sb = lane_base + Cfg::S_COL;
       for (int j = 0; j < nkv && ok; ++j) {
         ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, g, 6));
@@ -400,7 +467,13 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         tc_fence_after();
         const bool diag = (j == qt);
         bool pv_seen = (j == 0);  // PV_{j-1} has completed (O and the P columns are free)
+        bool have_b = false;      // the half [64, 128) of S_j has landed
         if (mode == 0) {
+          // The online max needs the whole score row.
+          ok = __all_sync(0xffffffffu, mbar_wait(s_full_b, j & 1, g, 17));
+          if (!ok) break;
+          tc_fence_after();
+          have_b = true;
           const float mx = (diag ? score_row_max<true>(sb, r) : score_row_max<false>(sb, r)) * sl2;
           // Lazy rescale: refresh the reference max only when it grows by > 8 (log2 units).
           const bool need = mx > m_run + 8.0f;
@@ -426,18 +499,32 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
           }
         }
         const float neg_m = mode != 0 ? -ref : -m_run;
-        uint32_t pk[64];
-        l_run += diag ? exp_row_regs<true>(sb, r, sl2, neg_m, pk) : exp_row_regs<false>(sb, r, sl2, neg_m, pk);
+        uint32_t pk[32];
+        // keys [0, 64)
+        l_run += diag ? exp_half_regs<true>(sb, 0, r, sl2, neg_m, pk) : exp_half_regs<false>(sb, 0, r, sl2, neg_m, pk);
         tc_fence_before();
-        mbar_arrive(s_empty);  // S_j fully read: S_{j+1} may overwrite it
+        mbar_arrive(s_empty);
         if (!pv_seen) {
           ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, g, 12));
           if (!ok) break;
           tc_fence_after();
         }
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-          tmem_st16(lane_base + Cfg::P_COL + 16 * q4, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * q4));
+        for (int q2 = 0; q2 < 2; ++q2)
+          tmem_st16(lane_base + Cfg::P_COL + 16 * q2, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * q2));
+        tmem_st_wait();  // the registers of pk are rewritten below
+        // keys [64, 128)
+        if (!have_b) {
+          ok = __all_sync(0xffffffffu, mbar_wait(s_full_b, j & 1, g, 17));
+          if (!ok) break;
+          tc_fence_after();
+        }
+        l_run += diag ? exp_half_regs<true>(sb, 1, r, sl2, neg_m, pk) : exp_half_regs<false>(sb, 1, r, sl2, neg_m, pk);
+        tc_fence_before();
+        mbar_arrive(s_empty_b);
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2)
+          tmem_st16(lane_base + Cfg::P_COL + 32 + 16 * q2, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * q2));
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(p_full);
