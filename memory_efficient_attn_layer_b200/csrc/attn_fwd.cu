@@ -14,11 +14,11 @@
 // thread.  Key tiles above the diagonal are never loaded (causal skipping); the
 // diagonal tile is masked.
 //
-// TMEM, N <= 64: S [0,128), P [128,192), O [192, 192+N).  The softmax warps
-// build a whole row of bf16 P in registers, release S_j (s_empty) once read,
-// so S_{j+1} = Q K_{j+1}^T runs while they finish, and write P_j into its own
-// columns once PV_{j-1} has consumed the previous P (pv_done): the per-tile
-// chain is softmax + S MMA, with PV off it.  N = 128 (O needs 128 columns): S
+// TMEM, N <= 64: S [0,128), P [128,192), O [192, 192+N).  S_j is computed in
+// two 64-key halves with their own barriers; the softmax warps turn each half
+// into bf16 P in registers, release it (so that half of S_{j+1} = Q K_{j+1}^T
+// runs while they work on the other) and write its P columns once PV_{j-1} has
+// consumed the previous P (pv_done): neither MMA sits on the per-tile chain.  N = 128 (O needs 128 columns): S
 // [0,128) with P written over it in place, O [128,256); S_{j+1} is issued after
 // PV_j (tcgen05 MMAs of one thread run in issue order).
 //
@@ -144,46 +144,6 @@ __device__ __forceinline__ float exp_pack_row(uint32_t sb, int r, float sl2, flo
     tmem_wait_ld_tied(b);
     if (c + 2 < 8) tmem_ld16(sb + 16 * (c + 2), a);
     exp_chunk<DIAG>(b, sb, c + 1, r, scale2, bias2, acc0, acc1);
-    if (c + 2 < 8) tmem_wait_ld_tied(a);
-  }
-  return (acc0.x + acc0.y) + (acc1.x + acc1.y);
-}
-
-// P = exp2(s * sl2 - m) for one row into registers (packed bf16 pairs, key
-// columns [2i, 2i+2) in pk[i]); returns the row sum of P.  Every TMEM load of
-// the score row has completed on return.
-template <bool DIAG>
-__device__ __forceinline__ float exp_row_regs(uint32_t sb, int r, float sl2, float neg_m, uint32_t (&pk)[64]) {
-  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-  const float2 scale2 = make_float2(sl2, sl2), bias2 = make_float2(neg_m, neg_m);
-  uint32_t a[16], b[16];
-  auto chunk = [&](const uint32_t(&v)[16], int c) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float2 t = ffma2(make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), scale2, bias2);
-      const float2 pp = exp2_pair(t, (kPolyPairsFwd >> e) & 1);
-      float p0 = pp.x, p1 = pp.y;
-      if (DIAG) {
-        const int c0 = 16 * c + 2 * e;
-        p0 = c0 > r ? 0.f : p0;
-        p1 = c0 + 1 > r ? 0.f : p1;
-      }
-      if (e & 1)
-        acc1 = fadd2(acc1, make_float2(p0, p1));
-      else
-        acc0 = fadd2(acc0, make_float2(p0, p1));
-      pk[8 * c + e] = pack_bf16(p0, p1);
-    }
-  };
-  tmem_ld16(sb, a);
-  tmem_wait_ld_tied(a);
-#pragma unroll
-  for (int c = 0; c < 8; c += 2) {
-    tmem_ld16(sb + 16 * (c + 1), b);
-    chunk(a, c);
-    tmem_wait_ld_tied(b);
-    if (c + 2 < 8) tmem_ld16(sb + 16 * (c + 2), a);
-    chunk(b, c + 1);
     if (c + 2 < 8) tmem_wait_ld_tied(a);
   }
   return (acc0.x + acc0.y) + (acc1.x + acc1.y);
