@@ -62,7 +62,8 @@ struct AttnBwdMaps {
 template <int HD>
 struct AttnBwdCfg {
   static constexpr bool OVERLAP = HD <= 64;
-  static constexpr int STAGES = HD <= 64 ? 2 : 1;  // Q/dO ring depth
+  static constexpr int STAGES = HD <= 64 ? 2 : 1;   // Q/dO ring depth
+  static constexpr int KV_BUFS = HD <= 64 ? 2 : 1;  // K/V buffers: the next work item's load overlaps this one
   static constexpr uint32_t TB = 128 * HD * 2;
   static constexpr uint32_t PT = 128 * 128 * 2;  // one bf16 [128 x 128] P or dS tile
   static constexpr uint32_t S_COL = 0, DP_COL = 128;
@@ -72,15 +73,45 @@ struct AttnBwdCfg {
   static constexpr uint32_t DQ_COL = OVERLAP ? DK_COL + HD : DP_COL;
   static constexpr uint32_t TMEM_COLS = 512;
   static_assert(!OVERLAP || DQ_COL + HD <= 512, "TMEM budget");
-  static constexpr uint32_t OFF_K = 0, OFF_V = TB, OFF_Q = 2 * TB, OFF_DO = OFF_Q + STAGES * TB;
+  static constexpr uint32_t OFF_KV = 0;  // buffer b: K at OFF_KV + 2*TB*b, V right after it
+  static constexpr uint32_t OFF_Q = KV_BUFS * 2 * TB, OFF_DO = OFF_Q + STAGES * TB;
   static constexpr uint32_t OFF_P = OFF_DO + STAGES * TB, OFF_DS = OFF_P + PT;
   static constexpr uint32_t OFF_LSE = OFF_DS + PT;
-  static constexpr int DQ_COLS = HD < 64 ? HD : 64;             // dQ columns staged per round
-  static constexpr int DQ_ROUNDS = HD / DQ_COLS;                // rounds per dQ tile (2 for N = 128)
+  static constexpr int DQ_COLS = HD <= 64 ? 32 : 64;            // dQ columns staged per round
+  static constexpr int DQ_ROUNDS = HD / DQ_COLS;                // rounds per dQ tile
   static constexpr uint32_t OFF_DQ = OFF_LSE + STAGES * 1024;   // DQ_COLS/32 boxes of [128 x 32] fp32
   static constexpr uint32_t DQ_BYTES = DQ_COLS * 512;
   static constexpr uint32_t OFF_BAR = OFF_DQ + DQ_BYTES;
   static constexpr size_t SMEM = 1024 + OFF_BAR + 256;
+};
+
+// Work items of the persistent backward: one (b,h) and one 128-row key tile jt,
+// walking the nq - jt query tiles from the diagonal.  Items come in pairs of
+// key tiles (k, nq-1-k) of one head, which together walk nq + 1 query tiles,
+// so CTAs striding over pairs get equal work; consecutive pairs belong to the
+// same head, so the CTAs running at one time share a few heads' Q/dO and dQ
+// rows in L2.  Every role of a CTA walks the same sequence.
+struct BwdItems {
+  int nq, pairs_per_head, total_pairs, stride;
+  int p, side;
+  __device__ BwdItems(int nq_, int bh_count, int start, int stride_)
+      : nq(nq_), pairs_per_head((nq_ + 1) / 2), total_pairs(bh_count * ((nq_ + 1) / 2)), stride(stride_), p(start),
+        side(0) {}
+  __device__ bool valid() const { return p < total_pairs; }
+  __device__ void get(int& bh, int& jt) const {
+    bh = p / pairs_per_head;
+    const int k = p - bh * pairs_per_head;
+    jt = side ? nq - 1 - k : k;
+  }
+  __device__ void next() {
+    const int k = p % pairs_per_head;
+    if (side == 0 && nq - 1 - k != k) {
+      side = 1;
+    } else {
+      side = 0;
+      p += stride;
+    }
+  }
 };
 
 // MN-major descriptor of a [128 q rows x 128 kv] bf16 tile stored as two
@@ -179,6 +210,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
   using Cfg = AttnBwdCfg<HD>;
   using Tile = HeadTile<HD>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int KV_BUFS = Cfg::KV_BUFS;
   constexpr uint32_t TB = Cfg::TB;
   constexpr bool OVERLAP = Cfg::OVERLAP;
   constexpr uint32_t IDESC_SS = idesc_bf16(128, 128, 0, 0);  // S, dP
@@ -188,39 +220,39 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t base = smem_u32(smem);
-  const uint32_t sK = base + Cfg::OFF_K, sV = base + Cfg::OFF_V;
+  auto sK = [&](int b) { return base + Cfg::OFF_KV + 2 * TB * b; };
+  auto sV = [&](int b) { return base + Cfg::OFF_KV + 2 * TB * b + TB; };
   auto sQ = [&](int s) { return base + Cfg::OFF_Q + s * TB; };
   auto sdO = [&](int s) { return base + Cfg::OFF_DO + s * TB; };
   const uint32_t sP = base + Cfg::OFF_P, sDS = base + Cfg::OFF_DS;
   float* lse_s = reinterpret_cast<float*>(smem + Cfg::OFF_LSE);  // [STAGES][2][128]: lse2, delta
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
   const uint32_t b0 = smem_u32(bars);
-  const uint32_t kv_full = b0;
-  auto qdo_full = [&](int s) { return b0 + 8u * (1 + s); };
-  auto qdo_empty = [&](int s) { return b0 + 8u * (1 + STAGES + s); };
-  const uint32_t st_full = b0 + 8u * (1 + 2 * STAGES);
+  auto kv_full = [&](int b) { return b0 + 8u * b; };
+  auto kv_empty = [&](int b) { return b0 + 8u * (2 + b); };
+  auto qdo_full = [&](int s) { return b0 + 8u * (4 + s); };
+  auto qdo_empty = [&](int s) { return b0 + 8u * (4 + STAGES + s); };
+  const uint32_t st_full = b0 + 8u * (4 + 2 * STAGES);
   const uint32_t ds_full = st_full + 8;
   const uint32_t dq_full = st_full + 16;
   const uint32_t dq_empty = st_full + 24;
   const uint32_t drain_bar = st_full + 32;
-  const uint32_t st_empty = st_full + 40;   // softmax warps have read S_n and dP_n
-  const uint32_t stg_full = st_full + 48;   // dQ staging tile written
-  const uint32_t stg_empty = st_full + 56;  // previous TMA reduce has read the staging tile
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9 + 2 * STAGES);
+  const uint32_t st_empty = st_full + 40;     // softmax warps have read S_n and dP_n
+  const uint32_t stg_full = st_full + 48;     // dQ staging tile written
+  const uint32_t stg_empty = st_full + 56;    // previous TMA reduce has read the staging tile
+  const uint32_t kvacc_empty = st_full + 64;  // dK / dV of the previous work item read out of TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13 + 2 * STAGES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nq = p.T / 128;
-  // Head-major order: the key tiles of one (b,h) run side by side, so their dQ
-  // reductions land in the same L2-resident rows; the longest walks (small jt)
-  // start first within a head.
-  const int bh = int(blockIdx.x) / nq;
-  const int jt = int(blockIdx.x) % nq;
-  const int nsteps = nq - jt;
-  const int row0 = bh * p.T;
+  const int BH = p.B * p.H;
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(kv_full(b), 1);
+      mbar_init(kv_empty(b), 1);
+    }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(qdo_full(s), 1);
       mbar_init(qdo_empty(s), 1);
@@ -233,6 +265,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     mbar_init(st_empty, 256);
     mbar_init(stg_full, 128);
     mbar_init(stg_empty, 1);
+    mbar_init(kvacc_empty, 256);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -255,11 +288,11 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     }
   };
   // Register shares per warpgroup (launched with 512 threads x 128 = 65536):
-  // 128 x 72 (TMA/MMA) + 256 x 184 (softmax) + 128 x 72 (dQ) = 65536.  Each role
+  // 128 x 80 (TMA/MMA) + 256 x 184 (softmax) + 128 x 64 (dQ) = 65536.  Each role
   // sets its share first and ends in `finish`, so every role is compiled
   // against its own budget.
   if (warp < 4) {
-    reg_dealloc<72>();
+    reg_dealloc<80>();
     if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (elect_one()) {
@@ -267,77 +300,114 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
       tma_prefetch_desc(&maps.k);
       tma_prefetch_desc(&maps.v);
       tma_prefetch_desc(&maps.dO);
-      mbar_expect_tx(kv_full, 2 * TB);
-#pragma unroll
-      for (int c = 0; c < Tile::NCHUNK; ++c) {
-        tma_load_2d(sK + c * 128 * Tile::SWB, &maps.k, kv_full, c * Tile::CHUNK_ELEMS, row0 + jt * 128);
-        tma_load_2d(sV + c * 128 * Tile::SWB, &maps.v, kv_full, c * Tile::CHUNK_ELEMS, row0 + jt * 128);
-      }
       int last_par[STAGES];
       for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
-      for (int n = 0; n < nsteps; ++n) {
-        const int s = n % STAGES;
-        const uint32_t ph = (n / STAGES) & 1;
-        if (!mbar_wait(qdo_empty(s), ph ^ 1, g, 1)) break;
-        const int qrow = row0 + (jt + n) * 128;
-        const uint32_t fb = qdo_full(s);
-        mbar_expect_tx(fb, 2 * TB + 1024);
+      int kv_par[2] = {-1, -1};
+      int gstep = 0, item = 0;
+      for (BwdItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && g.ok; it.next(), ++item) {
+        int bh, jt;
+        it.get(bh, jt);
+        const int row0 = bh * p.T;
+        const int nsteps = nq - jt;
+        // K, V of this item into buffer kb once the item that last used it has
+        // finished its MMAs (kv_empty, committed after its last dQ)
+        const int kb = item % KV_BUFS;
+        if (item >= KV_BUFS && !mbar_wait(kv_empty(kb), uint32_t((item / KV_BUFS - 1) & 1), g, 16)) break;
+        mbar_expect_tx(kv_full(kb), 2 * TB);
 #pragma unroll
         for (int c = 0; c < Tile::NCHUNK; ++c) {
-          tma_load_2d(sQ(s) + c * 128 * Tile::SWB, &maps.q, fb, c * Tile::CHUNK_ELEMS, qrow);
-          tma_load_2d(sdO(s) + c * 128 * Tile::SWB, &maps.dO, fb, c * Tile::CHUNK_ELEMS, qrow);
+          tma_load_2d(sK(kb) + c * 128 * Tile::SWB, &maps.k, kv_full(kb), c * Tile::CHUNK_ELEMS, row0 + jt * 128);
+          tma_load_2d(sV(kb) + c * 128 * Tile::SWB, &maps.v, kv_full(kb), c * Tile::CHUNK_ELEMS, row0 + jt * 128);
         }
-        bulk_load(smem_u32(lse_s + s * 256), p.lse2 + qrow, 512, fb);
-        bulk_load(smem_u32(lse_s + s * 256 + 128), p.delta + qrow, 512, fb);
-        last_par[s] = int(ph);
+        kv_par[kb] = (item / KV_BUFS) & 1;
+        for (int n = 0; n < nsteps; ++n, ++gstep) {
+          const int s = gstep % STAGES;
+          const uint32_t ph = (gstep / STAGES) & 1;
+          if (!mbar_wait(qdo_empty(s), ph ^ 1, g, 1)) break;
+          const int qrow = row0 + (jt + n) * 128;
+          const uint32_t fb = qdo_full(s);
+          mbar_expect_tx(fb, 2 * TB + 1024);
+#pragma unroll
+          for (int c = 0; c < Tile::NCHUNK; ++c) {
+            tma_load_2d(sQ(s) + c * 128 * Tile::SWB, &maps.q, fb, c * Tile::CHUNK_ELEMS, qrow);
+            tma_load_2d(sdO(s) + c * 128 * Tile::SWB, &maps.dO, fb, c * Tile::CHUNK_ELEMS, qrow);
+          }
+          bulk_load(smem_u32(lse_s + s * 256), p.lse2 + qrow, 512, fb);
+          bulk_load(smem_u32(lse_s + s * 256 + 128), p.delta + qrow, 512, fb);
+          last_par[s] = int(ph);
+        }
       }
       if (!g.ok) {
-        mbar_drain(kv_full, 0);
+        for (int b = 0; b < 2; ++b)
+          if (kv_par[b] >= 0) mbar_drain(kv_full(b), uint32_t(kv_par[b]));
         for (int s = 0; s < STAGES; ++s)
           if (last_par[s] >= 0) mbar_drain(qdo_full(s), uint32_t(last_par[s]));
       } else {
         // Tail: wait for the MMA warp's release (tcgen05.commit) of every Q/dO
-        // slot's last fill, so no asynchronous arrive targets this CTA's shared
-        // memory after it exits.
+        // slot's and K/V buffer's last fill, so no asynchronous arrive targets
+        // this CTA's shared memory after it exits.
         for (int s = 0; s < STAGES; ++s)
           if (last_par[s] >= 0) mbar_wait(qdo_empty(s), uint32_t(last_par[s]), g, 15);
+        for (int b = 0; b < 2; ++b)
+          if (kv_par[b] >= 0) mbar_wait(kv_empty(b), uint32_t(kv_par[b]), g, 17);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (elect_one()) {
       bool any = false;
-      // S_n = Q_n K^T and dP_n = dO_n V^T, committed together to st_full.
-      auto issue_sdp = [&](int n) -> bool {
-        const int s = n % STAGES;
-        if (!mbar_wait(qdo_full(s), (n / STAGES) & 1, g, 3)) return false;
+      // S_g = Q_g K^T and dP_g = dO_g V^T (global step g, K/V buffer kb), committed together to st_full.
+      auto issue_sdp = [&](int gs, int kb) -> bool {
+        const int s = gs % STAGES;
+        if (!mbar_wait(qdo_full(s), (gs / STAGES) & 1, g, 3)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          mma_ss(tmem + Cfg::S_COL, Tile::kmajor(sQ(s), 128, kk), Tile::kmajor(sK, 128, kk), IDESC_SS, kk > 0 ? 1u : 0u);
-        if (!OVERLAP && n > 0) {  // dP's columns held dQ_{n-1}: wait for its read-out
-          if (!mbar_wait(dq_empty, (n - 1) & 1, g, 4)) return false;
+          mma_ss(tmem + Cfg::S_COL, Tile::kmajor(sQ(s), 128, kk), Tile::kmajor(sK(kb), 128, kk), IDESC_SS,
+                 kk > 0 ? 1u : 0u);
+        if (!OVERLAP && gs > 0) {  // dP's columns held dQ_{g-1}: wait for its read-out
+          if (!mbar_wait(dq_empty, (gs - 1) & 1, g, 4)) return false;
           tc_fence_after();
         }
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          mma_ss(tmem + Cfg::DP_COL, Tile::kmajor(sdO(s), 128, kk), Tile::kmajor(sV, 128, kk), IDESC_SS,
+          mma_ss(tmem + Cfg::DP_COL, Tile::kmajor(sdO(s), 128, kk), Tile::kmajor(sV(kb), 128, kk), IDESC_SS,
                  kk > 0 ? 1u : 0u);
         mma_commit(st_full);
         any = true;
         return true;
       };
-      if (mbar_wait(kv_full, 0, g, 2) && issue_sdp(0)) {
-        for (int n = 0; n < nsteps; ++n) {
-          const int s = n % STAGES;
-          if (OVERLAP && n + 1 < nsteps) {  // S_n, dP_n read: issue the next scores now
-            if (!mbar_wait(st_empty, n & 1, g, 12)) break;
+      int gstep = 0, item = 0;
+      bool first = true;
+      for (BwdItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && g.ok; it.next(), ++item) {
+        int bh, jt;
+        it.get(bh, jt);
+        const int nsteps = nq - jt;
+        const int kb = item % KV_BUFS;
+        BwdItems nx = it;
+        nx.next();
+        const bool has_next = nx.valid();
+        const int nkb = (item + 1) % KV_BUFS;
+        if (first) {  // later items' first scores are issued at the end of the previous item
+          if (!mbar_wait(kv_full(kb), 0, g, 2) || !issue_sdp(gstep, kb)) break;
+          first = false;
+        }
+        for (int n = 0; n < nsteps; ++n, ++gstep) {
+          const int s = gstep % STAGES;
+          const bool last = (n + 1 == nsteps);
+          if (OVERLAP && (!last || has_next)) {  // S_g, dP_g read: issue the next scores now
+            if (!mbar_wait(st_empty, gstep & 1, g, 12)) break;
             tc_fence_after();
-            if (!issue_sdp(n + 1)) break;
+            if (last && !mbar_wait(kv_full(nkb), ((item + 1) / KV_BUFS) & 1, g, 18)) break;
+            if (!issue_sdp(gstep + 1, last ? nkb : kb)) break;
           }
-          if (!mbar_wait(ds_full, n & 1, g, 5)) break;
+          if (!mbar_wait(ds_full, gstep & 1, g, 5)) break;
           tc_fence_after();
-          // dV += P^T dO_n ; dK += dS^T Q_n  (A operands MN-major from shared memory)
+          if (n == 0 && item > 0) {  // dK / dV of the previous item have been read out
+            if (!mbar_wait(kvacc_empty, (item - 1) & 1, g, 19)) break;
+            tc_fence_after();
+          }
+          // dV += P^T dO_g ; dK += dS^T Q_g  (A operands MN-major from shared memory)
 #pragma unroll
           for (int kc = 0; kc < 8; ++kc)
             mma_ss(tmem + Cfg::DV_COL, ptile_mn(sP, kc), Tile::mnmajor(sdO(s), 128, kc), IDESC_KV,
@@ -346,18 +416,22 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
           for (int kc = 0; kc < 8; ++kc)
             mma_ss(tmem + Cfg::DK_COL, ptile_mn(sDS, kc), Tile::mnmajor(sQ(s), 128, kc), IDESC_KV,
                    (n > 0 || kc > 0) ? 1u : 0u);
-          if (OVERLAP && n > 0) {
-            if (!mbar_wait(dq_empty, (n - 1) & 1, g, 6)) break;
+          if (OVERLAP && gstep > 0) {
+            if (!mbar_wait(dq_empty, (gstep - 1) & 1, g, 6)) break;
             tc_fence_after();
           }
-          // dQ_n = dS K  (dS from TMEM, packed bf16)
+          // dQ_g = dS K  (dS from TMEM, packed bf16)
 #pragma unroll
           for (int kc = 0; kc < 8; ++kc)
-            mma_ts(tmem + Cfg::DQ_COL, tmem + Cfg::DS_COL + kc * 8, Tile::mnmajor(sK, 128, kc), IDESC_DQ,
+            mma_ts(tmem + Cfg::DQ_COL, tmem + Cfg::DS_COL + kc * 8, Tile::mnmajor(sK(kb), 128, kc), IDESC_DQ,
                    kc > 0 ? 1u : 0u);
           mma_commit(qdo_empty(s));
           mma_commit(dq_full);
-          if (!OVERLAP && n + 1 < nsteps && !issue_sdp(n + 1)) break;
+          if (last) mma_commit(kv_empty(kb));  // every MMA reading this K/V buffer is complete
+          if (!OVERLAP && (!last || has_next)) {
+            if (last && !mbar_wait(kv_full(nkb), ((item + 1) / KV_BUFS) & 1, g, 18)) break;
+            if (!issue_sdp(gstep + 1, last ? nkb : kb)) break;
+          }
         }
       }
       if (!g.ok && any) {
@@ -374,58 +448,64 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     // ---------------- softmax warps 4..11 ----------------
     // Query row r = TMEM lane; warps 4..7 take key columns [0, 64), warps 8..11
     // [64, 128), so each sub-partition runs two softmax warps.  The same warps
-    // write dK / dV at the end.
+    // write each item's dK / dV at its end.
     const int quarter = warp & 3;
     const int hh = (warp - 4) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
     bool ok = true;
-    for (int n = 0; n < nsteps; ++n) {
-      const int s = n % STAGES;
-      ok = mbar_wait(qdo_full(s), (n / STAGES) & 1, g, 7);
-      ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, n & 1, g, 8));
-      if (!ok) break;
-      tc_fence_after();
-      const float neg_lse = -lse_s[s * 256 + r];
-      const float dl = lse_s[s * 256 + 128 + r];
-      uint32_t pk[32], dsk[32];
-      if (n == 0)
-        bwd_half_row<true>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk);
-      else
-        bwd_half_row<false>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk);
-      if (OVERLAP) {  // every TMEM load of S_n / dP_n has completed
-        tc_fence_before();
-        mbar_arrive(st_empty);
-      }
-      if (n > 0) {  // P/dS tiles and the dS TMEM columns are free once step n-1's MMAs are done
-        ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (n - 1) & 1, g, 10));
+    int gstep = 0, item = 0;
+    for (BwdItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && ok; it.next(), ++item) {
+      int bh, jt;
+      it.get(bh, jt);
+      const int nsteps = nq - jt;
+      for (int n = 0; n < nsteps; ++n, ++gstep) {
+        const int s = gstep % STAGES;
+        ok = mbar_wait(qdo_full(s), (gstep / STAGES) & 1, g, 7);
+        ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, gstep & 1, g, 8));
         if (!ok) break;
         tc_fence_after();
-      }
+        const float neg_lse = -lse_s[s * 256 + r];
+        const float dl = lse_s[s * 256 + 128 + r];
+        uint32_t pk[32], dsk[32];
+        if (n == 0)  // the item's first query tile is the diagonal one
+          bwd_half_row<true>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk);
+        else
+          bwd_half_row<false>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk);
+        if (OVERLAP) {  // every TMEM load of S_g / dP_g has completed
+          tc_fence_before();
+          mbar_arrive(st_empty);
+        }
+        if (gstep > 0) {  // P/dS tiles and the dS TMEM columns are free once step g-1's MMAs are done
+          ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (gstep - 1) & 1, g, 10));
+          if (!ok) break;
+          tc_fence_after();
+        }
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        st_tile_row16(sP, r, 4 * hh + c, pk + 8 * c);
-        st_tile_row16(sDS, r, 4 * hh + c, dsk + 8 * c);
-      }
+        for (int c = 0; c < 4; ++c) {
+          st_tile_row16(sP, r, 4 * hh + c, pk + 8 * c);
+          st_tile_row16(sDS, r, 4 * hh + c, dsk + 8 * c);
+        }
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
-        tmem_st16(lane_base + Cfg::DS_COL + 32 * hh + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(dsk + 16 * c));
-      tmem_st_wait();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(ds_full);
-    }
-    if (ok) {  // every MMA of the walk has completed with the last dq_full
-      ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (nsteps - 1) & 1, g, 11));
-      if (ok) tc_fence_after();
-    }
-    // dK (scaled) and dV for key row r, columns [hh*HD/2, (hh+1)*HD/2).
-    if (ok) {
+        for (int c = 0; c < 2; ++c)
+          tmem_st16(lane_base + Cfg::DS_COL + 32 * hh + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(dsk + 16 * c));
+        tmem_st_wait();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(ds_full);
+      }
+      if (!ok) break;
+      // Item end: every MMA of the item has completed with its last dq_full.
+      ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (gstep - 1) & 1, g, 11));
+      if (!ok) break;
+      tc_fence_after();
+      // dK (scaled) and dV for key row r, columns [hh*HD/2, (hh+1)*HD/2); the
+      // TMEM columns go back to the next item's MMAs (kvacc_empty) once read.
       constexpr int HALF = HD / 2;
       const int b = bh / p.H, h = bh - b * p.H;
       const int t = jt * 128 + r;
-      __nv_bfloat16* dkrow = p.dk + (size_t(row0) + t) * HD + hh * HALF;
+      __nv_bfloat16* dkrow = p.dk + (size_t(bh) * p.T + t) * HD + hh * HALF;
       __nv_bfloat16* dvrow = p.dv + (size_t(b) * p.T + t) * p.ld_dv + size_t(h) * HD + hh * HALF;
 #pragma unroll
       for (int c = 0; c < HALF; c += 16) {
@@ -443,59 +523,67 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
         st_global_v4(dvrow + c, pv[0], pv[1], pv[2], pv[3]);
         st_global_v4(dvrow + c + 8, pv[4], pv[5], pv[6], pv[7]);
       }
+      tc_fence_before();
+      mbar_arrive(kvacc_empty);
     }
     if (!ok) g.ok = false;
     finish();
     return;
   }
   {
-    reg_dealloc<72>();
+    reg_dealloc<64>();
     // ---------------- dQ read-out warps 12..15 ----------------
     // Row r of each finished dQ tile out of TMEM (dq_full), scaled, added into
-    // the fp32 accumulator through the staging tile, 64 columns per round, and
-    // one TMA reduce-add per 32-column box (the lead thread waits for all 128
-    // writers, stg_full, and the tile is reused once the previous reduce-add
-    // has read it, stg_empty).
+    // the fp32 accumulator through the staging tile, DQ_COLS columns per round,
+    // and one TMA reduce-add per 32-column box (the lead thread waits for all
+    // 128 writers, stg_full, and the tile is reused once the previous
+    // reduce-add has read it, stg_empty).
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const bool lead = (warp == 12 && lane == 0);
     const uint32_t stg = base + Cfg::OFF_DQ;
     bool ok = true;
-    for (int k = 0; k < nsteps && ok; ++k) {
-      ok = __all_sync(0xffffffffu, mbar_wait(dq_full, k & 1, g, 9));
-      if (!ok) break;
-      tc_fence_after();
-      constexpr int NC = Cfg::DQ_COLS, NR = Cfg::DQ_ROUNDS;
+    int gstep = 0;
+    for (BwdItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && ok; it.next()) {
+      int bh, jt;
+      it.get(bh, jt);
+      const int nsteps = nq - jt;
+      for (int k = 0; k < nsteps && ok; ++k, ++gstep) {
+        ok = __all_sync(0xffffffffu, mbar_wait(dq_full, gstep & 1, g, 9));
+        if (!ok) break;
+        tc_fence_after();
+        constexpr int NC = Cfg::DQ_COLS, NR = Cfg::DQ_ROUNDS;
 #pragma unroll 1
-      for (int h = 0; h < NR && ok; ++h) {
-        const int rnd = k * NR + h;  // staging-tile round
-        if (rnd > 0) {
+        for (int h = 0; h < NR && ok; ++h) {
+          const int rnd = gstep * NR + h;  // staging-tile round
+          if (rnd > 0) {
+            if (lead) {
+              bulk_wait_read0();
+              mbar_arrive(stg_empty);
+            }
+            ok = __all_sync(0xffffffffu, mbar_wait(stg_empty, (rnd - 1) & 1, g, 13));
+            if (!ok) break;
+          }
+          dq_stage<NC>(lane_base + Cfg::DQ_COL, h * NC, r, stg, p.scale);
+          if (h == NR - 1) {  // every TMEM load of the dQ tile has completed
+            tc_fence_before();
+            mbar_arrive(dq_empty);
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(stg_full);
           if (lead) {
-            bulk_wait_read0();
-            mbar_arrive(stg_empty);
-          }
-          ok = __all_sync(0xffffffffu, mbar_wait(stg_empty, (rnd - 1) & 1, g, 13));
-          if (!ok) break;
-        }
-        dq_stage<NC>(lane_base + Cfg::DQ_COL, h * NC, r, stg, p.scale);
-        if (h == NR - 1) {  // every TMEM load of the dQ tile has completed
-          tc_fence_before();
-          mbar_arrive(dq_empty);
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(stg_full);
-        if (lead) {
-          ok = mbar_wait(stg_full, rnd & 1, g, 14);
-          if (ok) {
-            const int qrow = row0 + (jt + k) * 128;
+            ok = mbar_wait(stg_full, rnd & 1, g, 14);
+            if (ok) {
+              const int qrow = bh * p.T + (jt + k) * 128;
 #pragma unroll
-            for (int bx = 0; bx < NC / 32; ++bx)
-              tma_reduce_add_2d(&maps.dq, stg + bx * 16384, h * NC + bx * 32, qrow);
-            bulk_commit();
+              for (int bx = 0; bx < NC / 32; ++bx)
+                tma_reduce_add_2d(&maps.dq, stg + bx * 16384, h * NC + bx * 32, qrow);
+              bulk_commit();
+            }
           }
+          ok = __all_sync(0xffffffffu, ok);
         }
-        ok = __all_sync(0xffffffffu, ok);
       }
     }
     if (lead) bulk_wait0();  // every reduce-add has landed before the CTA exits
@@ -511,7 +599,9 @@ static int launch_attn_bwd_t(const AttnBwdMaps& maps, const AttnBwdParams& p, cu
   auto kern = attn_bwd_kernel<HD>;
   if (!smem_attr_set(reinterpret_cast<const void*>(kern), int(Cfg::SMEM)))
     return set_error(MEA_ERR_CUDA, "cudaFuncSetAttribute(attn_bwd) failed");
-  const int grid = p.B * p.H * (p.T / 128);
+  // Persistent: one CTA per SM, each striding over pairs of work items.
+  const int pairs = p.B * p.H * ((p.T / 128 + 1) / 2);
+  const int grid = pairs < num_sms() ? pairs : num_sms();
   kern<<<grid, 512, Cfg::SMEM, st>>>(maps, p);
   return check_launch("attn_bwd_kernel");
 }
