@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     mbar_init(st_empty, 256);
     mbar_init(stg_full, 128);
     mbar_init(stg_empty, 1);
-    mbar_init(kvacc_empty, 256);
+    mbar_init(kvacc_empty, 128);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -447,16 +447,15 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     reg_alloc<184>();
     // ---------------- softmax warps 4..11 ----------------
     // Query row r = TMEM lane; warps 4..7 take key columns [0, 64), warps 8..11
-    // [64, 128), so each sub-partition runs two softmax warps.  The same warps
-    // write each item's dK / dV at its end.
+    // [64, 128), so each sub-partition runs two softmax warps.
     const int quarter = warp & 3;
     const int hh = (warp - 4) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
     bool ok = true;
-    int gstep = 0, item = 0;
-    for (BwdItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && ok; it.next(), ++item) {
+    int gstep = 0;
+    for (BwdItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && ok; it.next()) {
       int bh, jt;
       it.get(bh, jt);
       const int nsteps = nq - jt;
@@ -495,36 +494,6 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
         tc_fence_before();
         mbar_arrive(ds_full);
       }
-      if (!ok) break;
-      // Item end: every MMA of the item has completed with its last dq_full.
-      ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (gstep - 1) & 1, g, 11));
-      if (!ok) break;
-      tc_fence_after();
-      // dK (scaled) and dV for key row r, columns [hh*HD/2, (hh+1)*HD/2); the
-      // TMEM columns go back to the next item's MMAs (kvacc_empty) once read.
-      constexpr int HALF = HD / 2;
-      const int b = bh / p.H, h = bh - b * p.H;
-      const int t = jt * 128 + r;
-      __nv_bfloat16* dkrow = p.dk + (size_t(bh) * p.T + t) * HD + hh * HALF;
-      __nv_bfloat16* dvrow = p.dv + (size_t(b) * p.T + t) * p.ld_dv + size_t(h) * HD + hh * HALF;
-#pragma unroll
-      for (int c = 0; c < HALF; c += 16) {
-        uint32_t a[16], v[16];
-        tmem_load16(lane_base + Cfg::DK_COL + hh * HALF + c, a);
-        tmem_load16(lane_base + Cfg::DV_COL + hh * HALF + c, v);
-        uint32_t pa[8], pv[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          pa[j] = pack_bf16(__uint_as_float(a[2 * j]) * p.scale, __uint_as_float(a[2 * j + 1]) * p.scale);
-          pv[j] = pack_bf16(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-        }
-        st_global_v4(dkrow + c, pa[0], pa[1], pa[2], pa[3]);
-        st_global_v4(dkrow + c + 8, pa[4], pa[5], pa[6], pa[7]);
-        st_global_v4(dvrow + c, pv[0], pv[1], pv[2], pv[3]);
-        st_global_v4(dvrow + c + 8, pv[4], pv[5], pv[6], pv[7]);
-      }
-      tc_fence_before();
-      mbar_arrive(kvacc_empty);
     }
     if (!ok) g.ok = false;
     finish();
@@ -532,12 +501,14 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
   }
   {
     reg_dealloc<64>();
-    // ---------------- dQ read-out warps 12..15 ----------------
+    // ---------------- dQ / dK / dV read-out warps 12..15 ----------------
     // Row r of each finished dQ tile out of TMEM (dq_full), scaled, added into
     // the fp32 accumulator through the staging tile, DQ_COLS columns per round,
     // and one TMA reduce-add per 32-column box (the lead thread waits for all
     // 128 writers, stg_full, and the tile is reused once the previous
-    // reduce-add has read it, stg_empty).
+    // reduce-add has read it, stg_empty).  At the end of each work item the
+    // same warps write its dK and dV (key row r) and hand their TMEM columns
+    // to the next item's MMAs (kvacc_empty), off the softmax warps' path.
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
@@ -585,6 +556,30 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
           ok = __all_sync(0xffffffffu, ok);
         }
       }
+      if (!ok) break;
+      // Item end: its last dq_full (waited above) completed every MMA of the item.
+      const int b = bh / p.H, h = bh - b * p.H;
+      const int t = jt * 128 + r;
+      __nv_bfloat16* dkrow = p.dk + (size_t(bh) * p.T + t) * HD;
+      __nv_bfloat16* dvrow = p.dv + (size_t(b) * p.T + t) * p.ld_dv + size_t(h) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 16) {
+        uint32_t a[16];
+        uint32_t pa[8];
+        tmem_load16(lane_base + Cfg::DK_COL + c, a);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          pa[j] = pack_bf16(__uint_as_float(a[2 * j]) * p.scale, __uint_as_float(a[2 * j + 1]) * p.scale);
+        st_global_v4(dkrow + c, pa[0], pa[1], pa[2], pa[3]);
+        st_global_v4(dkrow + c + 8, pa[4], pa[5], pa[6], pa[7]);
+        tmem_load16(lane_base + Cfg::DV_COL + c, a);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) pa[j] = pack_bf16(__uint_as_float(a[2 * j]), __uint_as_float(a[2 * j + 1]));
+        st_global_v4(dvrow + c, pa[0], pa[1], pa[2], pa[3]);
+        st_global_v4(dvrow + c + 8, pa[4], pa[5], pa[6], pa[7]);
+      }
+      tc_fence_before();
+      mbar_arrive(kvacc_empty);
     }
     if (lead) bulk_wait0();  // every reduce-add has landed before the CTA exits
     if (!ok) g.ok = false;
