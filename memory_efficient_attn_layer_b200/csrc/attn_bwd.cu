@@ -57,6 +57,8 @@ struct AttnBwdParams {
 struct AttnBwdMaps {
   CUtensorMap q, k, v, dO;
   CUtensorMap dq;  // dq_acc as [B*H*T, N] fp32, 32x128 boxes, 128-byte swizzle
+  CUtensorMap dk;  // dk as [B*H*T, N] bf16, min(N,64) x 128 boxes
+  CUtensorMap dv;  // dv as [B*T, ld_dv] bf16 (head h at column h*N), min(N,64) x 128 boxes
 };
 
 template <int HD>
@@ -288,7 +290,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     }
   };
   // Register shares per warpgroup (launched with 512 threads x 128 = 65536):
-  // 128 x 80 (TMA/MMA) + 256 x 184 (softmax) + 128 x 64 (dQ) = 65536.  Each role
+  // 128 x 80 (TMA/MMA) + 256 x 176 (softmax) + 128 x 80 (read-out) = 65536.  Each role
   // sets its share first and ends in `finish`, so every role is compiled
   // against its own budget.
   if (warp < 4) {
@@ -444,7 +446,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     return;
   }
   if (warp < 12) {
-    reg_alloc<184>();
+    reg_alloc<176>();
     // ---------------- softmax warps 4..11 ----------------
     // Query row r = TMEM lane; warps 4..7 take key columns [0, 64), warps 8..11
     // [64, 128), so each sub-partition runs two softmax warps.
@@ -500,7 +502,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     return;
   }
   {
-    reg_dealloc<64>();
+    reg_dealloc<80>();
     // ---------------- dQ / dK / dV read-out warps 12..15 ----------------
     // Row r of each finished dQ tile out of TMEM (dq_full), scaled, added into
     // the fp32 accumulator through the staging tile, DQ_COLS columns per round,
@@ -515,6 +517,49 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     const bool lead = (warp == 12 && lane == 0);
     const uint32_t stg = base + Cfg::OFF_DQ;
     bool ok = true;
+    // Staging-tile rounds (dQ column blocks, then each item's dK and dV): a round
+    // starts once the previous round's TMA op has read the tile (stg_empty) and
+    // its op is issued by the lead thread once all 128 writers are done (stg_full).
+    int rnd = 0;
+    auto stage_begin = [&]() -> bool {
+      if (rnd > 0) {
+        if (lead) {
+          bulk_wait_read0();
+          mbar_arrive(stg_empty);
+        }
+        return __all_sync(0xffffffffu, mbar_wait(stg_empty, (rnd - 1) & 1, g, 13));
+      }
+      return true;
+    };
+    auto stage_end = [&](auto&& issue) -> bool {
+      fence_proxy_async_smem();
+      mbar_arrive(stg_full);
+      bool okk = true;
+      if (lead) {
+        okk = mbar_wait(stg_full, rnd & 1, g, 14);
+        if (okk) {
+          issue();
+          bulk_commit();
+        }
+      }
+      ++rnd;
+      return __all_sync(0xffffffffu, okk);
+    };
+    // bf16 tile row r, columns [c, c+16) (packed pairs in w[0..7]) into the staging
+    // tile in the swizzled layout of the dK / dV tensor maps (boxes of 64 columns).
+    auto stage_bf16 = [&](int c, const uint32_t* w) {
+      constexpr int BW = HD < 64 ? HD : 64;  // box width (elements)
+      const uint32_t box = stg + (c / BW) * (128 * BW * 2);
+#pragma unroll
+      for (int u2 = 0; u2 < 2; ++u2) {
+        const int u = ((c % BW) >> 3) + u2;
+        const uint32_t addr = BW == 64 ? box + r * 128 + ((u ^ (r & 7)) << 4)
+                                       : box + r * 64 + ((u ^ ((r >> 1) & 3)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(w[4 * u2]), "r"(w[4 * u2 + 1]),
+                     "r"(w[4 * u2 + 2]), "r"(w[4 * u2 + 3])
+                     : "memory");
+      }
+    };
     int gstep = 0;
     for (BwdItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && ok; it.next()) {
       int bh, jt;
@@ -525,61 +570,61 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
         if (!ok) break;
         tc_fence_after();
         constexpr int NC = Cfg::DQ_COLS, NR = Cfg::DQ_ROUNDS;
+        const int qrow = bh * p.T + (jt + k) * 128;
 #pragma unroll 1
         for (int h = 0; h < NR && ok; ++h) {
-          const int rnd = gstep * NR + h;  // staging-tile round
-          if (rnd > 0) {
-            if (lead) {
-              bulk_wait_read0();
-              mbar_arrive(stg_empty);
-            }
-            ok = __all_sync(0xffffffffu, mbar_wait(stg_empty, (rnd - 1) & 1, g, 13));
-            if (!ok) break;
-          }
+          if (!(ok = stage_begin())) break;
           dq_stage<NC>(lane_base + Cfg::DQ_COL, h * NC, r, stg, p.scale);
           if (h == NR - 1) {  // every TMEM load of the dQ tile has completed
             tc_fence_before();
             mbar_arrive(dq_empty);
           }
-          fence_proxy_async_smem();
-          mbar_arrive(stg_full);
-          if (lead) {
-            ok = mbar_wait(stg_full, rnd & 1, g, 14);
-            if (ok) {
-              const int qrow = bh * p.T + (jt + k) * 128;
+          ok = stage_end([&] {
 #pragma unroll
-              for (int bx = 0; bx < NC / 32; ++bx)
-                tma_reduce_add_2d(&maps.dq, stg + bx * 16384, h * NC + bx * 32, qrow);
-              bulk_commit();
-            }
-          }
-          ok = __all_sync(0xffffffffu, ok);
+            for (int bx = 0; bx < NC / 32; ++bx)
+              tma_reduce_add_2d(&maps.dq, stg + bx * 16384, h * NC + bx * 32, qrow);
+          });
         }
       }
       if (!ok) break;
       // Item end: its last dq_full (waited above) completed every MMA of the item.
+      // dK (scaled) and dV go out through the staging tile by TMA; their TMEM
+      // columns go to the next item's MMAs (kvacc_empty) once read.
       const int b = bh / p.H, h = bh - b * p.H;
-      const int t = jt * 128 + r;
-      __nv_bfloat16* dkrow = p.dk + (size_t(bh) * p.T + t) * HD;
-      __nv_bfloat16* dvrow = p.dv + (size_t(b) * p.T + t) * p.ld_dv + size_t(h) * HD;
+      constexpr int BW = HD < 64 ? HD : 64;
 #pragma unroll 1
-      for (int c = 0; c < HD; c += 16) {
-        uint32_t a[16];
-        uint32_t pa[8];
-        tmem_load16(lane_base + Cfg::DK_COL + c, a);
+      for (int which = 0; which < 2 && ok; ++which) {
+        if (!(ok = stage_begin())) break;
+        const uint32_t col = which ? Cfg::DV_COL : Cfg::DK_COL;
+        const float sc = which ? 1.0f : p.scale;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t a0[16], a1[16];
+          tmem_ld16(lane_base + col + c, a0);
+          tmem_ld16(lane_base + col + c + 16, a1);
+          tmem_wait_ld_tied2(a0, a1);
+          uint32_t w[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          pa[j] = pack_bf16(__uint_as_float(a[2 * j]) * p.scale, __uint_as_float(a[2 * j + 1]) * p.scale);
-        st_global_v4(dkrow + c, pa[0], pa[1], pa[2], pa[3]);
-        st_global_v4(dkrow + c + 8, pa[4], pa[5], pa[6], pa[7]);
-        tmem_load16(lane_base + Cfg::DV_COL + c, a);
+          for (int j = 0; j < 8; ++j) w[j] = pack_bf16(__uint_as_float(a0[2 * j]) * sc, __uint_as_float(a0[2 * j + 1]) * sc);
+          stage_bf16(c, w);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) pa[j] = pack_bf16(__uint_as_float(a[2 * j]), __uint_as_float(a[2 * j + 1]));
-        st_global_v4(dvrow + c, pa[0], pa[1], pa[2], pa[3]);
-        st_global_v4(dvrow + c + 8, pa[4], pa[5], pa[6], pa[7]);
+          for (int j = 0; j < 8; ++j) w[j] = pack_bf16(__uint_as_float(a1[2 * j]) * sc, __uint_as_float(a1[2 * j + 1]) * sc);
+          stage_bf16(c + 16, w);
+        }
+        if (which) {
+          tc_fence_before();
+          mbar_arrive(kvacc_empty);
+        }
+        ok = stage_end([&] {
+#pragma unroll
+          for (int bx = 0; bx < HD / BW; ++bx) {
+            if (which)
+              tma_store_2d(&maps.dv, stg + bx * (128 * BW * 2), h * HD + bx * BW, b * p.T + jt * 128);
+            else
+              tma_store_2d(&maps.dk, stg + bx * (128 * BW * 2), bx * BW, bh * p.T + jt * 128);
+          }
+        });
       }
-      tc_fence_before();
-      mbar_arrive(kvacc_empty);
     }
     if (lead) bulk_wait0();  // every reduce-add has landed before the CTA exits
     if (!ok) g.ok = false;
@@ -610,6 +655,8 @@ int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, cons
     return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "attention backward: T=%d must be a positive multiple of 128", T);
   if ((reinterpret_cast<uintptr_t>(lse2) | reinterpret_cast<uintptr_t>(delta)) & 15)
     return set_error(MEA_ERR_ALIGNMENT, "attention backward: lse/delta must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15 || ld_dv % 8 || ld_dv < (long long)H * HD)
+    return set_error(MEA_ERR_ALIGNMENT, "attention backward: dk/dv must be 16-byte aligned, ld_dv a multiple of 8 >= H*N");
   const uint64_t rows = uint64_t(B) * H * T;
   const int swb = HD * 2 >= 128 ? 128 : HD * 2;
   const int box_inner = swb / 2;
@@ -621,6 +668,10 @@ int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, cons
   rc |= make_tmap_2d(&maps.dO, dO, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
   rc |= make_tmap_2d(&maps.dq, dq_acc, HD, rows, uint64_t(HD) * 4, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+  const uint32_t bw = HD < 64 ? uint32_t(HD) : 64u;
+  rc |= make_tmap_2d(&maps.dk, dk, HD, rows, uint64_t(HD) * 2, bw, 128, swizzle_for(bw * 2));
+  rc |= make_tmap_2d(&maps.dv, dv, uint64_t(H) * HD, uint64_t(B) * T, uint64_t(ld_dv) * 2, bw, 128,
+                     swizzle_for(bw * 2));
   if (rc) return set_error(MEA_ERR_CUDA, "attention backward: tensor map encode failed");
   AttnBwdParams p;
   p.B = B;
