@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     }
   };
   // Register shares per warpgroup (launched with 512 threads x 128 = 65536):
-  // 128 x 80 (TMA/MMA) + 256 x 176 (softmax) + 128 x 80 (read-out) = 65536.  Each role
+  // 128 x 80 (TMA/MMA) + 256 x 168 (softmax) + 128 x 96 (read-out) = 65536.  Each role
   // sets its share first and ends in `finish`, so every role is compiled
   // against its own budget.
   if (warp < 4) {
@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     return;
   }
   if (warp < 12) {
-    reg_alloc<176>();
+    reg_alloc<168>();
     // ---------------- softmax warps 4..11 ----------------
     // Query row r = TMEM lane; warps 4..7 take key columns [0, 64), warps 8..11
     // [64, 128), so each sub-partition runs two softmax warps.
@@ -502,7 +502,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     return;
   }
   {
-    reg_dealloc<80>();
+    reg_dealloc<96>();
     // ---------------- dQ / dK / dV read-out warps 12..15 ----------------
     // Row r of each finished dQ tile out of TMEM (dq_full), scaled, added into
     // the fp32 accumulator through the staging tile, DQ_COLS columns per round,
@@ -571,13 +571,41 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
         tc_fence_after();
         constexpr int NC = Cfg::DQ_COLS, NR = Cfg::DQ_ROUNDS;
         const int qrow = bh * p.T + (jt + k) * 128;
-#pragma unroll 1
+        // N <= 64: the whole dQ tile goes to registers first, so its TMEM columns
+        // return to the next dQ MMA (dq_empty) before the staging rounds.
+        uint32_t v[OVERLAP ? HD / 16 : 1][16];
+        if constexpr (OVERLAP) {
+#pragma unroll
+          for (int c = 0; c < HD / 16; ++c) tmem_ld16(lane_base + Cfg::DQ_COL + 16 * c, v[c]);
+#pragma unroll
+          for (int c = 0; c < HD / 16; c += 2) tmem_wait_ld_tied2(v[c], v[c + 1]);
+          tc_fence_before();
+          mbar_arrive(dq_empty);
+        }
+#pragma unroll
         for (int h = 0; h < NR && ok; ++h) {
           if (!(ok = stage_begin())) break;
-          dq_stage<NC>(lane_base + Cfg::DQ_COL, h * NC, r, stg, p.scale);
-          if (h == NR - 1) {  // every TMEM load of the dQ tile has completed
-            tc_fence_before();
-            mbar_arrive(dq_empty);
+          if constexpr (OVERLAP) {
+#pragma unroll
+            for (int c = 0; c < NC; c += 16) {
+              const uint32_t* vv = v[(h * NC + c) / 16];
+              const uint32_t row = stg + (c >> 5) * 16384 + r * 128;
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int unit = ((c & 31) >> 2) + u;
+                asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(row + ((unit ^ (r & 7)) << 4)),
+                             "f"(__uint_as_float(vv[4 * u]) * p.scale), "f"(__uint_as_float(vv[4 * u + 1]) * p.scale),
+                             "f"(__uint_as_float(vv[4 * u + 2]) * p.scale),
+                             "f"(__uint_as_float(vv[4 * u + 3]) * p.scale)
+                             : "memory");
+              }
+            }
+          } else {
+            dq_stage<NC>(lane_base + Cfg::DQ_COL, h * NC, r, stg, p.scale);
+            if (h == NR - 1) {  // every TMEM load of the dQ tile has completed
+              tc_fence_before();
+              mbar_arrive(dq_empty);
+            }
           }
           ok = stage_end([&] {
 #pragma unroll
