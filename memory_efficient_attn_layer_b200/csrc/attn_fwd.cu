@@ -54,6 +54,9 @@ struct AttnFwdParams {
 
 struct AttnFwdMaps {
   CUtensorMap q, k, v;
+  // (N <= 64) epilogue: sigmoid(g) tile in ([B*H*T, N], 128-row box), gated out
+  // ([B*T, H*N], 32-row boxes), O out ([B*H*T, N], 32-row boxes)
+  CUtensorMap gs, gated, o;
 };
 
 template <int HD>
@@ -221,7 +224,9 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
   // [0, 64), s_full_b / s_empty_b for [64, 128)
   const uint32_t s_full_b = s_full + 48;
   const uint32_t s_empty_b = s_full + 56;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9 + 2 * KS + 2 * VS);
+  const uint32_t q_free = s_full + 64;  // (SEP_P) the last score MMA has read Q
+  const uint32_t gs_bar = s_full + 72;  // (SEP_P) sigmoid(g) tile landed in Q's buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11 + 2 * KS + 2 * VS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -253,6 +258,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     mbar_init(pv_done, 1);
     mbar_init(s_full_b, 1);
     mbar_init(s_empty_b, 128);
+    mbar_init(q_free, 1);
+    mbar_init(gs_bar, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -340,6 +347,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
           tc_fence_after();
           issue_half(0, 0);
           issue_half(0, 1);
+          if (nkv == 1) mma_commit(q_free);
           any = true;
           for (int j = 0; j < nkv; ++j) {
             const int sv = j % VS;
@@ -351,6 +359,13 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
               if (!mbar_wait(s_empty_b, j & 1, g, 16)) break;
               tc_fence_after();
               issue_half(j + 1, 1);
+              if (j + 2 == nkv) mma_commit(q_free);
+            } else {
+              // Q is no longer read: bring the tile's sigmoid(g) into its buffer for
+              // the epilogue while the last softmax tile runs.
+              if (!mbar_wait(q_free, 0, g, 19)) break;
+              mbar_expect_tx(gs_bar, TB);
+              tma_load_2d(sQ, &maps.gs, gs_bar, 0, row0 + qt * 128);
             }
             if (!mbar_wait(p_full, j & 1, g, 3)) break;
             if (!mbar_wait(v_full(sv), (j / VS) & 1, g, 4)) break;
@@ -531,6 +546,60 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       mbar_arrive(p_full);
     }
     // ---- epilogue: O / l, gate, repack ----
+    if constexpr (Cfg::SEP_P) {
+      // The sigmoid(g) tile is in Q's buffer (gs_bar); each warp writes its 32
+      // rows of gated and O into the first K / V slots (free after the last S and
+      // PV MMAs) in the tensor maps' swizzle and stores them by TMA.
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_bar, 0, g, 8));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkv - 1) & 1, g, 15));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(gs_bar, 0, g, 20));
+      if (ok) {
+        tc_fence_after();
+        const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+        if (mode != 0) m_run = ref;
+        const float inv_l = mode == 2 ? 1.0f : 1.0f / l_run;
+        constexpr int ROWB = Tile::SWB;  // bytes per tile row (HD <= 64: one swizzle chunk)
+        auto unit = [&](uint32_t tile, int u) -> uint32_t {
+          return ROWB == 128 ? tile + r * 128 + ((u ^ (r & 7)) << 4) : tile + r * 64 + ((u ^ ((r >> 1) & 3)) << 4);
+        };
+#pragma unroll
+        for (int c = 0; c < HD; c += 16) {
+          uint32_t ov[16];
+          tmem_load16(lane_base + Cfg::O_COL + c, ov);
+#pragma unroll
+          for (int u2 = 0; u2 < 2; ++u2) {
+            const int u = c / 8 + u2;
+            uint32_t gw[4];
+            asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(gw[0]), "=r"(gw[1]), "=r"(gw[2]), "=r"(gw[3])
+                         : "r"(unit(sQ, u)) : "memory");
+            uint32_t go[4], oo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float o0 = __uint_as_float(ov[8 * u2 + 2 * e]) * inv_l;
+              const float o1 = __uint_as_float(ov[8 * u2 + 2 * e + 1]) * inv_l;
+              go[e] = pack_bf16(o0 * bf16_lo(gw[e]), o1 * bf16_hi(gw[e]));
+              oo[e] = pack_bf16(o0, o1);
+            }
+            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(unit(sK, u)), "r"(go[0]), "r"(go[1]), "r"(go[2]),
+                         "r"(go[3]) : "memory");
+            if (p.o_out)
+              asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(unit(sV, u)), "r"(oo[0]), "r"(oo[1]),
+                           "r"(oo[2]), "r"(oo[3]) : "memory");
+          }
+        }
+        if (p.lse2) p.lse2[bht] = m_run + __log2f(l_run);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t box = uint32_t(quarter * 32 * ROWB);
+          tma_store_2d(&maps.gated, sK + box, h * HD, b * p.T + qt * 128 + quarter * 32);
+          if (p.o_out) tma_store_2d(&maps.o, sV + box, 0, row0 + qt * 128 + quarter * 32);
+          bulk_commit();
+          bulk_wait0();
+        }
+        __syncwarp();
+      }
+    } else {
     // sigmoid(g) of this row is fetched while the last PV completes.
     uint4 gv[HD / 8];
     if (ok) {
@@ -538,9 +607,6 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       for (int c = 0; c < HD / 8; ++c) gv[c] = __ldg(reinterpret_cast<const uint4*>(p.gs + bht * HD) + c);
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_bar, 0, g, 8));
-    if constexpr (Cfg::SEP_P) {  // the last PV's own completion arrive, before the CTA can exit
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkv - 1) & 1, g, 15));
-    }
     if (ok) {
       tc_fence_after();
       const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
@@ -570,6 +636,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         }
       }
       if (p.lse2) p.lse2[bht] = m_run + __log2f(l_run);
+    }
     }
     if (!ok) g.ok = false;
   }
@@ -607,6 +674,11 @@ int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, cons
   int rc = make_tmap_2d(&maps.q, q, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
   rc |= make_tmap_2d(&maps.k, k, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
   rc |= make_tmap_2d(&maps.v, v, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
+  if (HD <= 64) {
+    rc |= make_tmap_2d(&maps.gs, gs, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
+    rc |= make_tmap_2d(&maps.gated, gated, uint64_t(H) * HD, uint64_t(B) * T, uint64_t(H) * HD * 2, box_inner, 32, sw);
+    rc |= make_tmap_2d(&maps.o, o_out ? o_out : gated, HD, rows, uint64_t(HD) * 2, box_inner, 32, sw);
+  }
   if (rc) return set_error(MEA_ERR_CUDA, "attention: tensor map encode failed");
   AttnFwdParams p;
   p.B = B;
