@@ -446,12 +446,14 @@ int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq
                status, st));
   // The recompute takes the forward's LSE as its exp2 reference: P comes out
   // normalised, the same P the attention backward rebuilds.
+  // (N <= 64: the recompute also clears the dQ accumulator; otherwise a memset does.)
+  const bool zero_in_fwd = d->N <= 64;
   MEA_STAGE(ST_BWD_ATTN_FWD, run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated,
-                       nullptr, ws + w.o, nullptr, lse2, status, st));
+                       nullptr, ws + w.o, nullptr, lse2, status, st, zero_in_fwd ? dqacc : nullptr));
   {
     StageScope scope_(ST_BWD_MEMSET, st);
     MEA_TRY(memset_async(dw32, size_t(5) * HN * C * 4, st));
-    MEA_TRY(memset_async(dqacc, BHTN * 4, st));
+    if (!zero_in_fwd) MEA_TRY(memset_async(dqacc, BHTN * 4, st));
     MEA_TRY(memset_async(dfactor1, size_t(d->T_max) * d->N * 4, st));
     MEA_TRY(memset_async(dfactor2, size_t(d->T_max) * d->N * 4, st));
   }

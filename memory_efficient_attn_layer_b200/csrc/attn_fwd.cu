@@ -49,6 +49,7 @@ struct AttnFwdParams {
   __nv_bfloat16* o_out;     // optional [B,H,T,N]
   const float* bound;       // optional device scalar: bound on every scaled score (log2 units)
   const float* lse_in;      // optional saved lse2: normalised recompute
+  float* dq_zero;           // optional fp32 [B,H,T,N] cleared by the epilogue (N <= 64)
   int* status;
 };
 
@@ -57,6 +58,7 @@ struct AttnFwdMaps {
   // (N <= 64) epilogue: sigmoid(g) tile in ([B*H*T, N], 128-row box), gated out
   // ([B*T, H*N], 32-row boxes), O out ([B*H*T, N], 32-row boxes)
   CUtensorMap gs, gated, o;
+  CUtensorMap dqz;  // (N <= 64) dq_zero as [B*H*T, N] fp32, 32-column x 32-row boxes
 };
 
 template <int HD>
@@ -590,10 +592,25 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         if (p.lse2) p.lse2[bht] = m_run + __log2f(l_run);
         fence_proxy_async_smem();
         __syncwarp();
+        if (p.dq_zero) {
+          // Zero rows for the backward's dQ accumulator: a 32-row x 128-byte zero
+          // tile per warp in the free second K / V slots, stored HD/32 times.
+          const uint32_t zb = (quarter < 2 ? sK : sV) + TB + uint32_t((quarter & 1) * 4096);
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            asm volatile("st.shared.v4.b32 [%0], {%1,%1,%1,%1};" ::"r"(zb + lane * 128 + u * 16), "r"(0u) : "memory");
+          fence_proxy_async_smem();
+        }
+        __syncwarp();
         if (lane == 0) {
           const uint32_t box = uint32_t(quarter * 32 * ROWB);
           tma_store_2d(&maps.gated, sK + box, h * HD, b * p.T + qt * 128 + quarter * 32);
           if (p.o_out) tma_store_2d(&maps.o, sV + box, 0, row0 + qt * 128 + quarter * 32);
+          if (p.dq_zero)
+#pragma unroll
+            for (int c = 0; c < HD; c += 32)
+              tma_store_2d(&maps.dqz, (quarter < 2 ? sK : sV) + TB + uint32_t((quarter & 1) * 4096), c,
+                           row0 + qt * 128 + quarter * 32);
           bulk_commit();
           bulk_wait0();
         }
@@ -661,7 +678,10 @@ static int launch_attn_fwd_t(const AttnFwdMaps& maps, const AttnFwdParams& p, cu
 }
 
 int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* gs, void* gated,
-                 float* lse2, void* o_out, const float* bound, const float* lse_in, int* status, cudaStream_t st) {
+                 float* lse2, void* o_out, const float* bound, const float* lse_in, int* status, cudaStream_t st,
+                 float* dq_zero) {
+  if (dq_zero && HD > 64)
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "attention: dQ clearing is built for head dims <= 64");
   if (HD != 32 && HD != 64 && HD != 128)
     return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "attention: head dim %d not in {32, 64, 128}", HD);
   if (T % 128 != 0 || T <= 0 || B <= 0 || H <= 0)
@@ -678,6 +698,9 @@ int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, cons
     rc |= make_tmap_2d(&maps.gs, gs, HD, rows, uint64_t(HD) * 2, box_inner, 128, sw);
     rc |= make_tmap_2d(&maps.gated, gated, uint64_t(H) * HD, uint64_t(B) * T, uint64_t(H) * HD * 2, box_inner, 32, sw);
     rc |= make_tmap_2d(&maps.o, o_out ? o_out : gated, HD, rows, uint64_t(HD) * 2, box_inner, 32, sw);
+    if (dq_zero)
+      rc |= make_tmap_2d(&maps.dqz, dq_zero, HD, rows, uint64_t(HD) * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
   }
   if (rc) return set_error(MEA_ERR_CUDA, "attention: tensor map encode failed");
   AttnFwdParams p;
@@ -690,6 +713,7 @@ int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, cons
   p.o_out = static_cast<__nv_bfloat16*>(o_out);
   p.bound = lse_in ? nullptr : bound;
   p.lse_in = lse_in;
+  p.dq_zero = dq_zero;
   p.lse2 = lse_in ? nullptr : lse2;
   p.status = status;
   switch (HD) {

@@ -53,10 +53,13 @@ int auto_splits(int m_tiles, int n_tiles, int kb_total, int waves);
 // Reference for the exponentials: `lse_in` (the saved row log-sum-exp; O comes
 // out normalised and lse2 is not written), else `*bound` when it is at most
 // ATTN_MAX_BOUND (a device scalar bounding every scaled score), else the
-// online running max.  Both pointers may be NULL.
+// online running max.  Both pointers may be NULL.  `dq_zero` (fp32 [B,H,T,N],
+// may be NULL; head dim <= 64 only) is zeroed by the kernel's epilogue: the
+// backward's dQ accumulator, cleared while the recompute runs.
 constexpr float ATTN_MAX_BOUND = 50.f;
 int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* gs, void* gated,
-                 float* lse2, void* o_out, const float* bound, const float* lse_in, int* status, cudaStream_t st);
+                 float* lse2, void* o_out, const float* bound, const float* lse_in, int* status, cudaStream_t st,
+                 float* dq_zero = nullptr);
 int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
                  const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv, int* status,
                  cudaStream_t st);
