@@ -130,10 +130,12 @@ def test_attention_forward(N, T, mag):
     assert maxrel(gated.float(), want) < 2e-2, "gated output"
 
 
-@pytest.mark.parametrize("N", [32, 64, 128])
-@pytest.mark.parametrize("T", [128, 384])
-def test_attention_backward(N, T):
-    B, H = 2, 2
+@pytest.mark.parametrize("B,H,T,N", [(2, 2, T, N) for N in (32, 64, 128) for T in (128, 384)]
+                         + [(32, 8, 512, 64), (16, 4, 640, 128)])
+def test_attention_backward(B, H, T, N):
+    """The persistent backward walks pairs of key tiles (k, nq-1-k); the last two
+    cases give every CTA several pairs of mixed lengths (K/V buffers reused
+    across items, odd nq with a single middle tile)."""
     q = bf16(unit_rms(rnd(B, H, T, N, seed=30)))
     k = bf16(unit_rms(rnd(B, H, T, N, seed=31)))
     v = bf16(rnd(B, H, T, N, seed=32))
