@@ -237,6 +237,84 @@ def reference_triton_block():
     return fast_triton_attn.fused_attn
 
 
+# --------------------------------------------------------------------------- model level
+def run_stack(args, cfg, device):
+    """The block's caller at model level (README.md:1, "-1GB of memory usage" on a 50M model): a stack of
+    `--stack L` pre-norm residual layers x += attn(x) ; x += mlp(norm(x)) with a 4C ReLU^2 MLP, every
+    layer's attention through `--impl` (ours / triton / eager) and the same MLP (torch).  Prints one
+    JSON line with model-level fwd+bwd tokens/s and peak activation memory (not a bench line of the
+    block metric)."""
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    from memory_efficient_attn_layer_b200 import CausalSoftmaxAttention, Yarn
+
+    B, T, C, H, N = (cfg[k] for k in ("B", "T", "C", "H", "N"))
+    L = args.stack
+    torch.manual_seed(0)
+    attn = nn.ModuleList([CausalSoftmaxAttention(C, H, N) for _ in range(L)]).to(device=device, dtype=torch.bfloat16)
+    for blk in attn:  # o_proj zero-init (README.md:35) would cut the gradient path: give it values
+        nn.init.uniform_(blk.o_proj.weight, -0.5 / math.sqrt(H * N), 0.5 / math.sqrt(H * N))
+    up = nn.ModuleList([nn.Linear(C, 4 * C, bias=False) for _ in range(L)]).to(device=device, dtype=torch.bfloat16)
+    down = nn.ModuleList([nn.Linear(4 * C, C, bias=False) for _ in range(L)]).to(device=device, dtype=torch.bfloat16)
+    yarn = Yarn(N, T, device=device)
+    ref_fused = reference_triton_block() if args.impl == "triton" else None
+    if args.impl == "triton" and ref_fused is None:
+        print(json.dumps({"impl": "triton", "unavailable": "baseline/_ref/fast_triton_attn.py not installed"}))
+        return
+
+    def attention(l, h):
+        blk = attn[l]
+        if args.impl == "triton":
+            return ref_fused(h, blk.q_proj, blk.k_proj, blk.v_proj, blk.g_proj, blk.o_proj, yarn, H, N)
+        if args.impl == "eager":
+            ws = [blk.q_proj.weight, blk.k_proj.weight, blk.v_proj.weight, blk.g_proj.weight, blk.o_proj.weight]
+            return eager_block(h, ws, yarn, H, N)
+        return blk(h, yarn)
+
+    def model(h):
+        for l in range(L):
+            h = h + attention(l, h)
+            h = h + down[l](F.relu(up[l](F.rms_norm(h, (C,), eps=1e-6))).square())
+        return h
+
+    g = torch.Generator(device=device).manual_seed(1000)
+    x = torch.randn(B, T, C, device=device, generator=g).to(torch.bfloat16)
+    dy = torch.randn(B, T, C, device=device, generator=g).to(torch.bfloat16)
+    params = sum(p.numel() for m in (attn, up, down) for p in m.parameters())
+
+    def step():
+        y = model(x.detach().requires_grad_(True))
+        y.backward(dy)
+        for m in (attn, up, down):
+            for p in m.parameters():
+                p.grad = None
+
+    step()
+    torch.cuda.synchronize(device)
+    torch.cuda.reset_peak_memory_stats(device)
+    m0 = torch.cuda.memory_allocated(device)
+    step()
+    torch.cuda.synchronize(device)
+    peak = torch.cuda.max_memory_allocated(device) - m0
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize(device)
+    ms = t0.elapsed_time(t1) / args.steps
+    print(json.dumps({
+        "impl": args.impl, "metric": "model fwd+bwd tokens/s (stack of the block + MLP)", "value": B * T / (ms / 1e3),
+        "unit": "tokens/s", "ms_per_step": ms, "layers": L, "params": params, "tokens_per_step": B * T,
+        "peak_activation_gb": peak / 1e9, "config": {"workload": cfg["name"], "layer": "x += attn(x); x += "
+                                                     "mlp(rmsnorm(x)), mlp = W2 relu(W1 x)^2, 4C hidden"},
+    }), flush=True)
+
+
 def run_gpu(args, cfg, rank, world, device):
     import torch.distributed as dist
 
@@ -468,6 +546,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0,
                     help="per-GPU batch override (smaller cases for profiler captures; not a bench line)")
+    ap.add_argument("--stack", type=int, default=0,
+                    help="model-level mode: a stack of this many block + MLP layers (memory and tokens/s of the "
+                         "caller; one GPU; not a bench line)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -490,6 +571,11 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     try:
+        if args.stack > 0:
+            if world > 1:
+                raise SystemExit("--stack runs on one GPU")
+            run_stack(args, cfg, device)
+            return
         run_gpu(args, cfg, rank, world, device)
     finally:
         if world > 1:
