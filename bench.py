@@ -102,21 +102,51 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
+        self.rows = []  # (arrival time, fields)
+        self.thread = None
+        self.window = None
 
     def start(self):
+        """Starts sampling (call before the warm-up steps: nvidia-smi takes a moment to come up)."""
+        import threading
+
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True, bufsize=1)
         except OSError:
             self.proc = None
+            return
+
+        def reader():
+            for line in self.proc.stdout:
+                if line.count(",") >= 8:
+                    self.rows.append((time.time(), line.strip().split(",")))
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+
+    def mark(self, t0, t1):
+        """Host wall-clock bounds of the timed region (after device synchronisation)."""
+        self.window = (t0, t1)
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
-        out, _ = self.proc.communicate(timeout=10)
-        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        try:
+            self.proc.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        rows = [r for _, r in self.rows]
+        used = "warm-up + timed steps"
+        if self.window is not None:
+            t0, t1 = self.window
+            inside = [r for t, r in self.rows if t0 <= t <= t1 + 0.25]
+            if len(inside) >= 2:
+                rows, used = inside, "timed steps"
         sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -127,7 +157,7 @@ class ClockSampler:
                     reasons.add(name)
         load = sorted(sm)[len(sm) // 4:] if sm else []  # drop ramp-up samples
         return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+                "reasons": sorted(reasons), "samples": len(rows), "window": used}
 
 
 # --------------------------------------------------------------------------- inputs
@@ -380,6 +410,8 @@ def run_gpu(args, cfg, rank, world, device):
         w.grad = None
 
     # ---- device-timed steps (inputs resident in HBM; x is 2*B*T*C bytes > L2)
+    clocks = ClockSampler(device.index if device.index is not None else 0)
+    clocks.start()  # sampling spans warm-up and timed steps; the timed window is marked below
     for _ in range(args.warmup):
         step(x, dy)
     if world > 1:
@@ -387,14 +419,14 @@ def run_gpu(args, cfg, rank, world, device):
     torch.cuda.synchronize(device)
     if not eager:
         _lib.profile_enable(True)
-    clocks = ClockSampler(device.index if device.index is not None else 0)
-    clocks.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
     ev0.record()
     for _ in range(args.steps):
         step(x, dy)
     ev1.record()
     torch.cuda.synchronize(device)
+    clocks.mark(t_wall0, time.time())
     ms = ev0.elapsed_time(ev1)
     if world > 1:
         dist.barrier()
