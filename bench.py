@@ -107,28 +107,41 @@ class ClockSampler:
         self.window = None
 
     def start(self):
-        """Starts sampling (call before the warm-up steps: nvidia-smi takes a moment to come up)."""
+        """Starts sampling early (nvidia-smi takes up to a second to come up).  Its output goes to a
+        pseudo-terminal, so every sample line arrives (and is time-stamped) as it is taken."""
+        import pty
         import threading
 
         try:
+            master, slave = pty.openpty()
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True, bufsize=1)
+                 "-lms", "200"], stdout=slave, stderr=subprocess.DEVNULL, close_fds=True)
+            os.close(slave)
         except OSError:
             self.proc = None
             return
 
         def reader():
-            for line in self.proc.stdout:
-                if line.count(",") >= 8:
-                    self.rows.append((time.time(), line.strip().split(",")))
+            try:
+                with os.fdopen(master, "r", buffering=1, errors="replace") as f:
+                    for line in f:
+                        if line.count(",") >= 8:
+                            self.rows.append((time.time(), line.strip().split(",")))
+            except OSError:  # the terminal closes when nvidia-smi exits
+                pass
 
         self.thread = threading.Thread(target=reader, daemon=True)
         self.thread.start()
 
-    def mark(self, t0, t1):
-        """Host wall-clock bounds of the timed region (after device synchronisation)."""
+    def in_window(self, t0, t1):
+        return sum(1 for t, _ in self.rows if t0 <= t <= t1)
+
+    def mark(self, t0, t1, extended=False):
+        """Host wall-clock bounds of the timed region (after device synchronisation); `extended` when
+        the same steps kept running after it to collect samples."""
         self.window = (t0, t1)
+        self.extended = extended
 
     def stop(self):
         if self.proc is None:
@@ -146,7 +159,8 @@ class ClockSampler:
             t0, t1 = self.window
             inside = [r for t, r in self.rows if t0 <= t <= t1 + 0.25]
             if len(inside) >= 2:
-                rows, used = inside, "timed steps"
+                rows = inside
+                used = "timed steps + the same steps continued" if getattr(self, "extended", False) else "timed steps"
         sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -353,12 +367,15 @@ def run_gpu(args, cfg, rank, world, device):
 
     B, T, C, H, N = (cfg[k] for k in ("B", "T", "C", "H", "N"))
     tokens_rank = B * T
+    clocks = ClockSampler(device.index if device.index is not None else 0)
+    clocks.start()  # samples are kept for the timed window only (marked below)
     x, ws, yarn, dy = make_block_inputs(cfg, device, rank)
     eager = args.impl in ("eager", "triton")  # comparators: no library profiler
     ref_fused = None
     if args.impl == "triton":
         ref_fused = reference_triton_block()
         if ref_fused is None:
+            clocks.stop()
             if rank == 0:
                 print(json.dumps({"impl": "triton", "unavailable": "baseline/_ref/fast_triton_attn.py not installed"}))
             return
@@ -410,8 +427,6 @@ def run_gpu(args, cfg, rank, world, device):
         w.grad = None
 
     # ---- device-timed steps (inputs resident in HBM; x is 2*B*T*C bytes > L2)
-    clocks = ClockSampler(device.index if device.index is not None else 0)
-    clocks.start()  # sampling spans warm-up and timed steps; the timed window is marked below
     for _ in range(args.warmup):
         step(x, dy)
     if world > 1:
@@ -426,15 +441,29 @@ def run_gpu(args, cfg, rank, world, device):
         step(x, dy)
     ev1.record()
     torch.cuda.synchronize(device)
-    clocks.mark(t_wall0, time.time())
+    t_wall1 = time.time()
     ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        dist.barrier()
-    clk = clocks.stop()
     stages = {}
     if not eager:
         stages = _lib.profile_read()
         _lib.profile_enable(False)
+    # A short timed region can end before nvidia-smi has taken two samples in it: then the same steps
+    # keep running (untimed, at most 2 s) until it has, and the clocks cover that span too.
+    # Every rank runs the same number of these steps (their collectives must pair up).
+    while True:
+        need = clocks.proc is not None and clocks.in_window(t_wall0, time.time()) < 2 and time.time() - t_wall1 < 2.0
+        if world > 1:
+            f = torch.tensor([1 if need else 0], device=device, dtype=torch.int32)
+            dist.all_reduce(f, op=dist.ReduceOp.MAX)
+            need = bool(f.item())
+        if not need:
+            break
+        step(x, dy)
+        torch.cuda.synchronize(device)
+    clocks.mark(t_wall0, time.time(), extended=time.time() - t_wall1 > 0.01)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
     if world > 1:
         t = torch.tensor([ms], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
