@@ -393,19 +393,44 @@ def run_gpu(args, cfg, rank, world, device):
             return eager_block(inp, ws, yarn, H, N)
         return FusedAttentionFunction.apply(inp, *ws, yarn.factor1, yarn.factor2, H, N, 1e-6)
 
+    # --optim: the step ends with the sharded AdamW update (reduce-scatter of the fp32 weight gradients the
+    # backward hands over directly, the fused update kernel on this rank's shard, all-gather of the bf16
+    # weights) instead of an all-reduce.
+    opt, opt_ev = None, []
+    if args.optim:
+        if eager:
+            raise SystemExit("--optim runs with --impl ours")
+        from memory_efficient_attn_layer_b200.optim import ShardedAdamW
+
+        opt = ShardedAdamW(ws, lr=1e-4, weight_decay=1e-2)
+
     # Our block exchanges its weight gradients inside its own backward (the
     # all-reduce of each part starts as soon as the library marks it final);
     # the comparators exchange theirs after the backward.
-    overlap = world > 1 and not eager
+    overlap = world > 1 and not eager and opt is None
 
     def exchange_ctx():
         return overlap_grad_allreduce() if overlap else contextlib.nullcontext()
 
-    def step(inp, grad):
+    def opt_step(timed=False):
+        if not timed:
+            opt.step()
+            return
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        opt.step()
+        b.record()
+        opt_ev.append((a, b))
+
+    def step(inp, grad, timed=False):
+        if opt is not None:
+            opt.zero_grad()
         with exchange_ctx():
             y = fwd(inp)
             y.backward(grad)
-        if world > 1 and not overlap:
+        if opt is not None:
+            opt_step(timed)
+        elif world > 1 and not overlap:
             allreduce_grads(ws)
         for w in ws:
             w.grad = None
@@ -438,7 +463,7 @@ def run_gpu(args, cfg, rank, world, device):
     t_wall0 = time.time()
     ev0.record()
     for _ in range(args.steps):
-        step(x, dy)
+        step(x, dy, timed=True)
     ev1.record()
     torch.cuda.synchronize(device)
     t_wall1 = time.time()
@@ -500,12 +525,16 @@ def run_gpu(args, cfg, rank, world, device):
         if i + 1 < n:
             e2e_copy(i + 1)
         comp.wait_event(copied[b])
+        if opt is not None:
+            opt.zero_grad()
         with exchange_ctx():
             y = fwd(xbuf[b])
             loss = (y * dybuf[b]).sum(dtype=torch.float32)
             loss.backward()
         consumed[b].record(comp)
-        if world > 1 and not overlap:
+        if opt is not None:
+            opt.step()
+        elif world > 1 and not overlap:
             allreduce_grads(ws)
         for w in ws:
             w.grad = None
@@ -544,7 +573,12 @@ def run_gpu(args, cfg, rank, world, device):
         "config": {"workload": cfg["name"], "B_per_gpu": B, "global_batch": B * world, "T": T, "C": C, "H": H,
                    "N": N, "parallelism": f"dp{world}" if world > 1 else "single",
                    "grad_exchange": ("nccl all-reduce overlapped with the backward" if overlap else
-                                     "nccl all-reduce after the backward") if world > 1 else None,
+                                     "nccl reduce-scatter + all-gather around the sharded AdamW step"
+                                     if opt is not None else "nccl all-reduce after the backward")
+                   if world > 1 else None,
+                   "optimizer": ("ShardedAdamW in every step: fp32 weight gradients straight from the backward, "
+                                 "reduce-scatter, fused AdamW kernel on this rank's shard, all-gather of the "
+                                 "bf16 weights") if opt is not None else None,
                    "l2": f"inputs larger than L2 (x is {2 * B * T * C / 1e6:.0f} MB per GPU), no flush"},
     }
     if eager:
@@ -583,6 +617,17 @@ def run_gpu(args, cfg, rank, world, device):
                                 "unit": "GB/s", "frac": ach / peaks["hbm_gbs"], "traffic": traffic,
                                 "peak_source": peaks["source"]}
         line["gpu_launches"] = sum(cnt * LAUNCHES_PER_STAGE.get(n, 1) for n, (_, cnt) in stages.items())
+        if opt is not None:
+            line["gpu_launches"] += args.steps  # one mea_adamw_step kernel per step
+    if opt is not None:
+        o_ms = sum(a.elapsed_time(b) for a, b in opt_ev) / len(opt_ev)
+        n_shard = opt.layout.shard
+        o_bytes = 30 * n_shard  # fp32 w, m, v, g read (16 B); w, m, v written (12 B); bf16 w written (2 B)
+        line["optimizer"] = {"ms_per_step": o_ms, "share_of_step": o_ms / ms_step, "weights": opt.layout.numel,
+                             "shard": n_shard, "update_bytes": o_bytes,
+                             "update_gbs_upper_bound": o_bytes / (o_ms / 1e3) / 1e9,
+                             "note": "ms_per_step spans opt.step() (at N>1 the reduce-scatter and all-gather too); "
+                                     "the GB/s figure divides the update kernel's bytes by that whole span"}
     line["e2e"] = {"value": e2e_value, "unit": "tokens/s",
                    "h2d_bytes_per_step": world * (x.numel() * x.element_size() + dy.numel() * dy.element_size()),
                    "d2h_bytes_per_step": world * 4,
@@ -607,6 +652,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0,
                     help="per-GPU batch override (smaller cases for profiler captures; not a bench line)")
+    ap.add_argument("--optim", action="store_true",
+                    help="end every step with the ShardedAdamW update (reduce-scatter, fused AdamW kernel, "
+                         "all-gather) instead of the gradient all-reduce")
     ap.add_argument("--stack", type=int, default=0,
                     help="model-level mode: a stack of this many block + MLP layers (memory and tokens/s of the "
                          "caller; one GPU; not a bench line)")

@@ -161,6 +161,20 @@ int mea_attention_backward_noalloc(int B, int H, int T, int N, const void* q, co
                                    const void* dO, const float* lse2, const float* delta, void* dq, void* dk,
                                    void* dv, long long ld_dv, int* status, void* stream);
 
+/* ---------------------------------------------------------------- optimizer
+ * No counterpart in the reference, whose module (README.md:6-68) leaves the
+ * weight update to the caller's optimizer.  One AdamW step, in the order
+ * torch.optim.AdamW applies it (decoupled weight decay, bias-corrected
+ * moments, step counted from 1), over n contiguous fp32 master weights and
+ * their two moments, all updated in place, with g = grad * grad_scale.  When
+ * param_bf16 is non-NULL it receives bf16(master) after the update.  This is
+ * the step a data-parallel trainer runs on its own shard between the
+ * reduce-scatter of the gradients and the all-gather of the weights.  fp32
+ * buffers 16-byte aligned, param_bf16 8-byte aligned. */
+int mea_adamw_step(long long n, float* master, float* exp_avg, float* exp_avg_sq, const float* grad,
+                   void* param_bf16, double lr, double beta1, double beta2, double eps, double weight_decay,
+                   float grad_scale, int step, void* stream);
+
 /* ---------------------------------------------------------------- profiling
  * No counterpart in the reference (it has no timing hooks).  When enabled,
  * mea_block_forward / mea_block_backward record CUDA events on the caller's

@@ -8,6 +8,7 @@ names and call surface; the work runs in hand-written tcgen05/TMA kernels in
 from .dp import allreduce_grads, overlap_grad_allreduce
 from .fused_attn import FusedAttentionFunction, fused_attn
 from .module import CausalSoftmaxAttention, Yarn
+from .optim import ShardedAdamW
 
 __all__ = ["fused_attn", "FusedAttentionFunction", "CausalSoftmaxAttention", "Yarn", "allreduce_grads",
-           "overlap_grad_allreduce"]
+           "overlap_grad_allreduce", "ShardedAdamW"]

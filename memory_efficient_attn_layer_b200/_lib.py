@@ -32,6 +32,7 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _LL = ctypes.c_longlong
 _F = ctypes.c_float
+_DB = ctypes.c_double
 _S = ctypes.c_size_t
 _D = ctypes.POINTER(MeaBlockDims)
 
@@ -57,6 +58,7 @@ SIGNATURES = {
     "mea_qk_norm_rope_backward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P, _P]),
     "mea_rmsnorm_backward": (_I, [_I, _I, _P, _P, _P, _P, _P]),
     "mea_attention_backward_noalloc": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P]),
+    "mea_adamw_step": (_I, [_LL, _P, _P, _P, _P, _P, _DB, _DB, _DB, _DB, _DB, _F, _I, _P]),
     "mea_profile_enable": (_I, [_I]),
     "mea_profile_read": (_I, [_I, ctypes.POINTER(_F), ctypes.POINTER(_I)]),
     "mea_profile_stage_name": (ctypes.c_char_p, [_I]),

@@ -577,6 +577,13 @@ int mea_rmsnorm_backward(int rows, int C, const void* dxn, const void* x, const 
   return run_rmsnorm_bwd(rows, C, dxn, x, r, dx, static_cast<cudaStream_t>(stream));
 }
 
+int mea_adamw_step(long long n, float* master, float* exp_avg, float* exp_avg_sq, const float* grad,
+                   void* param_bf16, double lr, double beta1, double beta2, double eps, double weight_decay,
+                   float grad_scale, int step, void* stream) {
+  return run_adamw(n, master, exp_avg, exp_avg_sq, grad, param_bf16, lr, beta1, beta2, eps, weight_decay, grad_scale,
+                   step, static_cast<cudaStream_t>(stream));
+}
+
 int mea_profile_enable(int on) {
   std::lock_guard<std::mutex> lock(g_prof.mu);
   for (auto& r : g_prof.recs) {

@@ -74,4 +74,9 @@ int run_cast_f32_bf16(long long n, const float* src, void* dst, cudaStream_t st)
 // *out = bound (log2 units) on every scaled score q.k/sqrt(N) of the block.
 int run_rope_bound(int T, int HD, const void* f1, const void* f2, long long ldf, float* out, cudaStream_t st);
 
+// ---- optimizer (optim.cu) ----
+int run_adamw(long long n, float* master, float* exp_avg, float* exp_avg_sq, const float* grad, void* param,
+              double lr, double beta1, double beta2, double eps, double weight_decay, float grad_scale, int step,
+              cudaStream_t st);
+
 }  // namespace mea

@@ -24,6 +24,7 @@ Two ways to run it:
 from __future__ import annotations
 
 import contextlib
+import weakref
 from typing import Callable, Iterable, Optional
 
 import torch
@@ -116,3 +117,27 @@ def overlap_grad_allreduce(group: Optional[dist.ProcessGroup] = None, average: b
         yield _ACTIVE
     finally:
         _ACTIVE = prev
+
+
+_SINKS: list = []
+
+
+def register_grad_sink(sink) -> None:
+    """Registers an object whose ``claim_block_grads(weights)`` may take the
+    fp32 weight gradients of a block backward (the sharded optimizer); held by
+    weak reference."""
+    _SINKS.append(weakref.ref(sink))
+
+
+def grad_sink_for(weights) -> Optional[tuple]:
+    """(fp32 destination [5·H·N·C], fresh) from the first registered sink that
+    owns these five weights (q, k, v, g, o), else None."""
+    for ref in list(_SINKS):
+        sink = ref()
+        if sink is None:
+            _SINKS.remove(ref)
+            continue
+        got = sink.claim_block_grads(weights)
+        if got is not None:
+            return got
+    return None

@@ -85,7 +85,6 @@ class FusedAttentionFunction(torch.autograd.Function):
         L = _lib.lib()
         dims = _dims(x, H, N, factor1, eps)
         dx = torch.empty_like(x)
-        dws = [torch.empty_like(w) for w in (wq, wk, wv, wg, wo)]
         want_df = ctx.needs_input_grad[6] or ctx.needs_input_grad[7]
         df1 = torch.empty(factor1.shape, dtype=torch.float32, device=x.device) if want_df else None
         df2 = torch.empty(factor2.shape, dtype=torch.float32, device=x.device) if want_df else None
@@ -94,8 +93,21 @@ class FusedAttentionFunction(torch.autograd.Function):
         status = _lib.status_buffer(x.device)
         args = (ctypes.byref(dims), _lib.ptr(x), _lib.ptr(wq), _lib.ptr(wk), _lib.ptr(wv), _lib.ptr(wg),
                 _lib.ptr(wo), _lib.ptr(factor1), _lib.ptr(factor2), _lib.ptr(lse), _lib.ptr(dy), _lib.ptr(dx))
+        sink = _dp.grad_sink_for((wq, wk, wv, wg, wo)) if all(ctx.needs_input_grad[1:6]) else None
         ex = ctx.exchange
-        if ex is None:
+        dws = None if sink is not None else [torch.empty_like(w) for w in (wq, wk, wv, wg, wo)]
+        if sink is not None:
+            # The sharded optimizer owns these weights: fp32 gradients go straight
+            # into its buffer (added when it already holds this step's gradient).
+            dst, fresh = sink
+            out = dst if fresh else torch.empty_like(dst)
+            _lib.check(L.mea_block_backward_ex(
+                *args, None, None, None, None, None, _lib.ptr(df1), _lib.ptr(df2), _lib.ptr(out), _lib.ptr(ws),
+                ws_bytes, _lib.ptr(status), _lib.stream_ptr(x.device), None, None))
+            if not fresh:
+                dst.add_(out)
+            dws = [None] * 5
+        elif ex is None:
             _lib.check(L.mea_block_backward(
                 *args, *[_lib.ptr(d) for d in dws], _lib.ptr(df1), _lib.ptr(df2), None, _lib.ptr(ws), ws_bytes,
                 _lib.ptr(status), _lib.stream_ptr(x.device)))
