@@ -4,6 +4,8 @@
 // All are one pass over HBM with 16-byte vector accesses.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "launch.h"
 #include "ptx.cuh"
 
@@ -43,6 +45,65 @@ __global__ void rmsnorm_fwd_kernel(int rows, int C, float eps, const __nv_bfloat
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[e] = pack_bf16(bf16_lo(w[e]) * r, bf16_hi(w[e]) * r);
     st_global_v4(yr + c, o[0], o[1], o[2], o[3]);
+  }
+}
+
+// The same for C = 256*V (V 16-byte pieces per lane and row): rows taken
+// grid-stride two at a time, every piece of both rows loaded before any is
+// used and kept in registers for the xn store, so x is read from HBM once
+// with 32*V bytes per lane in flight.  Same arithmetic, in the same order, as
+// rmsnorm_fwd_kernel.
+template <int V>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_rows_kernel(int rows, float eps, const __nv_bfloat16* __restrict__ x,
+                                                               __nv_bfloat16* __restrict__ xn, float* __restrict__ rout) {
+  constexpr int C = 256 * V;
+  const int lane = threadIdx.x & 31;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  for (int row0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row0 < rows; row0 += 2 * nw) {
+    const int row1 = row0 + nw;
+    const bool two = row1 < rows;
+    uint4 v[2][V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[0][i] = __ldg(reinterpret_cast<const uint4*>(x + size_t(row0) * C + 256 * i + lane * 8));
+    if (two) {
+#pragma unroll
+      for (int i = 0; i < V; ++i)
+        v[1][i] = __ldg(reinterpret_cast<const uint4*>(x + size_t(row1) * C + 256 * i + lane * 8));
+    }
+    float ss[2] = {0.f, 0.f};
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const uint32_t w[4] = {v[q][i].x, v[q][i].y, v[q][i].z, v[q][i].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a = bf16_lo(w[e]), b = bf16_hi(w[e]);
+          ss[q] = fmaf(a, a, fmaf(b, b, ss[q]));
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], o);
+      ss[1] += __shfl_xor_sync(0xffffffffu, ss[1], o);
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (q == 1 && !two) break;
+      const int row = q ? row1 : row0;
+      const float r = rsqrtf(ss[q] / float(C) + eps);
+      if (rout && lane == 0) rout[row] = r;
+      if (!xn) continue;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const uint32_t w[4] = {v[q][i].x, v[q][i].y, v[q][i].z, v[q][i].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = pack_bf16(bf16_lo(w[e]) * r, bf16_hi(w[e]) * r);
+        st_global_v4(xn + size_t(row) * C + 256 * i + lane * 8, o[0], o[1], o[2], o[3]);
+      }
+    }
   }
 }
 
@@ -332,8 +393,34 @@ int run_rope_bound(int T, int HD, const void* f1, const void* f2, long long ldf,
   return check_launch("rope_bound_kernel");
 }
 
+template <int V>
+static int rmsnorm_fwd_rows(int rows, float eps, const void* x, void* xn, float* r, cudaStream_t st) {
+  const int threads = 256;
+  static int resident = 0;  // CTAs per SM at this kernel's register count
+  if (!resident) {
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, rmsnorm_fwd_rows_kernel<V>, threads, 0) != cudaSuccess || nb < 1)
+      nb = 1;
+    resident = nb;
+  }
+  const long long want = ((long long)rows + 15) / 16;  // 8 warps of two rows
+  const int blocks = int(std::max<long long>(1, std::min<long long>(want, (long long)num_sms() * resident)));
+  rmsnorm_fwd_rows_kernel<V><<<blocks, threads, 0, st>>>(rows, eps, static_cast<const __nv_bfloat16*>(x),
+                                                         static_cast<__nv_bfloat16*>(xn), r);
+  return check_launch("rmsnorm_fwd_rows_kernel");
+}
+
 int run_rmsnorm_fwd(int rows, int C, float eps, const void* x, void* xn, float* r, cudaStream_t st) {
   if (C % 8 || C <= 0 || rows <= 0) return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "rmsnorm: C=%d must be a multiple of 8", C);
+  switch (C) {
+    case 256: return rmsnorm_fwd_rows<1>(rows, eps, x, xn, r, st);
+    case 512: return rmsnorm_fwd_rows<2>(rows, eps, x, xn, r, st);
+    case 768: return rmsnorm_fwd_rows<3>(rows, eps, x, xn, r, st);
+    case 1024: return rmsnorm_fwd_rows<4>(rows, eps, x, xn, r, st);
+    case 1536: return rmsnorm_fwd_rows<6>(rows, eps, x, xn, r, st);
+    case 2048: return rmsnorm_fwd_rows<8>(rows, eps, x, xn, r, st);
+    default: break;
+  }
   const int threads = 256;
   const int blocks = (rows * 32 + threads - 1) / threads;
   rmsnorm_fwd_kernel<<<blocks, threads, 0, st>>>(rows, C, eps, static_cast<const __nv_bfloat16*>(x),

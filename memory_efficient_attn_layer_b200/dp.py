@@ -20,6 +20,12 @@ Two ways to run it:
   caller's stream waits for the exchange only where the backward returns.  The
   gradients handed back to autograd are already the group mean (or sum), so
   ``allreduce_grads`` must not be called for those weights as well.
+
+A third way replaces the exchange: ``optim.ShardedAdamW`` registers itself as
+a gradient sink (``register_grad_sink``).  A block whose five weights it owns
+writes its fp32 weight gradients straight into the optimizer's buffer, and the
+optimizer reduce-scatters them in ``step()``.  The sink takes precedence over
+an enclosing ``overlap_grad_allreduce``.
 """
 from __future__ import annotations
 

@@ -37,7 +37,8 @@ def _worker(rank, world, port, average, q):
     try:
         params = _grads_for(rank)
         allreduce_grads(params, average=average)
-        q.put((rank, [p.grad.float() if p.grad is not None else None for p in params]))
+        # numpy arrays travel by value: a torch tensor would be fetched from this process after it exits
+        q.put((rank, [p.grad.float().numpy() if p.grad is not None else None for p in params]))
     finally:
         dist.destroy_process_group()
 
@@ -51,7 +52,8 @@ def test_allreduce_grads_two_ranks(average):
     procs = [ctx.Process(target=_worker, args=(r, world, port, average, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=120) for _ in range(world))
+    results = {r: [None if a is None else torch.from_numpy(a) for a in v]
+               for r, v in (q.get(timeout=120) for _ in range(world))}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -78,7 +80,7 @@ def _reduce_worker(rank, world, port, average, q):
         reduce_weight_grads(buf, 4 * 12, average=average, before_qkvg=lambda: marks.append("qkvg"))
         with overlap_grad_allreduce(average=average) as ex:
             tagged = active_exchange() is ex
-        q.put((rank, buf, marks, tagged))
+        q.put((rank, buf.numpy(), marks, tagged))
     finally:
         dist.destroy_process_group()
 
@@ -94,7 +96,7 @@ def test_reduce_weight_grads_two_ranks(average):
     procs = [ctx.Process(target=_reduce_worker, args=(r, world, port, average, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = {r: rest for r, *rest in (q.get(timeout=120) for _ in range(world))}
+    results = {r: [torch.from_numpy(b), *rest] for r, b, *rest in (q.get(timeout=120) for _ in range(world))}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

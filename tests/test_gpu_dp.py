@@ -66,7 +66,8 @@ def _rank(rank, world, port, overlap, q):
             leaves = _weight_grads(inp, dev, rank * per, (rank + 1) * per)
             allreduce_grads(leaves, average=False)
         torch.cuda.synchronize(dev)
-        q.put((rank, [w.grad.float().cpu() for w in leaves]))
+        # numpy arrays travel by value: a torch tensor would be fetched from this process after it exits
+        q.put((rank, [w.grad.float().cpu().numpy() for w in leaves]))
     finally:
         dist.destroy_process_group()
 
@@ -82,7 +83,7 @@ def test_dp_two_ranks_match_full_batch(overlap):
     procs = [ctx.Process(target=_rank, args=(r, world, port, overlap, q)) for r in range(world)]
     for p in procs:
         p.start()
-    got = dict(q.get(timeout=300) for _ in range(world))
+    got = {r: [torch.from_numpy(a) for a in v] for r, v in (q.get(timeout=300) for _ in range(world))}
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0

@@ -59,8 +59,10 @@ def test_gemm_split_k_accumulate():
 
 
 # ------------------------------------------------------------------ RMSNorm
-def test_rmsnorm_forward():
-    rows, C = 512, 384
+@pytest.mark.parametrize("rows,C", [(512, 384), (512, 256), (4097, 512), (3001, 768), (515, 1024), (333, 2048)])
+def test_rmsnorm_forward(rows, C):
+    # C = 384: the one-row-per-warp loop; the others: the row-batched kernel (odd row counts leave the
+    # last warp with one row)
     x = bf16(rnd(rows, C, scale=3.0, seed=5))
     xn = torch.empty_like(x)
     r = torch.empty(rows, device=DEV)
@@ -68,6 +70,10 @@ def test_rmsnorm_forward():
     rr = torch.rsqrt(x.float().pow(2).mean(-1) + EPS)
     assert maxrel(r, rr) < 1e-5
     assert maxrel(xn.float(), x.float() * rr[:, None]) < 8e-3
+    assert torch.equal(xn, (x.float() * r[:, None]).to(torch.bfloat16))
+    r_only = torch.full((rows,), float("nan"), device=DEV)
+    call("mea_rmsnorm_forward", rows, C, EPS, P(x), None, P(r_only), stream())
+    assert torch.equal(r_only, r)  # the forward (r only) and the recompute (r and x_n) agree bit for bit
 
 
 def test_rmsnorm_backward():

@@ -155,7 +155,8 @@ def _rank(rank, world, port, q):
                             device_id=dev)
     try:
         per = 4 // world
-        q.put((rank, _train(dev, rank * per, (rank + 1) * per, 3)))
+        # numpy arrays travel by value: a torch tensor would be fetched from this process after it exits
+        q.put((rank, [w.numpy() for w in _train(dev, rank * per, (rank + 1) * per, 3)]))
     finally:
         dist.destroy_process_group()
 
@@ -170,7 +171,7 @@ def test_sharded_adamw_two_ranks_match_one_gpu():
     procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    got = dict(q.get(timeout=300) for _ in range(world))
+    got = {r: [torch.from_numpy(a) for a in v] for r, v in (q.get(timeout=300) for _ in range(world))}
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0

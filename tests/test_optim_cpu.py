@@ -135,7 +135,8 @@ def _worker(rank, world, port, q):
         v = np.zeros_like(master)
         new = adamw_step(master, m, v, gshard.numpy(), step=1, grad_scale=1.0 / world, **HP)
         lay.all_gather(torch.from_numpy(new).to(torch.bfloat16))
-        q.put((rank, lay.flat.float().clone(), [p.detach().float().clone() for p in ps]))
+        # numpy arrays travel by value: a torch tensor would be fetched from this process after it exits
+        q.put((rank, lay.flat.float().numpy(), [p.detach().float().numpy() for p in ps]))
     finally:
         dist.destroy_process_group()
 
@@ -151,7 +152,7 @@ def test_two_rank_reduce_scatter_step_all_gather():
     got = {}
     for _ in range(world):
         r, flat, ps = q.get(timeout=120)
-        got[r] = (flat, ps)
+        got[r] = (torch.from_numpy(flat), [torch.from_numpy(p) for p in ps])
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
