@@ -95,9 +95,12 @@ def test_block_forward_is_deterministic():
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("B,T,C,H,N", [(128, 2048, 512, 8, 64), (32, 4096, 1024, 8, 128)])
+@pytest.mark.parametrize("B,T,C,H,N", [(128, 2048, 512, 8, 64), (32, 4096, 1024, 8, 128), (128, 2048, 768, 12, 64),
+                                       (4, 4096, 2048, 16, 128)])
 def test_block_full_size_single_sequence_gradient(B, T, C, H, N):
-    """Baseline-size shapes (configs 2 and 3).  The upstream gradient is non-zero
+    """Baseline-size shapes: configs 2, 3 and 5 in full, and config 4's block
+    (B=4, C=2048, H=16, N=128) at T=4096 (the fp32 oracle materialises the
+    T x T scores; at T=16384 they alone take 17 GB).  The upstream gradient is non-zero
     for sequence 0 only, so (a) y[0], dx[0] and every weight gradient must equal
     the oracle run on sequence 0 alone, and (b) dx of every other sequence must
     be exactly zero: a size-independent check of the batch independence."""
