@@ -148,7 +148,13 @@ class ShardedAdamW(torch.optim.Optimizer):
     over its own batch shard); otherwise the sum.  ``fused_grads``: accept the
     block backward's fp32 weight gradients directly (their ``.grad`` stays
     None).  The weights must start identical on every rank; the first rank's
-    are broadcast at construction."""
+    are broadcast at construction.
+
+    Every ``step()`` updates every managed weight: a weight that received no
+    gradient since ``zero_grad()`` is stepped with a zero gradient (its moments
+    decay and weight decay applies), where torch.optim.AdamW would skip it.
+    Under data parallelism every rank must call ``step()`` the same number of
+    times, as for any collective."""
 
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-3, betas=(0.9, 0.999),
                  eps: float = 1e-8, weight_decay: float = 1e-2, group=None, average: bool = True,
