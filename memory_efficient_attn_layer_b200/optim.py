@@ -26,7 +26,6 @@ is added in at ``step()``.  ``zero_grad()`` clears both.
 """
 from __future__ import annotations
 
-import ctypes
 from typing import Iterable, Optional
 
 import torch
