@@ -75,6 +75,15 @@ struct AttnBwdCfg {
   static constexpr uint32_t DQ_COL = OVERLAP ? DK_COL + HD : DP_COL;
   static constexpr uint32_t TMEM_COLS = 512;
   static_assert(!OVERLAP || DQ_COL + HD <= 512, "TMEM budget");
+  // Registers per thread of each warpgroup after setmaxnreg (launched with 512
+  // threads x 128 = 65536): 128 x REG_TMA_MMA + 256 x REG_SOFTMAX + 128 x
+  // REG_READOUT = 65536.  At N = 128 the TMA/MMA warps' serial-schedule loop
+  // needs more than 80 (it spilled to local memory there), the softmax warps
+  // fit in 152.
+  static constexpr int REG_TMA_MMA = HD >= 128 ? 112 : 80;
+  static constexpr int REG_SOFTMAX = HD >= 128 ? 152 : 168;
+  static constexpr int REG_READOUT = 96;
+  static_assert(128 * REG_TMA_MMA + 256 * REG_SOFTMAX + 128 * REG_READOUT == 512 * 128, "register split");
   static constexpr uint32_t OFF_KV = 0;  // buffer b: K at OFF_KV + 2*TB*b, V right after it
   static constexpr uint32_t OFF_Q = KV_BUFS * 2 * TB, OFF_DO = OFF_Q + STAGES * TB;
   static constexpr uint32_t OFF_P = OFF_DO + STAGES * TB, OFF_DS = OFF_P + PT;
@@ -289,12 +298,11 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
       tmem_dealloc(tmem, Cfg::TMEM_COLS);
     }
   };
-  // Register shares per warpgroup (launched with 512 threads x 128 = 65536):
-  // 128 x 80 (TMA/MMA) + 256 x 168 (softmax) + 128 x 96 (read-out) = 65536.  Each role
-  // sets its share first and ends in `finish`, so every role is compiled
-  // against its own budget.
+  // Register shares per warpgroup: Cfg::REG_* (sum 65536).  Each role sets its
+  // share first and ends in `finish`, so every role is compiled against its own
+  // budget.
   if (warp < 4) {
-    reg_dealloc<80>();
+    reg_dealloc<Cfg::REG_TMA_MMA>();
     if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (elect_one()) {
@@ -446,7 +454,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     return;
   }
   if (warp < 12) {
-    reg_alloc<168>();
+    reg_alloc<Cfg::REG_SOFTMAX>();
     // ---------------- softmax warps 4..11 ----------------
     // Query row r = TMEM lane; warps 4..7 take key columns [0, 64), warps 8..11
     // [64, 128), so each sub-partition runs two softmax warps.
@@ -502,7 +510,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     return;
   }
   {
-    reg_dealloc<96>();
+    reg_dealloc<Cfg::REG_READOUT>();
     // ---------------- dQ / dK / dV read-out warps 12..15 ----------------
     // Row r of each finished dQ tile out of TMEM (dq_full), scaled, added into
     // the fp32 accumulator through the staging tile, DQ_COLS columns per round,
