@@ -237,9 +237,12 @@ __device__ __forceinline__ void epi_f32(const GemmMaps& maps, uint32_t taddr, ui
 //   out[n] = qn[n]*f1[t,n] + qn[n^1]*f2[t,n]      (fast_triton_attn.py:102-106, :132-141)
 // with the rotary-table row read from the quarter's table tile.  `rs` is the
 // row's input-norm scale (1 when the GEMM input is already normalised).
-template <int HD>
+// EARLY (HD <= 64, the slab is the warp's last TMEM read of the tile): hand the
+// accumulator back (release_acc on acce_cl) as soon as the slab is in registers.
+template <int HD, bool EARLY = false>
 __device__ __forceinline__ void qk_slab(const GemmParams& p, uint32_t tcol, uint32_t slab, uint32_t tab, int lane,
-                                        int typ, float rs, size_t bht, bool valid) {
+                                        int typ, float rs, size_t bht, bool valid, uint32_t acce_cl = 0) {
+  static_assert(!EARLY || HD <= 64, "early release needs the whole slab in registers");
   constexpr int NCH = HD / 32;
   constexpr uint32_t TAB_BYTES = 32 * HD * 2;
   uint32_t v[HD <= 64 ? NCH : 1][32];
@@ -252,6 +255,7 @@ __device__ __forceinline__ void qk_slab(const GemmParams& p, uint32_t tcol, uint
     } else {
       tmem_wait_ld_tied(v[0]);
     }
+    if constexpr (EARLY) release_acc(acce_cl, lane);
 #pragma unroll
     for (int ci = 0; ci < NCH; ++ci)
 #pragma unroll
@@ -309,27 +313,51 @@ __device__ __forceinline__ void qk_slab(const GemmParams& p, uint32_t tcol, uint
 }
 
 // v slab (stored as is, fast_triton_attn.py:108) or g slab (sigmoid, :123).
+// 32 columns of one slab chunk from registers into the staging slab.
 template <int HD>
-__device__ __forceinline__ void vg_slab(uint32_t tcol, uint32_t slab, int lane, bool sig, float rs) {
-#pragma unroll 1
-  for (int ci = 0; ci < HD / 32; ++ci) {
-    uint32_t w[32];
-    tmem_load32(tcol + 32 * ci, w);
+__device__ __forceinline__ void vg_chunk(const uint32_t (&w)[32], int ci, uint32_t slab, int lane, bool sig, float rs) {
 #pragma unroll
-    for (int j4 = 0; j4 < 4; ++j4) {
-      uint32_t pk[4];
+  for (int j4 = 0; j4 < 4; ++j4) {
+    uint32_t pk[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int j = 8 * j4 + 2 * e;
-        float a = __uint_as_float(w[j]) * rs;
-        float b = __uint_as_float(w[j + 1]) * rs;
-        if (sig) {
-          a = __fdividef(1.0f, 1.0f + __expf(-a));
-          b = __fdividef(1.0f, 1.0f + __expf(-b));
-        }
-        pk[e] = pack_bf16(a, b);
+    for (int e = 0; e < 4; ++e) {
+      const int j = 8 * j4 + 2 * e;
+      float a = __uint_as_float(w[j]) * rs;
+      float b = __uint_as_float(w[j + 1]) * rs;
+      if (sig) {
+        a = __fdividef(1.0f, 1.0f + __expf(-a));
+        b = __fdividef(1.0f, 1.0f + __expf(-b));
       }
-      sts_v4(hd_unit<HD>(slab, lane, 4 * ci + j4), pk);
+      pk[e] = pack_bf16(a, b);
+    }
+    sts_v4(hd_unit<HD>(slab, lane, 4 * ci + j4), pk);
+  }
+}
+// EARLY (HD <= 64): the whole slab is loaded first and the accumulator handed
+// back (release_acc on acce_cl) before the stores, as in qk_slab.
+template <int HD, bool EARLY = false>
+__device__ __forceinline__ void vg_slab(uint32_t tcol, uint32_t slab, int lane, bool sig, float rs,
+                                        uint32_t acce_cl = 0) {
+  if constexpr (EARLY) {
+    static_assert(HD <= 64, "early release needs the whole slab in registers");
+    constexpr int NCH = HD / 32;
+    uint32_t v[NCH][32];
+    tmem_ld32(tcol, v[0]);
+    if constexpr (NCH == 2) {
+      tmem_ld32(tcol + 32, v[NCH - 1]);
+      tmem_wait_ld_tied2x32(v[0], v[NCH - 1]);
+    } else {
+      tmem_wait_ld_tied(v[0]);
+    }
+    release_acc(acce_cl, lane);
+#pragma unroll
+    for (int ci = 0; ci < NCH; ++ci) vg_chunk<HD>(v[ci], ci, slab, lane, sig, rs);
+  } else {
+#pragma unroll 1
+    for (int ci = 0; ci < HD / 32; ++ci) {
+      uint32_t w[32];
+      tmem_load32(tcol + 32 * ci, w);
+      vg_chunk<HD>(w, ci, slab, lane, sig, rs);
     }
   }
 }
@@ -344,6 +372,10 @@ __device__ __forceinline__ void epi_qkvg(const GemmMaps& maps, const GemmParams&
   constexpr int G = HD >= 128 ? 2 : 4;  // warp groups splitting the slabs (GemmCfg::QK_GROUPS)
   constexpr int NJ = BN / HD / G;
   constexpr uint32_t SLAB_BYTES = 32 * HD * 2;
+  // One slab per warp and tile (BN = 256, HD = 64): the slab's TMEM loads are the
+  // warp's last reads of the accumulator, so it is handed back to the MMA issuer
+  // right after them, before the norm / rotary / sigmoid math and the stores.
+  constexpr bool EARLY = NJ == 1 && HD <= 64;
   const int b = mq / p.T;
   const int tq = mq - b * p.T;  // token of lane 0
   const int m = mq + lane;
@@ -364,16 +396,16 @@ __device__ __forceinline__ void epi_qkvg(const GemmMaps& maps, const GemmParams&
         any_qk = true;
       }
       const size_t bht = (size_t(b) * p.H + (sg >> 2)) * p.T + tq + lane;
-      qk_slab<HD>(p, taddr + s * HD, stg + j * SLAB_BYTES, tab, lane, typ, rs, bht, valid);
+      qk_slab<HD, EARLY>(p, taddr + s * HD, stg + j * SLAB_BYTES, tab, lane, typ, rs, bht, valid, acce_cl);
     } else {
-      vg_slab<HD>(taddr + s * HD, stg + j * SLAB_BYTES, lane, typ == 3, rs);
+      vg_slab<HD, EARLY>(taddr + s * HD, stg + j * SLAB_BYTES, lane, typ == 3, rs, acce_cl);
     }
   }
   if (any_qk) {
     __syncwarp();
     if (lane == 0) mbar_arrive(tab_empty);
   }
-  release_acc(acce_cl, lane);
+  if constexpr (!EARLY) release_acc(acce_cl, lane);
   staging_publish();
   if (lane == 0) {
 #pragma unroll
