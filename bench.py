@@ -45,7 +45,7 @@ CONFIGS = {
     "c4": dict(B=4, T=16384, C=2048, H=16, N=128, name="c4: long-context block B=4 T=16384 C=2048 H=16 N=128"),
     "c5": dict(B=128, T=2048, C=768, H=12, N=64, name="c5: DP block, global B=1024 T=2048 C=768 H=12 N=64 (B=128 per GPU at 8 GPUs)"),
 }
-LAUNCHES_PER_STAGE = {"bwd.cast": 5, "bwd.memset": 0, "fwd.attention": 2}
+LAUNCHES_PER_STAGE = {"bwd.memset": 0, "fwd.attention": 2}
 # DRAM bytes per launch and per sequence, dram__bytes.sum from ncu captures of the c2 kernels at
 # B=16 (every sequence is independent, so the traffic scales with B); the roofline's "traffic".
 DRAM_BYTES_PER_SEQ = {

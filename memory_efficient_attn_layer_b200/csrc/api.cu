@@ -500,8 +500,7 @@ int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq
   const size_t wsz = size_t(HN) * C;
   StageScope cast_scope(ST_BWD_CAST, st);
   void* dst[5] = {dwq, dwk, dwv, dwg, dwo};
-  for (int i = 0; i < 5; ++i)
-    if (dst[i]) MEA_TRY(run_cast_f32_bf16((long long)wsz, dw32 + i * wsz, dst[i], st));
+  MEA_TRY(run_cast_f32_bf16_parts((long long)wsz, dw32, dst, 5, st));
   return MEA_OK;
 }
 

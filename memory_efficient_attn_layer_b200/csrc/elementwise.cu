@@ -307,14 +307,31 @@ __global__ void __launch_bounds__(256) qk_bwd_kernel(int BH, int H, int T, int b
   }
 }
 
-__global__ void cast_f32_bf16_kernel(long long n, const float* __restrict__ src, __nv_bfloat16* __restrict__ dst) {
-  const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+__device__ __forceinline__ void cast4(long long i, long long n, const float* __restrict__ src,
+                                      __nv_bfloat16* __restrict__ dst) {
   if (i + 3 < n) {
     const float4 v = *reinterpret_cast<const float4*>(src + i);
     *reinterpret_cast<uint2*>(dst + i) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
   } else {
     for (long long j = i; j < n; ++j) dst[j] = __float2bfloat16_rn(src[j]);
   }
+}
+
+__global__ void cast_f32_bf16_kernel(long long n, const float* __restrict__ src, __nv_bfloat16* __restrict__ dst) {
+  cast4(((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4, n, src, dst);
+}
+
+// Up to kCastParts consecutive fp32 parts of n elements each (part y at src +
+// y*n) into their own bf16 tensors in one launch (blockIdx.y = part; a NULL
+// destination skips its part): the five weight gradients of the backward.
+constexpr int kCastParts = 5;
+struct CastParts {
+  __nv_bfloat16* dst[kCastParts];
+};
+__global__ void cast_f32_bf16_parts_kernel(long long n, const float* __restrict__ src, const CastParts parts) {
+  __nv_bfloat16* dst = parts.dst[blockIdx.y];
+  if (!dst) return;
+  cast4(((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4, n, src + (long long)blockIdx.y * n, dst);
 }
 
 // ---------------------------------------------------------------------------
@@ -473,6 +490,23 @@ int run_qk_norm_rope_bwd(int B, int H, int T, int HD, const float* dq_acc, const
       return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "qk backward: head dim %d not in {32, 64, 128}", HD);
   }
   return check_launch("qk_bwd_kernel");
+}
+
+int run_cast_f32_bf16_parts(long long n, const float* src, void* const* dst, int parts, cudaStream_t st) {
+  if (parts < 1 || parts > kCastParts)
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "cast: %d parts (1..%d)", parts, kCastParts);
+  if (n <= 0) return MEA_OK;
+  CastParts cp{};
+  bool any = false;
+  for (int i = 0; i < parts; ++i) {
+    cp.dst[i] = static_cast<__nv_bfloat16*>(dst[i]);
+    any |= dst[i] != nullptr;
+  }
+  if (!any) return MEA_OK;
+  const long long threads = 256;
+  const long long blocks = (n / 4 + threads) / threads;
+  cast_f32_bf16_parts_kernel<<<dim3(unsigned(blocks), unsigned(parts)), unsigned(threads), 0, st>>>(n, src, cp);
+  return check_launch("cast_f32_bf16_parts_kernel");
 }
 
 int run_cast_f32_bf16(long long n, const float* src, void* dst, cudaStream_t st) {
