@@ -7,7 +7,13 @@
  * unless a parameter says fp32.  No function allocates device memory: callers
  * pass a workspace sized by the matching *_workspace_size() query.  Every
  * function returns MEA_OK (0) or an MEA_ERR_* code; mea_last_error_string()
- * describes the last failure of the calling thread.
+ * describes the last failure of the calling thread.  Arguments are checked
+ * before any device work is queued: a rejected call leaves the stream as it was.
+ *
+ * Alignment: tensors 16-byte aligned (workspaces 256-byte), except the bf16
+ * weight-gradient outputs of the block backward and the bf16 dq of
+ * mea_attention_backward_noalloc, which need 8 bytes; MEA_ERR_ALIGNMENT
+ * otherwise.
  *
  * Device-side waits are bounded: a kernel that gives up writes a non-zero code
  * into the optional `status` word (device int, zero it before the call) and
@@ -51,8 +57,19 @@ int mea_version(void);
 const char* mea_last_error_string(void);
 /* MEA_OK when the current device is an sm_100 part the kernels were built for. */
 int mea_device_check(void);
-/* Synchronises `stream` and copies the device status word to *out. */
+/* Synchronises `stream` and copies the device status word to *out; returns
+ * MEA_ERR_DEVICE_TIMEOUT (with the kernel and wait site in the message) when
+ * the word is non-zero. */
 int mea_read_status(const int* status_dev, int* out, void* stream);
+/* Self-test of the device-side failure detection; no counterpart in the
+ * reference, which has none.  Launches one warp that waits on an mbarrier
+ * through the same bounded wait every kernel of the library uses, with a limit
+ * of limit_ns (at most 1e9).  With arrive != 0 the barrier completes at once
+ * and *status is left alone; with arrive == 0 nobody arrives, the wait gives
+ * up after limit_ns and records a timeout (kernel id 9, site 1) in *status,
+ * exactly as a stalled kernel would.  Nothing else is in flight in that
+ * kernel, so it always ends and leaves the context usable. */
+int mea_selftest_wait(int* status, unsigned long long limit_ns, int arrive, void* stream);
 
 /* ---------------------------------------------------------------- block level */
 
@@ -154,7 +171,7 @@ int mea_rmsnorm_backward(int rows, int C, const void* dxn, const void* x, const 
  * the fp32 dQ accumulator lives in a 16 MiB array inside the library (held by
  * every GPU that loads it), so B*H*T*N must not exceed 4,194,304; larger
  * problems return MEA_ERR_UNSUPPORTED_SHAPE.  dq is written as bf16
- * [B,H,T,N]; dk, dv as in mea_attention_backward.  All calls share that array:
+ * [B,H,T,N] (8-byte aligned); dk, dv as in mea_attention_backward.  All calls share that array:
  * calls that overlap on the GPU race.  The first call on a device looks up the
  * array's address; make it before any stream capture. */
 int mea_attention_backward_noalloc(int B, int H, int T, int N, const void* q, const void* k, const void* v,

@@ -59,6 +59,7 @@ SIGNATURES = {
     "mea_rmsnorm_backward": (_I, [_I, _I, _P, _P, _P, _P, _P]),
     "mea_attention_backward_noalloc": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P]),
     "mea_adamw_step": (_I, [_LL, _P, _P, _P, _P, _P, _DB, _DB, _DB, _DB, _DB, _F, _I, _P]),
+    "mea_selftest_wait": (_I, [_P, ctypes.c_ulonglong, _I, _P]),
     "mea_profile_enable": (_I, [_I]),
     "mea_profile_read": (_I, [_I, ctypes.POINTER(_F), ctypes.POINTER(_I)]),
     "mea_profile_stage_name": (ctypes.c_char_p, [_I]),
@@ -117,28 +118,110 @@ def stream_ptr(device=None) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-_status = {}
+MEA_ERR_DEVICE_TIMEOUT = 5
 _checked_devices = set()
+
+
+class _StatusWatch:
+    """Per-device failure reporting without a per-call synchronisation.
+
+    ``word`` is the device int32 the kernels write when a bounded wait gives
+    up (0 = ok).  After every library call the word is copied asynchronously
+    into pinned host memory on the calling stream and an event is recorded
+    behind the copy; the next call (or check_device_status) looks at the copy
+    once that event has completed, so a timeout surfaces as a MeaError at the
+    first call after the failing one whose copy has landed, without ever
+    blocking the host on the GPU."""
+
+    def __init__(self, device: torch.device):
+        self.word = torch.zeros(1, dtype=torch.int32, device=device)
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event = None
+
+    def note(self) -> None:
+        self.host.copy_(self.word, non_blocking=True)
+        if self.event is None:
+            self.event = torch.cuda.Event()
+        self.event.record()
+
+    def take(self, block: bool) -> int:
+        """The last copied value (0 when none has landed yet); clears a reported timeout."""
+        if self.event is None:
+            return 0
+        if block:
+            self.event.synchronize()
+        elif not self.event.query():
+            return 0
+        v = int(self.host[0])
+        if v != 0:
+            self.word.zero_()
+            self.host[0] = 0
+            self.event = None
+        return v
+
+
+_watch = {}
+
+
+def _device_index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
+def _watcher(device: torch.device) -> _StatusWatch:
+    idx = _device_index(device)
+    w = _watch.get(idx)
+    if w is None:
+        with torch.cuda.device(idx):
+            w = _StatusWatch(torch.device("cuda", idx))
+        _watch[idx] = w
+    return w
 
 
 def status_buffer(device: torch.device) -> torch.Tensor:
     """Per-device int32 word the kernels write when a bounded wait gives up."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    buf = _status.get(idx)
-    if buf is None:
-        buf = torch.zeros(1, dtype=torch.int32, device=device)
-        _status[idx] = buf
-    return buf
+    return _watcher(device).word
+
+
+def _timeout_error(v: int, when: str) -> MeaError:
+    return MeaError(MEA_ERR_DEVICE_TIMEOUT, f"device wait timed out (kernel {(v >> 8) & 0xFF}, site "
+                                            f"{(v >> 16) & 0xFFFF}) {when}")
+
+
+def note_status(device: torch.device) -> None:
+    """Queue the asynchronous host copy of the status word behind the work just
+    launched on the current stream (no synchronisation)."""
+    _watcher(device).note()
+
+
+def poll_status(device: torch.device) -> None:
+    """Raise MeaError(MEA_ERR_DEVICE_TIMEOUT) if the last status copy that has
+    already landed reports a timeout; never blocks."""
+    v = _watcher(device).take(block=False)
+    if v != 0:
+        raise _timeout_error(v, "in an earlier call")
+
+
+def check_device_status(device: torch.device | None = None) -> None:
+    """Wait for the last status copy of `device` (default: the current one) and
+    raise MeaError(MEA_ERR_DEVICE_TIMEOUT) if any kernel launched before it gave
+    up a bounded wait.  Call it where the caller synchronises anyway (end of an
+    epoch, before a checkpoint) to see a timeout of the very last call."""
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    v = _watcher(dev).take(block=True)
+    if v != 0:
+        raise _timeout_error(v, "in an earlier call")
 
 
 def read_status(device: torch.device) -> int:
     """Synchronises the current stream and raises MeaError if a kernel timed out."""
-    buf = status_buffer(device)
+    w = _watcher(device)
     out = ctypes.c_int(0)
-    rc = lib().mea_read_status(ctypes.c_void_p(buf.data_ptr()), ctypes.byref(out),
+    rc = lib().mea_read_status(ctypes.c_void_p(w.word.data_ptr()), ctypes.byref(out),
                                ctypes.c_void_p(stream_ptr(device)))
     if rc != MEA_OK:
-        buf.zero_()
+        w.word.zero_()
+        w.host[0] = 0
+        w.event = None
         check(rc)
     return out.value
 
@@ -148,7 +231,7 @@ def require_device(device: torch.device) -> None:
     if device.type != "cuda":
         raise RuntimeError("memory_efficient_attn_layer_b200 runs on CUDA (sm_100a) tensors only; "
                            f"got a tensor on {device}")
-    idx = device.index if device.index is not None else torch.cuda.current_device()
+    idx = _device_index(device)
     if idx in _checked_devices:
         return
     with torch.cuda.device(idx):

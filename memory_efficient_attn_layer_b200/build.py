@@ -21,7 +21,7 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(PKG, "libmea.so")
 
-SOURCES = ["api.cu", "gemm.cu", "attn_fwd.cu", "attn_bwd.cu", "elementwise.cu", "noalloc.cu", "optim.cu", "tma.cpp"]
+SOURCES = ["api.cu", "gemm.cu", "attn_fwd.cu", "attn_bwd.cu", "elementwise.cu", "noalloc.cu", "optim.cu", "selftest.cu", "tma.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + INCLUDE, "-I" + CSRC]

@@ -84,6 +84,23 @@ static int validate(const mea_block_dims* d) {
   return MEA_OK;
 }
 
+static bool aligned(const void* p, uintptr_t bytes) { return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0; }
+
+// Caller buffers of the block calls: the bf16 activations, weights and tables
+// and the fp32 row statistics are read and written with 16-byte vector and
+// TMA accesses, the workspace is carved at 256-byte offsets, and the bf16
+// weight gradients are written 8 bytes at a time.  Checked before any device
+// work is queued.
+static int check_block_buffers(const void* const* b16, int n16, const void* const* b8, int n8, const char* who) {
+  for (int i = 0; i < n16; ++i)
+    if (!aligned(b16[i], 16))
+      return set_error(MEA_ERR_ALIGNMENT, "%s: tensor argument %d is not 16-byte aligned", who, i);
+  for (int i = 0; i < n8; ++i)
+    if (!aligned(b8[i], 8))
+      return set_error(MEA_ERR_ALIGNMENT, "%s: weight-gradient output %d is not 8-byte aligned", who, i);
+  return MEA_OK;
+}
+
 struct Carve {
   size_t off = 0;
   size_t take(size_t bytes) {
@@ -361,6 +378,13 @@ int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, co
   const FwdWs w = fwd_layout(*d);
   if (!workspace || workspace_bytes < w.total)
     return set_error(MEA_ERR_WORKSPACE, "forward workspace needs %zu bytes, got %zu", w.total, workspace_bytes);
+  if (!x || !wq || !wk || !wv || !wg || !wo || !factor1 || !factor2 || !y || !lse2)
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "forward: NULL tensor pointer");
+  {
+    const void* b16[] = {x, wq, wk, wv, wg, wo, factor1, factor2, y, lse2};
+    MEA_TRY(check_block_buffers(b16, 10, nullptr, 0, "forward"));
+    if (!aligned(workspace, 256)) return set_error(MEA_ERR_ALIGNMENT, "forward: workspace must be 256-byte aligned");
+  }
   auto st = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
   const int M = d->B * d->T, HN = d->H * d->N;
@@ -423,6 +447,16 @@ int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq
   const BwdWs w = bwd_layout(*d);
   if (!workspace || workspace_bytes < w.total)
     return set_error(MEA_ERR_WORKSPACE, "backward workspace needs %zu bytes, got %zu", w.total, workspace_bytes);
+  if (!x || !wq || !wk || !wv || !wg || !wo || !factor1 || !factor2 || !lse2 || !dy || !dx)
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "backward: NULL tensor pointer");
+  if ((dfactor1 == nullptr) != (dfactor2 == nullptr))
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "backward: dfactor1 and dfactor2 must both be set or both be NULL");
+  {
+    const void* b16[] = {x, wq, wk, wv, wg, wo, factor1, factor2, lse2, dy, dx, dweights_f32};
+    const void* b8[] = {dwq, dwk, dwv, dwg, dwo};
+    MEA_TRY(check_block_buffers(b16, 12, b8, 5, "backward"));
+    if (!aligned(workspace, 256)) return set_error(MEA_ERR_ALIGNMENT, "backward: workspace must be 256-byte aligned");
+  }
   auto st = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
   const int M = d->B * d->T, HN = d->H * d->N, C = d->C;

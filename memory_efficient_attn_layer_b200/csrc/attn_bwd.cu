@@ -682,17 +682,35 @@ static int launch_attn_bwd_t(const AttnBwdMaps& maps, const AttnBwdParams& p, cu
   return check_launch("attn_bwd_kernel");
 }
 
-int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
-                 const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv, int* status,
-                 cudaStream_t st) {
+int check_attn_bwd_args(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
+                        const float* lse2, const float* delta, const void* dk, const void* dv, long long ld_dv) {
+  if (B <= 0 || H <= 0 || T <= 0)
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "attention backward: dims must be positive (B=%d H=%d T=%d)", B, H, T);
   if (HD != 32 && HD != 64 && HD != 128)
     return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "attention backward: head dim %d not in {32, 64, 128}", HD);
-  if (T % 128 != 0 || T <= 0 || B <= 0 || H <= 0)
+  if (T % 128 != 0)
     return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "attention backward: T=%d must be a positive multiple of 128", T);
+  if (uint64_t(B) * H * T * HD > (uint64_t(1) << 31))
+    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "attention backward: B*H*T*N must stay below 2^31");
+  if (!q || !k || !v || !dO || !lse2 || !delta || !dk || !dv)
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "attention backward: NULL tensor pointer");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(dO)) & 15)
+    return set_error(MEA_ERR_ALIGNMENT, "attention backward: q/k/v/dO must be 16-byte aligned");
   if ((reinterpret_cast<uintptr_t>(lse2) | reinterpret_cast<uintptr_t>(delta)) & 15)
     return set_error(MEA_ERR_ALIGNMENT, "attention backward: lse/delta must be 16-byte aligned");
   if ((reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15 || ld_dv % 8 || ld_dv < (long long)H * HD)
     return set_error(MEA_ERR_ALIGNMENT, "attention backward: dk/dv must be 16-byte aligned, ld_dv a multiple of 8 >= H*N");
+  return MEA_OK;
+}
+
+int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
+                 const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv, int* status,
+                 cudaStream_t st) {
+  const int rc0 = check_attn_bwd_args(B, H, T, HD, q, k, v, dO, lse2, delta, dk, dv, ld_dv);
+  if (rc0 != MEA_OK) return rc0;
+  if (!dq_acc || (reinterpret_cast<uintptr_t>(dq_acc) & 15))
+    return set_error(MEA_ERR_ALIGNMENT, "attention backward: dq_acc must be non-NULL and 16-byte aligned");
   const uint64_t rows = uint64_t(B) * H * T;
   const int swb = HD * 2 >= 128 ? 128 : HD * 2;
   const int box_inner = swb / 2;

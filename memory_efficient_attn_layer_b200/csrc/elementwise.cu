@@ -429,6 +429,8 @@ static int rmsnorm_fwd_rows(int rows, float eps, const void* x, void* xn, float*
 
 int run_rmsnorm_fwd(int rows, int C, float eps, const void* x, void* xn, float* r, cudaStream_t st) {
   if (C % 8 || C <= 0 || rows <= 0) return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "rmsnorm: C=%d must be a multiple of 8", C);
+  if (!x || (reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(xn)) & 15)
+    return set_error(MEA_ERR_ALIGNMENT, "rmsnorm: x (and xn) must be non-NULL and 16-byte aligned");
   switch (C) {
     case 256: return rmsnorm_fwd_rows<1>(rows, eps, x, xn, r, st);
     case 512: return rmsnorm_fwd_rows<2>(rows, eps, x, xn, r, st);
@@ -447,6 +449,9 @@ int run_rmsnorm_fwd(int rows, int C, float eps, const void* x, void* xn, float* 
 
 int run_rmsnorm_bwd(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, cudaStream_t st) {
   if (C % 8 || C <= 0 || rows <= 0) return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "rmsnorm bwd: C=%d must be a multiple of 8", C);
+  if (!dxn || !x || !r || !dx ||
+      (reinterpret_cast<uintptr_t>(dxn) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dx)) & 15)
+    return set_error(MEA_ERR_ALIGNMENT, "rmsnorm bwd: dxn, x, dx must be non-NULL and 16-byte aligned");
   const int threads = 256;
   const int blocks = (rows * 32 + threads - 1) / threads;
   rmsnorm_bwd_kernel<<<blocks, threads, 0, st>>>(rows, C, static_cast<const __nv_bfloat16*>(dxn),
@@ -501,7 +506,11 @@ int run_cast_f32_bf16_parts(long long n, const float* src, void* const* dst, int
   for (int i = 0; i < parts; ++i) {
     cp.dst[i] = static_cast<__nv_bfloat16*>(dst[i]);
     any |= dst[i] != nullptr;
+    if (reinterpret_cast<uintptr_t>(dst[i]) & 7)
+      return set_error(MEA_ERR_ALIGNMENT, "cast: bf16 output %d must be 8-byte aligned", i);
   }
+  if (any && ((reinterpret_cast<uintptr_t>(src) & 15) || n % 4))
+    return set_error(MEA_ERR_ALIGNMENT, "cast: fp32 parts must be 16-byte aligned with n %% 4 == 0");
   if (!any) return MEA_OK;
   const long long threads = 256;
   const long long blocks = (n / 4 + threads) / threads;
@@ -511,6 +520,8 @@ int run_cast_f32_bf16_parts(long long n, const float* src, void* const* dst, int
 
 int run_cast_f32_bf16(long long n, const float* src, void* dst, cudaStream_t st) {
   if (n <= 0) return MEA_OK;
+  if (!src || !dst || (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 7))
+    return set_error(MEA_ERR_ALIGNMENT, "cast: src must be 16-byte and dst 8-byte aligned");
   const long long threads = 256;
   const long long blocks = (n / 4 + threads) / threads;
   cast_f32_bf16_kernel<<<unsigned(blocks), unsigned(threads), 0, st>>>(n, src, static_cast<__nv_bfloat16*>(dst));

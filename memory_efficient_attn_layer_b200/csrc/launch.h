@@ -63,6 +63,10 @@ int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, cons
 int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
                  const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv, int* status,
                  cudaStream_t st);
+// The shape, pointer and alignment checks of run_attn_bwd (all but dq_acc),
+// with no device work: MEA_OK or the error run_attn_bwd would return.
+int check_attn_bwd_args(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
+                        const float* lse2, const float* delta, const void* dk, const void* dv, long long ld_dv);
 
 // ---- elementwise (elementwise.cu) ----
 int run_rmsnorm_fwd(int rows, int C, float eps, const void* x, void* xn, float* r, cudaStream_t st);

@@ -77,19 +77,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return done != 0;
 }
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, Guard& g, uint32_t site) {
+// Bounded wait for the phase with the given parity to complete, giving up
+// after `limit_ns` of wall-clock time.
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, Guard& g, uint32_t site,
+                                              uint64_t limit_ns) {
   if (!g.ok) return false;
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > MEA_WAIT_LIMIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
       g.ok = false;
       record_error(g.status, g.kid, site);
       return false;
     }
   }
+}
+// The wait every kernel of the library uses: limit MEA_WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, Guard& g, uint32_t site) {
+  return mbar_wait_for(bar, parity, g, site, MEA_WAIT_LIMIT_NS);
 }
 // Short bounded wait used only on teardown after an abort (no error recorded).
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {

@@ -18,6 +18,9 @@ import torch
 from . import _lib
 from . import dp as _dp
 
+# Device timeouts are always reported: by default at the first call after the
+# failing one whose asynchronous status copy has landed (no synchronisation);
+# with MEA_CHECK_STATUS=1 at the failing call itself (one synchronisation per call).
 _CHECK_STATUS = os.environ.get("MEA_CHECK_STATUS", "0") == "1"
 
 
@@ -56,6 +59,7 @@ class FusedAttentionFunction(torch.autograd.Function):
         factor1 = factor1.contiguous()
         factor2 = factor2.contiguous()
         _check_inputs(x, weights, factor1, factor2, H, N)
+        _lib.poll_status(x.device)  # a timeout of an earlier call whose status copy has landed
         B, T, C = x.shape
         L = _lib.lib()
         dims = _dims(x, H, N, factor1, eps)
@@ -72,6 +76,8 @@ class FusedAttentionFunction(torch.autograd.Function):
             _lib.stream_ptr(x.device)))
         if _CHECK_STATUS:
             _lib.read_status(x.device)
+        else:
+            _lib.note_status(x.device)
         ctx.save_for_backward(x, *weights, factor1, factor2, lse)
         ctx.H, ctx.N, ctx.eps = int(H), int(N), float(eps)
         ctx.exchange = _dp.active_exchange()
@@ -82,6 +88,7 @@ class FusedAttentionFunction(torch.autograd.Function):
         x, wq, wk, wv, wg, wo, factor1, factor2, lse = ctx.saved_tensors
         H, N, eps = ctx.H, ctx.N, ctx.eps
         dy = grad_output.to(torch.bfloat16).contiguous()
+        _lib.poll_status(x.device)
         L = _lib.lib()
         dims = _dims(x, H, N, factor1, eps)
         dx = torch.empty_like(x)
@@ -115,6 +122,8 @@ class FusedAttentionFunction(torch.autograd.Function):
             _exchange_backward(L, args, dws, df1, df2, ws, ws_bytes, status, x, ex)
         if _CHECK_STATUS:
             _lib.read_status(x.device)
+        else:
+            _lib.note_status(x.device)
         gf1 = df1.to(factor1.dtype) if want_df else None
         gf2 = df2.to(factor2.dtype) if want_df else None
         return (dx, *dws, gf1, gf2, None, None, None)
@@ -144,7 +153,33 @@ def _exchange_backward(L, args, dws, df1, df2, ws, ws_bytes, status, x, ex):
         _dp.reduce_weight_grads(dw32, 4 * n_w, ex.group, ex.average, before_qkvg=lambda: side.wait_event(ev_dw))
         for i, d in enumerate(dws):
             d.copy_(dw32[i * n_w:(i + 1) * n_w].view_as(d))
+    if _exchange_waits is not None:
+        reach, done = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reach.record(main)
+        done.record(side)
+        _exchange_waits.append((reach, done))
     main.wait_stream(side)
+
+
+_exchange_waits = None
+
+
+def record_exchange_waits(on: bool):
+    """Instrument the overlapped gradient exchange: while on, every backward
+    records when the caller's stream reaches the end of the backward and when
+    the side stream's all-reduce finishes.  Turning it off returns, per
+    backward, the milliseconds the caller's stream waited for the exchange
+    (0 when the all-reduce was hidden under the rest of the backward)."""
+    global _exchange_waits
+    if on:
+        _exchange_waits = []
+        return None
+    pairs, _exchange_waits = _exchange_waits or [], None
+    out = []
+    for reach, done in pairs:
+        done.synchronize()
+        out.append(max(0.0, reach.elapsed_time(done)))
+    return out
 
 
 def fused_attn(x, q_proj, k_proj, v_proj, g_proj, o_proj, yarn_module, H, N, eps=1e-6):

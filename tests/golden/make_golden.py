@@ -1,8 +1,9 @@
 """Generate golden vectors from the reference's own ``FusedAttentionFunction``.
 
-Run in the build container, where the reference source is mounted read-only:
+Run where the reference source is available (read-only is fine), naming the
+directory that holds its fast_triton_attn.py:
 
-    python tests/golden/make_golden.py --ref /root/reference
+    python tests/golden/make_golden.py --ref <reference checkout>
 
 The reference (fast_triton_attn.py) is imported unmodified and run on the CPU
 under the Triton interpreter (TRITON_INTERPRET=1).  Two things make that work:
@@ -108,7 +109,7 @@ def run_case(fta, name, B, T, C, H, N, seed, T_max):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="directory holding the reference's fast_triton_attn.py")
     ap.add_argument("--cases", nargs="*", default=list(CASES))
     args = ap.parse_args()
     fta = _load_reference(args.ref)

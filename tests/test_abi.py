@@ -67,3 +67,34 @@ def test_cpu_tensors_raise():
     f = torch.zeros(128, 32, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
         FusedAttentionFunction.apply(x, w, w, w, w, w, f, f, 4, 32, 1e-6)
+
+
+def _fake(i):
+    return ctypes.c_void_p(0x100000 * (i + 1))  # aligned stand-ins: the calls below never reach the device
+
+
+@pytest.mark.parametrize("slot,bad,text", [
+    (12, 0x7000002, b"weight-gradient output 0"),   # dwq only 2-byte aligned
+    (16, 0x7000004, b"weight-gradient output 4"),   # dwo only 4-byte aligned
+    (1, 0x7000008, b"tensor argument 0"),           # x only 8-byte aligned
+    (11, 0x7000008, b"tensor argument 10"),         # dx only 8-byte aligned
+])
+def test_block_backward_rejects_misaligned_buffers_before_device_work(L, slot, bad, text):
+    d = _lib.MeaBlockDims(2, 256, 128, 4, 32, 256, 1e-6)
+    need = L.mea_backward_workspace_size(ctypes.byref(d))
+    # d, x, wq, wk, wv, wg, wo, f1, f2, lse2, dy, dx, dwq, dwk, dwv, dwg, dwo, df1, df2, dw32, ws
+    args = [ctypes.byref(d)] + [_fake(i) for i in range(20)]
+    args[17] = args[18] = args[19] = None
+    args[slot] = ctypes.c_void_p(bad)
+    rc = L.mea_block_backward_ex(*args, need, None, None, None, None)
+    assert rc == 3, L.mea_last_error_string()
+    assert text in L.mea_last_error_string()
+
+
+def test_block_forward_rejects_misaligned_output_before_device_work(L):
+    d = _lib.MeaBlockDims(2, 256, 128, 4, 32, 256, 1e-6)
+    need = L.mea_forward_workspace_size(ctypes.byref(d))
+    args = [ctypes.byref(d)] + [_fake(i) for i in range(11)]
+    args[9] = ctypes.c_void_p(0x7000002)  # y
+    rc = L.mea_block_forward(*args, need, None, None)
+    assert rc == 3 and b"tensor argument 8" in L.mea_last_error_string()

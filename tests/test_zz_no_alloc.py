@@ -30,11 +30,38 @@ def test_noalloc_rejects_problems_above_the_limit():
     assert b"exceeds the built-in limit" in L.mea_last_error_string()
 
 
+# Every argument is checked before the entry point queues any device work (a
+# rejected call leaves the caller's stream untouched), so these run without a
+# GPU.  Fake but aligned device addresses stand in for the tensors.
+_FAKE = [0x10000 * (i + 1) for i in range(9)]  # q, k, v, dO, lse2, delta, dq, dk, dv
+
+
+@pytest.mark.parametrize("case,dims,override,code,text", [
+    ("null dq", (1, 2, 256, 64), {6: None}, 1, b"dq is NULL"),
+    ("zero batch", (0, 2, 256, 64), {}, 1, b"dims must be positive"),
+    ("T not a multiple of 128", (1, 2, 100, 64), {}, 2, b"multiple of 128"),
+    ("head dim 48", (1, 2, 256, 48), {}, 2, b"head dim 48"),
+    ("dq 2-byte aligned", (1, 2, 256, 64), {6: 0x70002}, 3, b"dq must be 8-byte aligned"),
+    ("dk 8-byte aligned", (1, 2, 256, 64), {7: 0x80008}, 3, b"dk/dv must be 16-byte aligned"),
+    ("null q", (1, 2, 256, 64), {0: None}, 1, b"NULL tensor pointer"),
+])
+def test_noalloc_rejects_bad_arguments_before_device_work(case, dims, override, code, text):
+    L = _lib.lib()
+    ptrs = list(_FAKE)
+    for i, v in override.items():
+        ptrs[i] = v
+    B, H, T, N = dims
+    rc = L.mea_attention_backward_noalloc(B, H, T, N, *ptrs, H * N, None, None)
+    assert rc == code, (case, rc, L.mea_last_error_string())
+    assert text in L.mea_last_error_string(), case
+
+
 @pytest.mark.gpu
-def test_noalloc_matches_allocating_entry_point_twice():
+@pytest.mark.parametrize("N", [32, 64, 128])
+def test_noalloc_matches_allocating_entry_point_twice(N):
     from gpu_util import DEV, P, call, cos, maxrel, status, stream
 
-    B, H, T, N = 2, 2, 384, 64
+    B, H, T = 2, 2, 384
     assert B * H * T * N <= LIMIT
     g = torch.Generator(device=DEV).manual_seed(123)
 
