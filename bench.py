@@ -315,6 +315,28 @@ def measure_block(fwd, x, dy, device, steps, warmup):
             "saved_for_backward_gb": saved / 1e9, "peak_fwd_bwd_gb": peak / 1e9, "steps": steps}
 
 
+def run_save_o_ablation(cfg, device, x, ws, yarn, dy, steps=10, warmup=3):
+    """This build with save_o=True (the forward keeps the attention output, as the reference does, and the
+    backward skips the attention recompute) on the same inputs: tokens/s, activation memory and the
+    per-stage times of its backward."""
+    from memory_efficient_attn_layer_b200 import FusedAttentionFunction, _lib
+
+    H, N = cfg["H"], cfg["N"]
+    wd = [w.detach() for w in ws]
+    r = measure_block(lambda inp: FusedAttentionFunction.apply(inp, *wd, yarn.factor1, yarn.factor2, H, N, 1e-6,
+                                                               True), x, dy, device, steps, warmup)
+    _lib.profile_enable(True)
+    for _ in range(3):
+        y = FusedAttentionFunction.apply(x.detach().requires_grad_(True), *wd, yarn.factor1, yarn.factor2, H, N,
+                                         1e-6, True)
+        y.backward(dy)
+    st = _lib.profile_read()
+    _lib.profile_enable(False)
+    r["stages_ms"] = {k: v[0] / v[1] for k, v in st.items() if k.startswith("bwd.")}
+    r["what"] = "save_o=True: saved set x + O + row LSE (the reference's), no attention recompute in the backward"
+    return r
+
+
 def run_comparators(cfg, device, x, ws, yarn, dy, our_saved, our_peak, our_value, steps=10, warmup=3):
     """The reference's own GPU block (fast_triton_attn.fused_attn from baseline/_ref, unmodified: its Triton
     kernels and ATen flash attention) and the README's eager SDPA block, run in this process on the same
@@ -723,6 +745,7 @@ def run_gpu(args, cfg, rank, world, device):
         line["exchange_wait"] = exchange_wait
     line["clocks"] = clk
     if world == 1 and not eager and not args.no_comparators:
+        line["save_o_ablation"] = run_save_o_ablation(cfg, device, x, ws, yarn, dy)
         line["comparators"] = run_comparators(cfg, device, x, ws, yarn, dy, saved, peak, value)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(cfg)

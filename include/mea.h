@@ -114,6 +114,25 @@ int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq
                           size_t workspace_bytes, int* status, void* stream, void* ev_dwo_ready,
                           void* ev_dw_ready);
 
+/* Keep-O variant (an ablation of the memory-saving default; it mirrors the
+ * reference, which keeps the attention output, fast_triton_attn.py:463-466):
+ * mea_block_forward that also writes the attention output
+ * o[B,H,T,N] (bf16, before the gate) for the backward. */
+int mea_block_forward_save_o(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                             const void* wg, const void* wo, const void* factor1, const void* factor2, void* y,
+                             float* lse2, void* o, void* workspace, size_t workspace_bytes, int* status,
+                             void* stream);
+/* mea_block_backward_ex given that o (from mea_block_forward_save_o): the
+ * attention recompute is skipped and the gated tile is formed from o
+ * (gate_repack_kernel_bwd_recompute, fast_triton_attn.py:334-367).  Same
+ * workspace size as mea_block_backward. */
+int mea_block_backward_from_o(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                              const void* wg, const void* wo, const void* factor1, const void* factor2,
+                              const float* lse2, const void* o, const void* dy, void* dx, void* dwq, void* dwk,
+                              void* dwv, void* dwg, void* dwo, float* dfactor1, float* dfactor2,
+                              float* dweights_f32, void* workspace, size_t workspace_bytes, int* status,
+                              void* stream, void* ev_dwo_ready, void* ev_dw_ready);
+
 /* ---------------------------------------------------------------- kernel level */
 
 /* rms_norm_kernel / rms_norm_kernel_recompute (fast_triton_attn.py:12-34, :181-210):

@@ -49,6 +49,9 @@ SIGNATURES = {
                                 _P, _S, _P, _P]),
     "mea_block_backward_ex": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                    _P, _P, _S, _P, _P, _P, _P]),
+    "mea_block_forward_save_o": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P, _P]),
+    "mea_block_backward_from_o": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                       _P, _P, _P, _P, _S, _P, _P, _P, _P]),
     "mea_rmsnorm_forward": (_I, [_I, _I, _F, _P, _P, _P, _P]),
     "mea_qkvg_forward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "mea_attention_forward": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),

@@ -131,6 +131,10 @@ static FwdWs fwd_layout(const mea_block_dims& d) {
 struct BwdWs {
   size_t xn, rx, q, k, v, gs, rq, rk, gated, o, dO, delta, dacc, dqacc, dk, dxn, dw32, total;
 };
+// Two slots are shared between tensors whose lifetimes do not overlap (kernel
+// order of mea_block_backward_ex): gated is last read by the dWo GEMM and dK is
+// first written by the attention backward, after it; O is last read by the
+// gate backward and dx_n first written by the dx GEMM, after it.
 static BwdWs bwd_layout(const mea_block_dims& d) {
   const size_t M = size_t(d.B) * d.T, HN = size_t(d.H) * d.N, BHT = size_t(d.B) * d.H * d.T;
   BwdWs w;
@@ -149,8 +153,8 @@ static BwdWs bwd_layout(const mea_block_dims& d) {
   w.delta = c.take(BHT * 4);
   w.dacc = c.take(M * 4 * HN * 2);
   w.dqacc = c.take(M * HN * 4);
-  w.dk = c.take(M * HN * 2);
-  w.dxn = c.take(M * d.C * 2);
+  w.dk = w.gated;
+  w.dxn = d.C <= HN ? w.o : c.take(M * d.C * 2);  // O's slot holds [M, H*N]; dx_n is [M, C]
   w.dw32 = c.take(5 * HN * d.C * 4);
   w.total = c.off;
   return w;
@@ -265,12 +269,13 @@ static int weight_grad(int Mp, int Np, int tokens, const void* a, long long lda,
 enum Stage : int {
   ST_FWD_NORM = 0, ST_FWD_QKVG, ST_FWD_ATTN, ST_FWD_OPROJ,
   ST_BWD_NORM, ST_BWD_QKVG, ST_BWD_ATTN_FWD, ST_BWD_MEMSET, ST_BWD_DWO, ST_BWD_DGATE, ST_BWD_ATTN, ST_BWD_QK,
-  ST_BWD_DW, ST_BWD_DX, ST_BWD_NORM_BWD, ST_BWD_CAST, ST_COUNT
+  ST_BWD_DW, ST_BWD_DX, ST_BWD_NORM_BWD, ST_BWD_CAST, ST_BWD_GATE_REPACK, ST_COUNT
 };
 static const char* kStageNames[ST_COUNT] = {
   "fwd.rmsnorm", "fwd.qkvg_gemm", "fwd.attention", "fwd.o_proj_gemm",
   "bwd.rmsnorm", "bwd.qkvg_gemm", "bwd.attention_recompute", "bwd.memset", "bwd.dWo_gemm", "bwd.dgate_gemm",
-  "bwd.attention_bwd", "bwd.qk_norm_rope_bwd", "bwd.dW_gemm", "bwd.dx_gemm", "bwd.rmsnorm_bwd", "bwd.cast"};
+  "bwd.attention_bwd", "bwd.qk_norm_rope_bwd", "bwd.dW_gemm", "bwd.dx_gemm", "bwd.rmsnorm_bwd", "bwd.cast",
+  "bwd.gate_repack"};
 
 struct Profiler {
   std::mutex mu;
@@ -371,9 +376,9 @@ size_t mea_backward_workspace_size(const mea_block_dims* d) {
   return bwd_layout(*d).total;
 }
 
-int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
-                      const void* wg, const void* wo, const void* factor1, const void* factor2, void* y, float* lse2,
-                      void* workspace, size_t workspace_bytes, int* status, void* stream) {
+static int block_forward(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                         const void* wg, const void* wo, const void* factor1, const void* factor2, void* y,
+                         float* lse2, void* o_out, void* workspace, size_t workspace_bytes, int* status, void* stream) {
   MEA_TRY(validate(d));
   const FwdWs w = fwd_layout(*d);
   if (!workspace || workspace_bytes < w.total)
@@ -381,8 +386,8 @@ int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, co
   if (!x || !wq || !wk || !wv || !wg || !wo || !factor1 || !factor2 || !y || !lse2)
     return set_error(MEA_ERR_INVALID_ARGUMENT, "forward: NULL tensor pointer");
   {
-    const void* b16[] = {x, wq, wk, wv, wg, wo, factor1, factor2, y, lse2};
-    MEA_TRY(check_block_buffers(b16, 10, nullptr, 0, "forward"));
+    const void* b16[] = {x, wq, wk, wv, wg, wo, factor1, factor2, y, lse2, o_out};
+    MEA_TRY(check_block_buffers(b16, 11, nullptr, 0, "forward"));
     if (!aligned(workspace, 256)) return set_error(MEA_ERR_ALIGNMENT, "forward: workspace must be 256-byte aligned");
   }
   auto st = static_cast<cudaStream_t>(stream);
@@ -400,7 +405,7 @@ int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, co
     StageScope scope_(ST_FWD_ATTN, st);
     float* bound = reinterpret_cast<float*>(ws + w.bound);
     MEA_TRY(run_rope_bound(d->T, d->N, factor1, factor2, d->N, bound, st));
-    MEA_TRY(run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated, lse2, nullptr,
+    MEA_TRY(run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated, lse2, o_out,
                          bound, nullptr, status, st));
   }
   GemmLaunch L{};
@@ -424,6 +429,22 @@ int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, co
   return run_gemm(L, p, st);
 }
 
+int mea_block_forward(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                      const void* wg, const void* wo, const void* factor1, const void* factor2, void* y, float* lse2,
+                      void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  return block_forward(d, x, wq, wk, wv, wg, wo, factor1, factor2, y, lse2, nullptr, workspace, workspace_bytes,
+                       status, stream);
+}
+
+int mea_block_forward_save_o(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                             const void* wg, const void* wo, const void* factor1, const void* factor2, void* y,
+                             float* lse2, void* o, void* workspace, size_t workspace_bytes, int* status,
+                             void* stream) {
+  if (!o) return set_error(MEA_ERR_INVALID_ARGUMENT, "forward: o is NULL");
+  return block_forward(d, x, wq, wk, wv, wg, wo, factor1, factor2, y, lse2, o, workspace, workspace_bytes, status,
+                       stream);
+}
+
 int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
                        const void* wg, const void* wo, const void* factor1, const void* factor2, const float* lse2,
                        const void* dy, void* dx, void* dwq, void* dwk, void* dwv, void* dwg, void* dwo,
@@ -434,11 +455,14 @@ int mea_block_backward(const mea_block_dims* d, const void* x, const void* wq, c
                                nullptr);
 }
 
-int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+// The block backward.  `o_saved` (may be NULL): the forward's attention output
+// O [B,H,T,N]; when given, the attention recompute is skipped and the gated
+// tile the dWo GEMM needs is formed from it.
+static int block_backward(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
                           const void* wg, const void* wo, const void* factor1, const void* factor2,
-                          const float* lse2, const void* dy, void* dx, void* dwq, void* dwk, void* dwv, void* dwg,
-                          void* dwo, float* dfactor1, float* dfactor2, float* dweights_f32, void* workspace,
-                          size_t workspace_bytes, int* status, void* stream, void* ev_dwo_ready,
+                          const float* lse2, const void* o_saved, const void* dy, void* dx, void* dwq, void* dwk,
+                          void* dwv, void* dwg, void* dwo, float* dfactor1, float* dfactor2, float* dweights_f32,
+                          void* workspace, size_t workspace_bytes, int* status, void* stream, void* ev_dwo_ready,
                           void* ev_dw_ready) {
   MEA_TRY(validate(d));
   const bool want_bf16 = dwq || dwk || dwv || dwg || dwo;
@@ -452,9 +476,9 @@ int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq
   if ((dfactor1 == nullptr) != (dfactor2 == nullptr))
     return set_error(MEA_ERR_INVALID_ARGUMENT, "backward: dfactor1 and dfactor2 must both be set or both be NULL");
   {
-    const void* b16[] = {x, wq, wk, wv, wg, wo, factor1, factor2, lse2, dy, dx, dweights_f32};
+    const void* b16[] = {x, wq, wk, wv, wg, wo, factor1, factor2, lse2, dy, dx, dweights_f32, o_saved};
     const void* b8[] = {dwq, dwk, dwv, dwg, dwo};
-    MEA_TRY(check_block_buffers(b16, 12, b8, 5, "backward"));
+    MEA_TRY(check_block_buffers(b16, 13, b8, 5, "backward"));
     if (!aligned(workspace, 256)) return set_error(MEA_ERR_ALIGNMENT, "backward: workspace must be 256-byte aligned");
   }
   auto st = static_cast<cudaStream_t>(stream);
@@ -481,9 +505,15 @@ int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq
   // The recompute takes the forward's LSE as its exp2 reference: P comes out
   // normalised, the same P the attention backward rebuilds.
   // (N <= 64: the recompute also clears the dQ accumulator; otherwise a memset does.)
-  const bool zero_in_fwd = d->N <= 64;
-  MEA_STAGE(ST_BWD_ATTN_FWD, run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, ws + w.gated,
-                       nullptr, ws + w.o, nullptr, lse2, status, st, zero_in_fwd ? dqacc : nullptr));
+  // With the forward's O kept, only the gated tile is formed from it.
+  const bool zero_in_fwd = d->N <= 64 && !o_saved;
+  const void* o = o_saved ? o_saved : ws + w.o;
+  if (o_saved)
+    MEA_STAGE(ST_BWD_GATE_REPACK, run_gate_repack(d->B, d->H, d->T, d->N, o_saved, ws + w.gs, ws + w.gated, st));
+  else
+    MEA_STAGE(ST_BWD_ATTN_FWD, run_attn_fwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.gs,
+                                            ws + w.gated, nullptr, ws + w.o, nullptr, lse2, status, st,
+                                            zero_in_fwd ? dqacc : nullptr));
   {
     StageScope scope_(ST_BWD_MEMSET, st);
     MEA_TRY(memset_async(dw32, size_t(5) * HN * C * 4, st));
@@ -494,7 +524,7 @@ int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq
   // o_proj backward: dWo = dY^T gated; dGated = dY Wo with the gate backward fused.
   MEA_STAGE(ST_BWD_DWO, weight_grad(C, HN, M, dy, C, ws + w.gated, HN, dwo32, status, st));
   MEA_TRY(record_event(ev_dwo_ready, st));
-  MEA_STAGE(ST_BWD_DGATE, gate_bwd(*d, dy, wo, ws + w.o, ws + w.gs, ws + w.dO, dacc + size_t(3) * HN * 2, ld_dacc, delta, status,
+  MEA_STAGE(ST_BWD_DGATE, gate_bwd(*d, dy, wo, o, ws + w.gs, ws + w.dO, dacc + size_t(3) * HN * 2, ld_dacc, delta, status,
                    st));
   // Attention backward: dq (fp32 accumulate), dk, dv -> v slot of dacc.
   MEA_STAGE(ST_BWD_ATTN, run_attn_bwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.dO, lse2, delta, dqacc, ws + w.dk,
@@ -536,6 +566,29 @@ int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq
   void* dst[5] = {dwq, dwk, dwv, dwg, dwo};
   MEA_TRY(run_cast_f32_bf16_parts((long long)wsz, dw32, dst, 5, st));
   return MEA_OK;
+}
+
+int mea_block_backward_ex(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                          const void* wg, const void* wo, const void* factor1, const void* factor2,
+                          const float* lse2, const void* dy, void* dx, void* dwq, void* dwk, void* dwv, void* dwg,
+                          void* dwo, float* dfactor1, float* dfactor2, float* dweights_f32, void* workspace,
+                          size_t workspace_bytes, int* status, void* stream, void* ev_dwo_ready,
+                          void* ev_dw_ready) {
+  return block_backward(d, x, wq, wk, wv, wg, wo, factor1, factor2, lse2, nullptr, dy, dx, dwq, dwk, dwv, dwg, dwo,
+                        dfactor1, dfactor2, dweights_f32, workspace, workspace_bytes, status, stream, ev_dwo_ready,
+                        ev_dw_ready);
+}
+
+int mea_block_backward_from_o(const mea_block_dims* d, const void* x, const void* wq, const void* wk, const void* wv,
+                              const void* wg, const void* wo, const void* factor1, const void* factor2,
+                              const float* lse2, const void* o, const void* dy, void* dx, void* dwq, void* dwk,
+                              void* dwv, void* dwg, void* dwo, float* dfactor1, float* dfactor2,
+                              float* dweights_f32, void* workspace, size_t workspace_bytes, int* status,
+                              void* stream, void* ev_dwo_ready, void* ev_dw_ready) {
+  if (!o) return set_error(MEA_ERR_INVALID_ARGUMENT, "backward: o is NULL");
+  return block_backward(d, x, wq, wk, wv, wg, wo, factor1, factor2, lse2, o, dy, dx, dwq, dwk, dwv, dwg, dwo,
+                        dfactor1, dfactor2, dweights_f32, workspace, workspace_bytes, status, stream, ev_dwo_ready,
+                        ev_dw_ready);
 }
 
 int mea_rmsnorm_forward(int rows, int C, float eps, const void* x, void* xn, float* r, void* stream) {

@@ -96,35 +96,6 @@ struct AttnBwdCfg {
   static constexpr size_t SMEM = 1024 + OFF_BAR + 256;
 };
 
-// Work items of the persistent backward: one (b,h) and one 128-row key tile jt,
-// walking the nq - jt query tiles from the diagonal.  Items come in pairs of
-// key tiles (k, nq-1-k) of one head, which together walk nq + 1 query tiles,
-// so CTAs striding over pairs get equal work; consecutive pairs belong to the
-// same head, so the CTAs running at one time share a few heads' Q/dO and dQ
-// rows in L2.  Every role of a CTA walks the same sequence.
-struct BwdItems {
-  int nq, pairs_per_head, total_pairs, stride;
-  int p, side;
-  __device__ BwdItems(int nq_, int bh_count, int start, int stride_)
-      : nq(nq_), pairs_per_head((nq_ + 1) / 2), total_pairs(bh_count * ((nq_ + 1) / 2)), stride(stride_), p(start),
-        side(0) {}
-  __device__ bool valid() const { return p < total_pairs; }
-  __device__ void get(int& bh, int& jt) const {
-    bh = p / pairs_per_head;
-    const int k = p - bh * pairs_per_head;
-    jt = side ? nq - 1 - k : k;
-  }
-  __device__ void next() {
-    const int k = p % pairs_per_head;
-    if (side == 0 && nq - 1 - k != k) {
-      side = 1;
-    } else {
-      side = 0;
-      p += stride;
-    }
-  }
-};
-
 // MN-major descriptor of a [128 q rows x 128 kv] bf16 tile stored as two
 // 64-column chunks (16 KB apart) of 128-byte swizzled rows; k-step of 16 rows.
 __device__ __forceinline__ uint64_t ptile_mn(uint32_t base, int kc) {
@@ -314,7 +285,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
       for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
       int kv_par[2] = {-1, -1};
       int gstep = 0, item = 0;
-      for (BwdItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && g.ok; it.next(), ++item) {
+      for (PairItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && g.ok; it.next(), ++item) {
         int bh, jt;
         it.get(bh, jt);
         const int row0 = bh * p.T;
@@ -389,12 +360,12 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
       };
       int gstep = 0, item = 0;
       bool first = true;
-      for (BwdItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && g.ok; it.next(), ++item) {
+      for (PairItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && g.ok; it.next(), ++item) {
         int bh, jt;
         it.get(bh, jt);
         const int nsteps = nq - jt;
         const int kb = item % KV_BUFS;
-        BwdItems nx = it;
+        PairItems nx = it;
         nx.next();
         const bool has_next = nx.valid();
         const int nkb = (item + 1) % KV_BUFS;
@@ -465,7 +436,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     const float sl2 = p.scale_log2;
     bool ok = true;
     int gstep = 0;
-    for (BwdItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && ok; it.next()) {
+    for (PairItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && ok; it.next()) {
       int bh, jt;
       it.get(bh, jt);
       const int nsteps = nq - jt;
@@ -569,7 +540,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
       }
     };
     int gstep = 0;
-    for (BwdItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && ok; it.next()) {
+    for (PairItems it(nq, BH, blockIdx.x, gridDim.x); it.valid() && ok; it.next()) {
       int bh, jt;
       it.get(bh, jt);
       const int nsteps = nq - jt;

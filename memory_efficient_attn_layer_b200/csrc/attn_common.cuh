@@ -29,6 +29,37 @@ __device__ __forceinline__ float2 exp2_pair(float2 t, bool poly) {
   return make_float2(ex2(t.x), ex2(t.y));
 }
 
+// Work items of the persistent attention kernels: one (b,h) and one 128-row
+// tile index, paired as (k, nq-1-k) within a head.  In the backward the index
+// is a key tile walking the nq - k query tiles from the diagonal, in the
+// forward a query tile walking its k + 1 key tiles up to the diagonal; either
+// way a pair holds nq + 1 tile steps, so CTAs striding over pairs get equal
+// work.  Consecutive pairs belong to the same head, so the CTAs running at one
+// time share a few heads' rows in L2.  Every role of a CTA walks the same
+// sequence.
+struct PairItems {
+  int nq, pairs_per_head, total_pairs, stride;
+  int p, side;
+  __device__ PairItems(int nq_, int bh_count, int start, int stride_)
+      : nq(nq_), pairs_per_head((nq_ + 1) / 2), total_pairs(bh_count * ((nq_ + 1) / 2)), stride(stride_), p(start),
+        side(0) {}
+  __device__ bool valid() const { return p < total_pairs; }
+  __device__ void get(int& bh, int& tile) const {
+    bh = p / pairs_per_head;
+    const int k = p - bh * pairs_per_head;
+    tile = side ? nq - 1 - k : k;
+  }
+  __device__ void next() {
+    const int k = p % pairs_per_head;
+    if (side == 0 && nq - 1 - k != k) {
+      side = 1;
+    } else {
+      side = 0;
+      p += stride;
+    }
+  }
+};
+
 template <int HD>
 struct HeadTile {
   static constexpr int SWB = HD * 2 >= 128 ? 128 : HD * 2;   // bytes per swizzled row

@@ -686,6 +686,14 @@ int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, cons
     return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "attention: head dim %d not in {32, 64, 128}", HD);
   if (T % 128 != 0 || T <= 0 || B <= 0 || H <= 0)
     return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "attention: T=%d must be a positive multiple of 128", T);
+  if (uint64_t(B) * H * T * HD > (uint64_t(1) << 31))
+    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "attention: B*H*T*N must stay below 2^31");
+  if (!q || !k || !v || !gs || !gated || (!lse2 && !lse_in))
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "attention: NULL tensor pointer");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(gs) | reinterpret_cast<uintptr_t>(gated) | reinterpret_cast<uintptr_t>(o_out) |
+       reinterpret_cast<uintptr_t>(dq_zero)) & 15)
+    return set_error(MEA_ERR_ALIGNMENT, "attention: q/k/v/gs/gated/o/dq tensors must be 16-byte aligned");
   const uint64_t rows = uint64_t(B) * H * T;
   const int swb = HD * 2 >= 128 ? 128 : HD * 2;
   const int box_inner = swb / 2;

@@ -398,8 +398,52 @@ __global__ void __launch_bounds__(1024) rope_bound_kernel(int T, int HD, const _
 }
 
 // ---------------------------------------------------------------------------
+// Gate + repack (fast_triton_attn.py:146-176, :334-367):
+//   gated[b, t, h*N + n] = O[b, h, t, n] * gs[b, h, t, n].
+// Used by the backward when the forward kept O (no attention recompute).  One
+// thread per 8 elements (16-byte loads and store); consecutive threads walk n,
+// then t, so every warp reads and writes whole 16-byte-aligned row pieces.
+// ---------------------------------------------------------------------------
+__global__ void gate_repack_kernel(long long units, int H, int T, int N, const __nv_bfloat16* __restrict__ o,
+                                   const __nv_bfloat16* __restrict__ gs, __nv_bfloat16* __restrict__ gated) {
+  const int per_row = N / 8;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < units;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / per_row;  // (b, h, t) row of O
+    const int u = int(i - row * per_row);
+    const int t = int(row % T);
+    const long long bh = row / T;
+    const int h = int(bh % H);
+    const long long b = bh / H;
+    const uint4 ov = __ldg(reinterpret_cast<const uint4*>(o) + i);
+    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gs) + i);
+    const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+    uint32_t out[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      out[e] = pack_bf16(bf16_lo(ow[e]) * bf16_lo(gw[e]), bf16_hi(ow[e]) * bf16_hi(gw[e]));
+    st_global_v4(gated + ((b * T + t) * H + h) * N + 8 * u, out[0], out[1], out[2], out[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
+int run_gate_repack(int B, int H, int T, int HD, const void* o, const void* gs, void* gated, cudaStream_t st) {
+  if (B <= 0 || H <= 0 || T <= 0 || HD % 8)
+    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gate repack: bad shape (head dim %d must be a multiple of 8)", HD);
+  if (!o || !gs || !gated ||
+      (reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(gs) | reinterpret_cast<uintptr_t>(gated)) & 15)
+    return set_error(MEA_ERR_ALIGNMENT, "gate repack: tensors must be non-NULL and 16-byte aligned");
+  const long long units = (long long)B * H * T * (HD / 8);
+  const int threads = 256;
+  const long long want = (units + threads - 1) / threads;
+  const int blocks = int(std::min<long long>(want, (long long)num_sms() * 8));
+  gate_repack_kernel<<<blocks, threads, 0, st>>>(units, H, T, HD, static_cast<const __nv_bfloat16*>(o),
+                                                 static_cast<const __nv_bfloat16*>(gs), static_cast<__nv_bfloat16*>(gated));
+  return check_launch("gate_repack_kernel");
+}
+
 int run_rope_bound(int T, int HD, const void* f1, const void* f2, long long ldf, float* out, cudaStream_t st) {
   if (T <= 0 || HD % 8 || ldf % 8 || !f1 || !f2 || !out)
     return set_error(MEA_ERR_INVALID_ARGUMENT, "rope bound: bad arguments");

@@ -75,6 +75,8 @@ int run_qk_norm_rope_bwd(int B, int H, int T, int HD, const float* dq_acc, const
                          const void* k_rot, const float* rq, const float* rk, const void* f1, const void* f2,
                          long long ldf, void* dacc, long long ld_dacc, float* df1, float* df2, cudaStream_t st);
 int run_cast_f32_bf16(long long n, const float* src, void* dst, cudaStream_t st);
+// gated[b,t,h*N+n] = o[b,h,t,n] * gs[b,h,t,n] (all bf16).
+int run_gate_repack(int B, int H, int T, int HD, const void* o, const void* gs, void* gated, cudaStream_t st);
 // `parts` (<= 5) consecutive fp32 blocks of n elements into dst[i] (NULL: skipped), one launch.
 int run_cast_f32_bf16_parts(long long n, const float* src, void* const* dst, int parts, cudaStream_t st);
 // *out = bound (log2 units) on every scaled score q.k/sqrt(N) of the block.

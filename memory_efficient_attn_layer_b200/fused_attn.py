@@ -53,7 +53,12 @@ class FusedAttentionFunction(torch.autograd.Function):
     """Autograd node of the block (fast_triton_attn.py:373)."""
 
     @staticmethod
-    def forward(ctx, x, q_weight, k_weight, v_weight, g_weight, o_weight, factor1, factor2, H, N, eps):
+    def forward(ctx, x, q_weight, k_weight, v_weight, g_weight, o_weight, factor1, factor2, H, N, eps, save_o=False):
+        """``save_o`` (no counterpart in the reference's signature; default off):
+        also keep the attention output O [B,H,T,N] for the backward, as the
+        reference does (fast_triton_attn.py:463-466), so the backward skips the
+        attention recompute.  Off, only x, the weights, the tables and the row
+        log-sum-exp are kept."""
         weights = [w.contiguous() for w in (q_weight, k_weight, v_weight, g_weight, o_weight)]
         x = x.contiguous()
         factor1 = factor1.contiguous()
@@ -70,22 +75,30 @@ class FusedAttentionFunction(torch.autograd.Function):
             _lib.check(L.mea_block_forward(ctypes.byref(dims), *([None] * 11), 0, None, None))
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         status = _lib.status_buffer(x.device)
-        _lib.check(L.mea_block_forward(
-            ctypes.byref(dims), _lib.ptr(x), *[_lib.ptr(w) for w in weights], _lib.ptr(factor1),
-            _lib.ptr(factor2), _lib.ptr(y), _lib.ptr(lse), _lib.ptr(ws), ws_bytes, _lib.ptr(status),
-            _lib.stream_ptr(x.device)))
+        head = (ctypes.byref(dims), _lib.ptr(x), *[_lib.ptr(w) for w in weights], _lib.ptr(factor1),
+                _lib.ptr(factor2), _lib.ptr(y), _lib.ptr(lse))
+        tail = (_lib.ptr(ws), ws_bytes, _lib.ptr(status), _lib.stream_ptr(x.device))
+        o = None
+        if save_o:
+            o = torch.empty(B, H, T, N, dtype=torch.bfloat16, device=x.device)
+            _lib.check(L.mea_block_forward_save_o(*head, _lib.ptr(o), *tail))
+        else:
+            _lib.check(L.mea_block_forward(*head, *tail))
+        del ws
         if _CHECK_STATUS:
             _lib.read_status(x.device)
         else:
             _lib.note_status(x.device)
-        ctx.save_for_backward(x, *weights, factor1, factor2, lse)
+        ctx.save_o = o is not None
+        ctx.save_for_backward(x, *weights, factor1, factor2, lse, *([o] if o is not None else []))
         ctx.H, ctx.N, ctx.eps = int(H), int(N), float(eps)
         ctx.exchange = _dp.active_exchange()
         return y
 
     @staticmethod
     def backward(ctx, grad_output):
-        x, wq, wk, wv, wg, wo, factor1, factor2, lse = ctx.saved_tensors
+        x, wq, wk, wv, wg, wo, factor1, factor2, lse = ctx.saved_tensors[:9]
+        o = ctx.saved_tensors[9] if ctx.save_o else None
         H, N, eps = ctx.H, ctx.N, ctx.eps
         dy = grad_output.to(torch.bfloat16).contiguous()
         _lib.poll_status(x.device)
@@ -98,8 +111,18 @@ class FusedAttentionFunction(torch.autograd.Function):
         ws_bytes = L.mea_backward_workspace_size(ctypes.byref(dims))
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         status = _lib.status_buffer(x.device)
-        args = (ctypes.byref(dims), _lib.ptr(x), _lib.ptr(wq), _lib.ptr(wk), _lib.ptr(wv), _lib.ptr(wg),
-                _lib.ptr(wo), _lib.ptr(factor1), _lib.ptr(factor2), _lib.ptr(lse), _lib.ptr(dy), _lib.ptr(dx))
+        head = (ctypes.byref(dims), _lib.ptr(x), _lib.ptr(wq), _lib.ptr(wk), _lib.ptr(wv), _lib.ptr(wg),
+                _lib.ptr(wo), _lib.ptr(factor1), _lib.ptr(factor2), _lib.ptr(lse))
+        fn = L.mea_block_backward_ex
+        if o is not None:  # the forward kept O: no attention recompute
+            fn = L.mea_block_backward_from_o
+            head = head + (_lib.ptr(o),)
+
+        def call(dw_bf16, dw32, ev_dwo=None, ev_dw=None):
+            _lib.check(fn(*head, _lib.ptr(dy), _lib.ptr(dx), *[_lib.ptr(d) for d in dw_bf16], _lib.ptr(df1),
+                          _lib.ptr(df2), _lib.ptr(dw32), _lib.ptr(ws), ws_bytes, _lib.ptr(status),
+                          _lib.stream_ptr(x.device), ev_dwo, ev_dw))
+
         sink = _dp.grad_sink_for((wq, wk, wv, wg, wo)) if all(ctx.needs_input_grad[1:6]) else None
         ex = ctx.exchange
         dws = None if sink is not None else [torch.empty_like(w) for w in (wq, wk, wv, wg, wo)]
@@ -108,28 +131,24 @@ class FusedAttentionFunction(torch.autograd.Function):
             # into its buffer (added when it already holds this step's gradient).
             dst, fresh = sink
             out = dst if fresh else torch.empty_like(dst)
-            _lib.check(L.mea_block_backward_ex(
-                *args, None, None, None, None, None, _lib.ptr(df1), _lib.ptr(df2), _lib.ptr(out), _lib.ptr(ws),
-                ws_bytes, _lib.ptr(status), _lib.stream_ptr(x.device), None, None))
+            call([None] * 5, out)
             if not fresh:
                 dst.add_(out)
             dws = [None] * 5
         elif ex is None:
-            _lib.check(L.mea_block_backward(
-                *args, *[_lib.ptr(d) for d in dws], _lib.ptr(df1), _lib.ptr(df2), None, _lib.ptr(ws), ws_bytes,
-                _lib.ptr(status), _lib.stream_ptr(x.device)))
+            call(dws, None)
         else:
-            _exchange_backward(L, args, dws, df1, df2, ws, ws_bytes, status, x, ex)
+            _exchange_backward(call, dws, x, ex)
         if _CHECK_STATUS:
             _lib.read_status(x.device)
         else:
             _lib.note_status(x.device)
         gf1 = df1.to(factor1.dtype) if want_df else None
         gf2 = df2.to(factor2.dtype) if want_df else None
-        return (dx, *dws, gf1, gf2, None, None, None)
+        return (dx, *dws, gf1, gf2, None, None, None, None)
 
 
-def _exchange_backward(L, args, dws, df1, df2, ws, ws_bytes, status, x, ex):
+def _exchange_backward(call, dws, x, ex):
     """Backward whose fp32 weight gradients are all-reduced across the exchange's
     group on a side stream, each part from the moment the library marks it
     final; the bf16 gradients are written from the reduced buffer on that
@@ -142,9 +161,7 @@ def _exchange_backward(L, args, dws, df1, df2, ws, ws_bytes, status, x, ex):
     ev_dwo, ev_dw = torch.cuda.Event(), torch.cuda.Event()
     ev_dwo.record(main)  # creates the events; the library records them again at the right points
     ev_dw.record(main)
-    _lib.check(L.mea_block_backward_ex(
-        *args, None, None, None, None, None, _lib.ptr(df1), _lib.ptr(df2), _lib.ptr(dw32), _lib.ptr(ws), ws_bytes,
-        _lib.ptr(status), _lib.stream_ptr(x.device), ev_dwo._as_parameter_, ev_dw._as_parameter_))
+    call([None] * 5, dw32, ev_dwo._as_parameter_, ev_dw._as_parameter_)
     dw32.record_stream(side)
     for d in dws:
         d.record_stream(side)
@@ -182,12 +199,14 @@ def record_exchange_waits(on: bool):
     return out
 
 
-def fused_attn(x, q_proj, k_proj, v_proj, g_proj, o_proj, yarn_module, H, N, eps=1e-6):
+def fused_attn(x, q_proj, k_proj, v_proj, g_proj, o_proj, yarn_module, H, N, eps=1e-6, save_o=False):
     """Gated causal attention block (fast_triton_attn.py:681-697).
 
     Reads ``.weight`` of the five bias-free ``nn.Linear`` projections and
     ``.factor1`` / ``.factor2`` of the rotary object, exactly as the reference.
+    ``save_o`` (default off) keeps the attention output for the backward
+    instead of recomputing it (see FusedAttentionFunction.forward).
     """
     return FusedAttentionFunction.apply(
         x, q_proj.weight, k_proj.weight, v_proj.weight, g_proj.weight, o_proj.weight,
-        yarn_module.factor1, yarn_module.factor2, H, N, eps)
+        yarn_module.factor1, yarn_module.factor2, H, N, eps, save_o)

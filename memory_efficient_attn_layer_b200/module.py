@@ -73,12 +73,15 @@ class Yarn(nn.Module):
 
 class CausalSoftmaxAttention(nn.Module):
     """The reference block module (README.md:6-68): five bias-free projections,
-    q/k/v/g: C -> H*N initialised U(+-0.5/sqrt(C)); o: H*N -> C zero-initialised."""
+    q/k/v/g: C -> H*N initialised U(+-0.5/sqrt(C)); o: H*N -> C zero-initialised.
+    ``save_o`` (default off) keeps the attention output for the backward
+    instead of recomputing it there."""
 
-    def __init__(self, input_dim: int, num_heads: int, head_dim: int):
+    def __init__(self, input_dim: int, num_heads: int, head_dim: int, save_o: bool = False):
         super().__init__()
         self.head_dim = head_dim
         self.num_heads = num_heads
+        self.save_o = save_o
         N, H, C = head_dim, num_heads, input_dim
         with torch.no_grad():
             bound = 0.5 / (C ** 0.5)
@@ -93,4 +96,4 @@ class CausalSoftmaxAttention(nn.Module):
 
     def forward(self, x: torch.Tensor, yarn) -> torch.Tensor:
         return fused_attn(x, self.q_proj, self.k_proj, self.v_proj, self.g_proj, self.o_proj, yarn,
-                          self.num_heads, self.head_dim)
+                          self.num_heads, self.head_dim, save_o=self.save_o)

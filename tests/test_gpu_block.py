@@ -18,13 +18,13 @@ Y_TOL = 2e-2
 COS_TOL = 0.999
 
 
-def run_block(inp, H, N, factor_grads=True):
+def run_block(inp, H, N, factor_grads=True, save_o=False):
     leaves = []
     for k in ("x", "wq", "wk", "wv", "wg", "wo", "f1", "f2"):
         t = inp[k].to(device=DEV, dtype=torch.bfloat16).contiguous()
         t.requires_grad_(k not in ("f1", "f2") or factor_grads)
         leaves.append(t)
-    y = FusedAttentionFunction.apply(*leaves, H, N, 1e-6)
+    y = FusedAttentionFunction.apply(*leaves, H, N, 1e-6, save_o)
     y.backward(inp["dy"].to(device=DEV, dtype=torch.bfloat16))
     torch.cuda.synchronize()
     out = {"y": y.detach().float().cpu()}
@@ -63,6 +63,20 @@ def test_block_matches_oracle_and_reference(case):
     # factor-table gradient rows beyond T are zero, as in the reference (fast_triton_attn.py:636-639)
     T = inp["x"].shape[1]
     assert torch.count_nonzero(got["df1"][T:]) == 0 and torch.count_nonzero(got["df2"][T:]) == 0
+
+
+@pytest.mark.parametrize("case", ["c1", "n64", "n128"])
+def test_block_save_o_matches_oracle_and_default(case):
+    """The keep-O ablation (the forward keeps the attention output, the backward
+    forms the gated tile from it instead of recomputing attention): same bars
+    against the oracle, and gradients within cosine 0.9999 of the default
+    memory-saving path (they differ only in where O is rounded to bf16)."""
+    (H, N), inp, _ = load_golden(case)
+    got = run_block(inp, H, N, save_o=True)
+    check(got, block_fwd_bwd(inp, H, N), ["y", *GRAD_NAMES])
+    default = run_block(inp, H, N)
+    assert torch.equal(got["y"], default["y"])  # the forward is the same computation
+    check(got, default, ["y", *GRAD_NAMES], cos_tol=0.9999)
 
 
 def test_block_nonorthogonal_table_is_exact():

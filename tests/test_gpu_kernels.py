@@ -115,10 +115,12 @@ def test_qkvg_forward(H, N, B, T):
 
 # ------------------------------------------------------------------ attention
 @pytest.mark.parametrize("N", [32, 64, 128])
-@pytest.mark.parametrize("T", [128, 384])
+@pytest.mark.parametrize("B,H,T", [(2, 2, 128), (2, 2, 384), (40, 8, 1152), (64, 8, 640)])
 @pytest.mark.parametrize("mag", [1.0, 3.0])
-def test_attention_forward(N, T, mag):
-    B, H = 2, 2
+def test_attention_forward(N, B, H, T, mag):
+    """Small grids (one work item per CTA) and grids with several work items per
+    persistent CTA: 40*8 heads x 5 pairs and 64*8 heads x 3 pairs (odd tile
+    counts, so one item of each head pairs with itself)."""
     q = bf16(unit_rms(rnd(B, H, T, N, seed=20)) * mag)
     k = bf16(unit_rms(rnd(B, H, T, N, seed=21)) * mag)
     v = bf16(rnd(B, H, T, N, seed=22))
