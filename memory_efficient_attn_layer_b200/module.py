@@ -32,10 +32,13 @@ class Yarn(nn.Module):
     (2i, 2i+1) by t*theta_i (fast_triton_attn.py:132-141) and scales by m.
 
     With ``scale == 1``: theta_i = base^(-2i/N), m = 1.
-    With ``scale > 1`` (YaRN): each frequency is interpolated between theta_i
-    and theta_i/scale by a linear ramp over its wavelength count in the
-    original context (``beta_fast`` .. ``beta_slow`` rotations), and
-    m = 0.1*ln(scale) + 1 unless ``mscale`` is given.
+    With ``scale > 1`` (YaRN, "NTK-by-parts"): pair i keeps theta_i (extrapolation)
+    below the correction range, takes theta_i/scale (interpolation) above it, and
+    is blended linearly in the pair index inside it.  The range runs from the
+    pair index that makes ``beta_fast`` rotations over the original context to
+    the one that makes ``beta_slow``, d(r) = N ln(L / (2 pi r)) / (2 ln base),
+    rounded outwards (floor / ceil) and clamped to [0, N-1], as in the published
+    YaRN reference code; m = 0.1*ln(scale) + 1 unless ``mscale`` is given.
     """
 
     def __init__(self, head_dim: int, max_seq: int, base: float = 10000.0, scale: float = 1.0,
@@ -49,12 +52,20 @@ class Yarn(nn.Module):
         m = 1.0
         if scale > 1.0:
             orig = original_max_seq or max_seq
-            rotations = orig * inv / (2 * math.pi)  # turns each pair makes over the original context
-            ramp = ((rotations - beta_slow) / (beta_fast - beta_slow)).clamp(0.0, 1.0)
-            inv = inv / scale * (1.0 - ramp) + inv * ramp
+
+            def corr_dim(rotations):  # pair-index coordinate d (in units of N) making `rotations` turns over orig
+                return head_dim * math.log(orig / (rotations * 2 * math.pi)) / (2 * math.log(base))
+
+            low = max(math.floor(corr_dim(beta_fast)), 0)
+            high = min(math.ceil(corr_dim(beta_slow)), head_dim - 1)
+            if low == high:
+                high += 0.001
+            ramp = ((torch.arange(head_dim // 2, dtype=torch.float64) - low) / (high - low)).clamp(0.0, 1.0)
+            inv = inv / scale * ramp + inv * (1.0 - ramp)
             m = 0.1 * math.log(scale) + 1.0
         if mscale is not None:
             m = mscale
+        self.inv_freq, self.mscale = inv, m
         ang = torch.arange(max_seq, dtype=torch.float64)[:, None] * inv[None, :]
         c, s = torch.cos(ang) * m, torch.sin(ang) * m
         f1 = torch.stack([c, c], dim=-1).reshape(max_seq, head_dim)

@@ -40,3 +40,28 @@ def test_yarn_scaling_interpolates_low_frequencies():
     ang = lambda t: torch.atan2(t.factor2[1, 1::2], t.factor1[1, ::2])
     assert math.isclose(float(ang(ext)[0]), float(ang(base)[0]), rel_tol=1e-9)
     assert math.isclose(float(ang(ext)[-1]), float(ang(base)[-1]) / 4.0, rel_tol=1e-6)
+
+
+def test_yarn_frequencies_match_published_implementation():
+    """YaRN "NTK-by-parts" frequencies and attention factor pinned to the YaRN
+    implementation shipped in transformers (modeling_rope_utils._compute_yarn_parameters):
+    same correction range (floor/ceil of the pair-index coordinates of beta_fast and
+    beta_slow rotations over the original context), same linear ramp in the pair
+    index, same magnitude 0.1 ln(scale) + 1."""
+    import pytest
+
+    tr = pytest.importorskip("transformers")
+    from transformers.modeling_rope_utils import _compute_yarn_parameters
+
+    for head_dim, scale, orig, base, bf, bs in [(64, 4.0, 2048, 10000.0, 32.0, 1.0), (128, 8.0, 4096, 500000.0, 32.0, 1.0),
+                                                (32, 2.0, 1024, 10000.0, 16.0, 2.0)]:
+        cfg = tr.LlamaConfig(hidden_size=head_dim * 4, num_attention_heads=4, head_dim=head_dim,
+                             max_position_embeddings=int(orig * scale),
+                             rope_parameters={"rope_type": "yarn", "rope_theta": base, "factor": scale,
+                                              "original_max_position_embeddings": orig, "beta_fast": bf,
+                                              "beta_slow": bs})
+        want_inv, want_att = _compute_yarn_parameters(cfg)
+        y = Yarn(head_dim, 64, base=base, scale=scale, original_max_seq=orig, beta_fast=bf, beta_slow=bs,
+                 dtype=torch.float32)
+        assert torch.allclose(y.inv_freq.float(), want_inv.float(), rtol=2e-6, atol=0), (head_dim, scale)
+        assert math.isclose(y.mscale, want_att, rel_tol=1e-12)
