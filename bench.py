@@ -116,7 +116,7 @@ class ClockSampler:
             master, slave = pty.openpty()
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=slave, stderr=subprocess.DEVNULL, close_fds=True)
+                 "-lms", "100"], stdout=slave, stderr=subprocess.DEVNULL, close_fds=True)
             os.close(slave)
         except OSError:
             self.proc = None
@@ -571,11 +571,11 @@ def run_gpu(args, cfg, rank, world, device):
             exchange_wait = {"ms_per_step": sum(waits) / len(waits), "max_ms": max(waits), "steps": len(waits),
                              "what": "time the caller's stream waited at the end of the backward for the "
                                      "side stream's all-reduce of the weight gradients (0 = fully overlapped)"}
-    # A short timed region can end before nvidia-smi has taken two samples in it: then the same steps
-    # keep running (untimed, at most 2 s) until it has, and the clocks cover that span too.
+    # A short timed region can end before nvidia-smi has taken enough samples in it: then the same steps
+    # keep running (untimed, at most 2 s) until it has five, and the clocks cover that span too.
     # Every rank runs the same number of these steps (their collectives must pair up).
     while True:
-        need = clocks.proc is not None and clocks.in_window(t_wall0, time.time()) < 2 and time.time() - t_wall1 < 2.0
+        need = clocks.proc is not None and clocks.in_window(t_wall0, time.time()) < 5 and time.time() - t_wall1 < 2.0
         if world > 1:
             f = torch.tensor([1 if need else 0], device=device, dtype=torch.int32)
             dist.all_reduce(f, op=dist.ReduceOp.MAX)
