@@ -447,6 +447,50 @@ def run_stack(args, cfg, device):
     }), flush=True)
 
 
+def run_gemm_e4m3(args, cfg, device):
+    """e4m3 against bf16 operands in the same CTA-pair GEMM (mea_gemm_e4m3 / mea_gemm, K-major A and B, fp32
+    out) on the block's long GEMM shapes at this config: the FP8-projection row's measurement.  Prints one
+    JSON line (not a bench line of the block metric)."""
+    import ctypes
+
+    from memory_efficient_attn_layer_b200 import _lib
+
+    L = _lib.lib()
+    B, T, C, H, N = (cfg[k] for k in ("B", "T", "C", "H", "N"))
+    M, HN = B * T, H * N
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    st = lambda: ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    rows = []
+    for (m, n, k, what) in [(M, C, 4 * HN, "dx = dAcc [W_q;W_k;W_v;W_g] shape"), (M, 4 * HN, C, "q/k/v/g projection shape")]:
+        out = torch.empty(m, n, device=device)
+        res = {"shape": what, "M": m, "N": n, "K": k}
+        for kind in ("bf16", "e4m3"):
+            if kind == "bf16":
+                a = torch.randn(m, k, device=device).bfloat16()
+                b = torch.randn(n, k, device=device).bfloat16()
+                fn = lambda: _lib.check(L.mea_gemm(m, n, k, P(a), k, 0, P(b), k, 0, P(out), n, 0, None, st()))
+            else:
+                a = torch.randn(m, k, device=device).to(torch.float8_e4m3fn)
+                b = torch.randn(n, k, device=device).to(torch.float8_e4m3fn)
+                fn = lambda: _lib.check(L.mea_gemm_e4m3(m, n, k, P(a), k, P(b), k, P(out), n, 0, None, st()))
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize(device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize(device)
+            ms = e0.elapsed_time(e1) / args.steps
+            res[kind] = {"ms": ms, "tflops": 2 * m * n * k / (ms / 1e3) / 1e12}
+            del a, b
+        res["speedup"] = res["bf16"]["ms"] / res["e4m3"]["ms"]
+        rows.append(res)
+    print(json.dumps({"probe": "e4m3 vs bf16 operands, CTA-pair tcgen05 GEMM, fp32 output",
+                      "config": cfg["name"], "rows": rows}), flush=True)
+
+
 def run_gpu(args, cfg, rank, world, device):
     import torch.distributed as dist
 
@@ -767,6 +811,9 @@ def main():
     ap.add_argument("--optim", action="store_true",
                     help="end every step with the ShardedAdamW update (reduce-scatter, fused AdamW kernel, "
                          "all-gather) instead of the gradient all-reduce")
+    ap.add_argument("--gemm-e4m3", action="store_true",
+                    help="probe: the e4m3 GEMM against the bf16 one on this config's GEMM shapes (one GPU; not a "
+                         "bench line)")
     ap.add_argument("--stack", type=int, default=0,
                     help="model-level mode: a stack of this many block + MLP layers (memory and tokens/s of the "
                          "caller; one GPU; not a bench line)")
@@ -796,6 +843,9 @@ def main():
             if world > 1:
                 raise SystemExit("--stack runs on one GPU")
             run_stack(args, cfg, device)
+            return
+        if args.gemm_e4m3:
+            run_gemm_e4m3(args, cfg, device)
             return
         run_gpu(args, cfg, rank, world, device)
     finally:

@@ -159,6 +159,17 @@ int mea_attention_forward(int B, int H, int T, int N, const void* q, const void*
 int mea_gemm(int M, int N, int K, const void* a, long long lda, int a_mn, const void* b, long long ldb, int b_mn,
              float* out, long long ldo, int accumulate, int* status, void* stream);
 
+/* e4m3 GEMM (no counterpart in the reference, which computes its projections
+ * in bf16): out[M,N] = sum_k A[m,k] B[n,k] with A [M,K] and B [N,K] both
+ * K-major e4m3 (one byte per element, row pitches lda/ldb in elements, multiples
+ * of 16), fp32 accumulate, written as fp32 (out_bf16 = 0) or bf16.  No
+ * scaling is applied: callers multiply by their per-tensor scales.  M % 128,
+ * N % 128 and K % 128 must be zero.  The block does not use it: e4m3's 3-bit
+ * mantissa costs ~3.5% max-relative error per projection GEMM, above the
+ * block's 2e-2 output tolerance. */
+int mea_gemm_e4m3(int M, int N, int K, const void* a, long long lda, const void* b, long long ldb, void* out,
+                  long long ldo, int out_bf16, int* status, void* stream);
+
 /* o_proj backward + gate backward (fast_triton_attn.py:576-584, :601):
  * dGated = dy * wo, then dO = dGated*gs ([B,H,T,N]), dg_pre = dGated*o*gs*(1-gs)
  * into dg[(b*T+t)*ld_dg + h*N + n], delta[B,H,T] = rowsum(dO*o) (fp32). */

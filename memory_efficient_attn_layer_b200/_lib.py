@@ -56,6 +56,7 @@ SIGNATURES = {
     "mea_qkvg_forward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "mea_attention_forward": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "mea_gemm": (_I, [_I, _I, _I, _P, _LL, _I, _P, _LL, _I, _P, _LL, _I, _P, _P]),
+    "mea_gemm_e4m3": (_I, [_I, _I, _I, _P, _LL, _P, _LL, _P, _LL, _I, _P, _P]),
     "mea_gate_backward": (_I, [_D, _P, _P, _P, _P, _P, _P, _LL, _P, _P, _P]),
     "mea_attention_backward": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P]),
     "mea_qk_norm_rope_backward": (_I, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _LL, _P, _P, _P]),

@@ -635,6 +635,33 @@ int mea_gemm(int M, int N, int K, const void* a, long long lda, int a_mn, const 
   return run_gemm(L, p, static_cast<cudaStream_t>(stream));
 }
 
+int mea_gemm_e4m3(int M, int N, int K, const void* a, long long lda, const void* b, long long ldb, void* out,
+                  long long ldo, int out_bf16, int* status, void* stream) {
+  if (!a || !b || !out) return set_error(MEA_ERR_INVALID_ARGUMENT, "mea_gemm_e4m3: NULL operand");
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(out)) & 15 ||
+      lda % 16 || ldb % 16 || ldo % (out_bf16 ? 8 : 4))
+    return set_error(MEA_ERR_ALIGNMENT, "mea_gemm_e4m3: operands 16-byte aligned with 16-byte row pitches");
+  GemmLaunch L{};
+  L.M = M;
+  L.N = N;
+  L.K = K;
+  L.bn = pick_bn(N);
+  L.amode = A_K;
+  L.bmode = B_K;
+  L.epi = out_bf16 ? EPI_BF16 : EPI_F32;
+  L.e4m3 = true;
+  L.a = a;
+  L.lda = lda;
+  L.b[0] = b;
+  L.ldb = ldb;
+  L.k_splits = 1;
+  L.out[0] = out;
+  L.ldo = ldo;
+  GemmParams p{};
+  p.status = status;
+  return run_gemm(L, p, static_cast<cudaStream_t>(stream));
+}
+
 int mea_gate_backward(const mea_block_dims* d, const void* dy, const void* wo, const void* o, const void* gs,
                       void* dO, void* dg, long long ld_dg, float* delta, int* status, void* stream) {
   MEA_TRY(validate(d));

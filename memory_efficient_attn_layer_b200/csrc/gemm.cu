@@ -9,10 +9,10 @@ namespace mea {
 
 // Persistent grid: one 2-CTA cluster per SM pair that can hold one, at most one
 // per work unit.
-template <int BN, int AM, int BMD, int EPI, int HD>
+template <int BN, int AM, int BMD, int EPI, int HD, bool E4M3 = false>
 static int launch_gemm_t(const GemmMaps& maps, const GemmParams& p, cudaStream_t st) {
   using Cfg = GemmCfg<BN, EPI, HD>;
-  auto kern = gemm_kernel<BN, AM, BMD, EPI, HD>;
+  auto kern = gemm_kernel<BN, AM, BMD, EPI, HD, E4M3>;
   if (!smem_attr_set(reinterpret_cast<const void*>(kern), int(Cfg::SMEM)))
     return set_error(MEA_ERR_CUDA, "cudaFuncSetAttribute(gemm) failed");
   cudaLaunchAttribute attr[1];
@@ -26,10 +26,10 @@ static int launch_gemm_t(const GemmMaps& maps, const GemmParams& p, cudaStream_t
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  static int max_pairs[64] = {0};  // per device
+  static int max_pairs[2][64] = {{0}};  // per instantiation kind and device
   int dev = 0;
   cudaGetDevice(&dev);
-  int& mp = max_pairs[dev & 63];
+  int& mp = max_pairs[E4M3 ? 1 : 0][dev & 63];
   if (mp <= 0) {
     cfg.gridDim = dim3(2 * (num_sms() / 2));
     int n = 0;
@@ -43,8 +43,8 @@ static int launch_gemm_t(const GemmMaps& maps, const GemmParams& p, cudaStream_t
   cfg.gridDim = dim3(2 * (units < mp ? units : mp));
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, p);
   char what[112];
-  snprintf(what, sizeof(what), "gemm_kernel<%d,%d,%d,%d,%d> M=%d N=%d K=%d splits=%d", BN, AM, BMD, EPI, HD, p.M, p.N,
-           p.K, p.k_splits);
+  snprintf(what, sizeof(what), "gemm_kernel<%d,%d,%d,%d,%d%s> M=%d N=%d K=%d splits=%d", BN, AM, BMD, EPI, HD,
+           E4M3 ? ",e4m3" : "", p.M, p.N, p.K, p.k_splits);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return set_error(MEA_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
@@ -63,7 +63,17 @@ static int launch_gemm_t(const GemmMaps& maps, const GemmParams& p, cudaStream_t
     if (p.hd == 128) return launch_gemm_t<BN_, AM_, BMD_, EPI_, 128>(maps, p, st); \
   }
 
-static int dispatch(int bn, int am, int bmd, int epi, const GemmMaps& maps, const GemmParams& p, cudaStream_t st) {
+static int dispatch(int bn, int am, int bmd, int epi, bool e4m3, const GemmMaps& maps, const GemmParams& p,
+                    cudaStream_t st) {
+  if (e4m3) {  // e4m3 operands: K-major A and B, fp32 or bf16 output
+    if (am == A_K && bmd == B_K && epi == EPI_F32)
+      return bn == 256 ? launch_gemm_t<256, A_K, B_K, EPI_F32, 0, true>(maps, p, st)
+                       : launch_gemm_t<128, A_K, B_K, EPI_F32, 0, true>(maps, p, st);
+    if (am == A_K && bmd == B_K && epi == EPI_BF16)
+      return bn == 256 ? launch_gemm_t<256, A_K, B_K, EPI_BF16, 0, true>(maps, p, st)
+                       : launch_gemm_t<128, A_K, B_K, EPI_BF16, 0, true>(maps, p, st);
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: e4m3 operands need K-major A and B and an fp32/bf16 output");
+  }
   // forward: fused projections, o_proj
   MEA_GEMM_CASE_HD(256, A_K, B_SLABS, EPI_QKVG)
   MEA_GEMM_CASE(256, A_K, B_K, EPI_BF16)
@@ -99,15 +109,23 @@ static int hd_map(CUtensorMap* m, const void* base, uint64_t rows, int hd, uint6
 
 int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
   const int bn = L.bn;
+  // K elements per 128-byte stage row: 64 bf16 or 128 e4m3
+  const int kbe = L.e4m3 ? 2 * GEMM_BK : GEMM_BK;
+  const int eb = L.e4m3 ? 1 : 2;  // operand element bytes
   if (bn != 128 && bn != 256) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: bn must be 128 or 256");
-  if (L.M % GEMM_BM || L.N % bn || L.K % GEMM_BK || L.M <= 0 || L.N <= 0 || L.K <= 0)
-    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: M=%d N=%d K=%d must be multiples of 128/%d/64", L.M, L.N, L.K, bn);
+  if (L.M % GEMM_BM || L.N % bn || L.K % kbe || L.M <= 0 || L.N <= 0 || L.K <= 0)
+    return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: M=%d N=%d K=%d must be multiples of 128/%d/%d", L.M, L.N, L.K,
+                     bn, kbe);
+  if (L.e4m3 && (L.amode != A_K || L.bmode != B_K))
+    return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: e4m3 operands must both be K-major");
   GemmMaps maps;
   memset(&maps, 0, sizeof(maps));
   const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
   int rc;
   // A operand (this CTA's 128 rows): K-major [M rows, K] or MN-major [K rows, M]
-  if (L.amode == A_K)
+  if (L.e4m3)
+    rc = make_tmap_2d(&maps.a, L.a, L.K, L.M, uint64_t(L.lda) * eb, kbe, 128, sw, CU_TENSOR_MAP_DATA_TYPE_UINT8);
+  else if (L.amode == A_K)
     rc = make_tmap_2d(&maps.a, L.a, L.K, L.M, uint64_t(L.lda) * 2, 64, 128, sw);
   else
     rc = make_tmap_2d(&maps.a, L.a, L.M, L.K, uint64_t(L.lda) * 2, 64, 64, sw);
@@ -117,7 +135,10 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
   for (int i = 0; i < nb; ++i) {
     const void* src = L.b[i];
     if (!src) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: B tensor %d is null", i);
-    if (L.bmode == B_K)
+    if (L.e4m3)
+      rc = make_tmap_2d(&maps.b[i], src, L.K, L.N, uint64_t(L.ldb) * eb, kbe, bn / 2, sw,
+                        CU_TENSOR_MAP_DATA_TYPE_UINT8);
+    else if (L.bmode == B_K)
       rc = make_tmap_2d(&maps.b[i], src, L.K, L.N, uint64_t(L.ldb) * 2, 64, bn / 2, sw);
     else if (L.bmode == B_MN)
       rc = make_tmap_2d(&maps.b[i], src, L.N, L.K, uint64_t(L.ldb) * 2, 64, 64, sw);
@@ -168,7 +189,7 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
   p.K = L.K;
   p.m_pairs = (L.M / GEMM_BM + 1) / 2;
   p.n_tiles = L.N / bn;
-  p.kb_total = L.K / GEMM_BK;
+  p.kb_total = L.K / kbe;
   int splits = L.k_splits < 1 ? 1 : L.k_splits;
   if (splits > p.kb_total) splits = p.kb_total;
   p.kb_per_split = (p.kb_total + splits - 1) / splits;
@@ -183,7 +204,7 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
     return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: K must be 4 x rows of each B tensor");
   if ((L.epi == EPI_QKVG || L.epi == EPI_DGATE) && (p.T % GEMM_BM || L.M % p.T))
     return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: per-head epilogue needs T %% 128 == 0 and M %% T == 0");
-  return dispatch(bn, L.amode, L.bmode, L.epi, maps, p, st);
+  return dispatch(bn, L.amode, L.bmode, L.epi, L.e4m3, maps, p, st);
 }
 
 // Split count for a long-K GEMM with few output tiles.  Each CTA pair runs

@@ -523,13 +523,19 @@ __device__ __forceinline__ void epi_dgate(const GemmMaps& maps, const GemmParams
 // The kernel (launched as 2-CTA clusters)
 // ---------------------------------------------------------------------------
 // HD: head dim for the per-head epilogues (EPI_QKVG, EPI_DGATE), 0 otherwise.
-template <int BN, int AM, int BMD, int EPI, int HD>
+// E4M3: e4m3 operands (both K-major).  A stage still holds 128-byte rows, i.e.
+// 2 * GEMM_BK one-byte elements of K, so only the K coordinate of the loads and
+// the MMA kind change.
+template <int BN, int AM, int BMD, int EPI, int HD, bool E4M3 = false>
 __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
     gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
   using Cfg = GemmCfg<BN, EPI, HD>;
   constexpr int STAGES = Cfg::STAGES;
+  static_assert(!E4M3 || (AM == A_K && BMD == B_K), "e4m3 GEMM: K-major operands only");
+  constexpr int KBE = E4M3 ? 2 * GEMM_BK : GEMM_BK;  // K elements per stage
   constexpr uint32_t IDESC =
-      idesc_bf16(2 * GEMM_BM, BN, AM == A_MN ? 1u : 0u, (BMD == B_MN || BMD == B_MN_KSPLIT4) ? 1u : 0u);
+      E4M3 ? idesc_e4m3(2 * GEMM_BM, BN)
+           : idesc_bf16(2 * GEMM_BM, BN, AM == A_MN ? 1u : 0u, (BMD == B_MN || BMD == B_MN_KSPLIT4) ? 1u : 0u);
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
   constexpr int HB = BN / 2;  // B columns staged by each CTA
 
@@ -607,13 +613,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
           const uint32_t a_dst = sA + stage * GEMM_A_BYTES;
           const uint32_t b_dst = sB + stage * Cfg::B_BYTES;
           if (AM == A_K) {
-            tma_load_2d_pair(a_dst, &maps.a, fb, kb * GEMM_BK, mc);
+            tma_load_2d_pair(a_dst, &maps.a, fb, kb * KBE, mc);
           } else {
             tma_load_2d_pair(a_dst, &maps.a, fb, mc, kb * GEMM_BK);
             tma_load_2d_pair(a_dst + 8192, &maps.a, fb, mc + 64, kb * GEMM_BK);
           }
           if (BMD == B_K) {
-            tma_load_2d_pair(b_dst, &maps.b[0], fb, kb * GEMM_BK, nc);
+            tma_load_2d_pair(b_dst, &maps.b[0], fb, kb * KBE, nc);
           } else if (BMD == B_MN) {
 #pragma unroll
             for (int i = 0; i < HB / 64; ++i)
@@ -678,7 +684,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
                                           : smem_desc(a_base + 2048 * k, 8192, 1024, SW_128B);
             const uint64_t bd = (BMD == B_K || BMD == B_SLABS) ? smem_desc(b_base + 32 * k, 16, 1024, SW_128B)
                                                                 : smem_desc(b_base + 2048 * k, 8192, 1024, SW_128B);
-            mma_ss_pair(d, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+            if constexpr (E4M3)
+              mma_ss_pair_e4m3(d, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+            else
+              mma_ss_pair(d, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           any = true;
           mma_commit_pair(empty_bar(stage), 0x3);

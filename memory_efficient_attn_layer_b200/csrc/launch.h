@@ -45,6 +45,7 @@ struct GemmLaunch {
   const void* in[2];
   long long ldin;
   int in_rows;
+  bool e4m3;  // A and B are e4m3 (K-major only; EPI_F32 / EPI_BF16)
 };
 int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st);
 int auto_splits(int m_tiles, int n_tiles, int kb_total, int waves);

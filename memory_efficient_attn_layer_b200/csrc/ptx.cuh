@@ -285,6 +285,16 @@ __device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, ui
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
+// The same with e4m3 operands (kind::f8f6f4): 32 one-byte elements per k-step,
+// i.e. the same 32 bytes of a 128-byte swizzled row as one bf16 k-step.
+__device__ __forceinline__ void mma_ss_pair_e4m3(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
 // Arrive once on the mbarrier at offset `bar` of every CTA in `cta_mask` when
 // the issuing thread's earlier tcgen05 ops complete.
 __device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask) {
@@ -390,6 +400,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16(uint32_t M, uint32_t N, uint32
          | (a_mn << 15) | (b_mn << 16)
          | ((N >> 3) << 17)   // N / 8
          | ((M >> 4) << 24);  // M / 16
+}
+
+// Instruction descriptor for kind::f8f6f4 with e4m3 A and B (format code 0),
+// fp32 D, both operands K-major, M x N tile.
+__host__ __device__ constexpr uint32_t idesc_e4m3(uint32_t M, uint32_t N) {
+  return (1u << 4) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
 // ----------------------------------------------------------------------------

@@ -98,3 +98,11 @@ def test_block_forward_rejects_misaligned_output_before_device_work(L):
     args[9] = ctypes.c_void_p(0x7000002)  # y
     rc = L.mea_block_forward(*args, need, None, None)
     assert rc == 3 and b"tensor argument 8" in L.mea_last_error_string()
+
+
+def test_gemm_e4m3_rejects_bad_arguments_before_device_work(L):
+    a, b, o = (ctypes.c_void_p(0x100000 * i) for i in (1, 2, 3))
+    assert L.mea_gemm_e4m3(256, 256, 192, a, 192, b, 192, o, 256, 0, None, None) == 2  # K % 128
+    assert b"multiples" in L.mea_last_error_string()
+    assert L.mea_gemm_e4m3(256, 256, 256, ctypes.c_void_p(0x100008), 256, b, 256, o, 256, 0, None, None) == 3
+    assert L.mea_gemm_e4m3(256, 256, 256, None, 256, b, 256, o, 256, 0, None, None) == 1

@@ -226,3 +226,21 @@ def test_qk_norm_rope_backward(H, N, mscale):
         got = dacc[:, slot * HN:(slot + 1) * HN].float().view(B, T, H, N).transpose(1, 2)
         assert cos(got, want) > 0.999 and maxrel(got, want) < 3e-2, slot
     assert cos(df1, F1.grad) > 0.999 and cos(df2, F2.grad) > 0.999
+
+
+# ------------------------------------------------------------------ e4m3 GEMM
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (384, 128, 640), (1024, 512, 2048), (512, 768, 1024)])
+@pytest.mark.parametrize("out_bf16", [0, 1])
+def test_gemm_e4m3(M, N, K, out_bf16):
+    """e4m3 operands (kind::f8f6f4 on CTA pairs) against torch's fp32 product of the
+    same e4m3 values: the products are exact in fp32, so an fp32 output agrees to
+    accumulation-order rounding and a bf16 output to its own rounding."""
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    a = torch.randn(M, K, device=DEV, generator=g).to(torch.float8_e4m3fn)
+    b = torch.randn(N, K, device=DEV, generator=g).to(torch.float8_e4m3fn)
+    out = torch.full((M, N), float("nan"), device=DEV, dtype=torch.bfloat16 if out_bf16 else torch.float32)
+    s = status()
+    call("mea_gemm_e4m3", M, N, K, P(a), K, P(b), K, P(out), N, out_bf16, P(s), stream(), status_buf=s)
+    want = a.float() @ b.float().t()
+    assert torch.isfinite(out.float()).all()
+    assert maxrel(out.float(), want) < (1e-2 if out_bf16 else 1e-5)
