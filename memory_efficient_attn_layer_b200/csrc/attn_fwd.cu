@@ -10,11 +10,8 @@
 // other CTA's MMAs keep the tensor core busy, and one CTA's prologue/epilogue
 // overlaps the other's main loop.  Warp 0 loads Q once and streams K and V
 // through separate TMA rings; warp 1 issues S_j = Q K_j^T and O += P_j V_j with
-// P read straight from TMEM; the softmax runs one query row per thread: for
-// N <= 64 two warpgroups (warps 2..5 and 6..9) each take one 64-key half of
-// every score tile, concurrently (16 softmax warps per SM keep the exp pipes
-// busier than 8: 15.8 against 13.5 exps/clk/SM measured), for N = 128 warps
-// 2..5 take whole rows.  Key tiles above the diagonal are never loaded (causal skipping); the
+// P read straight from TMEM; warps 2..5 run the softmax, one query row per
+// thread.  Key tiles above the diagonal are never loaded (causal skipping); the
 // diagonal tile is masked.
 //
 // TMEM, N <= 64: S [0,128), P [128,192), O [192, 192+N).  S_j is computed in
@@ -72,16 +69,7 @@ struct AttnFwdCfg {
   static constexpr bool SEP_P = HD <= 64;  // P in its own TMEM columns
   static constexpr uint32_t S_COL = 0, P_COL = SEP_P ? 128 : 0, O_COL = SEP_P ? 192 : 128;
   static constexpr uint32_t TMEM_COLS = 256;
-  // N <= 64: two softmax warpgroups, one per 64-key half of every score tile
-  // (warps 2..5 keys [0, 64), warps 6..9 keys [64, 128)); N = 128: one.
-  static constexpr int SOFTMAX_GROUPS = SEP_P ? 2 : 1;
-  static constexpr int THREADS = 64 + 128 * SOFTMAX_GROUPS;
-  // (SEP_P) after the barriers: the half-row maxima of the online-max fallback
-  // ([2 tiles][2 halves][128 rows] fp32) and the second half's row sums.
-  static constexpr uint32_t OFF_BAR = TILE_BYTES * (1 + KS + VS);
-  static constexpr uint32_t OFF_XCH = OFF_BAR + 256;
-  static constexpr uint32_t OFF_LSUM = OFF_XCH + 2 * 2 * 128 * 4;
-  static constexpr size_t SMEM = 1024 + OFF_LSUM + 512;
+  static constexpr size_t SMEM = 1024 + TILE_BYTES * (1 + KS + VS) + 256;
 };
 
 // Max of 16 raw scores of key columns [16c, 16c+16) into four chains.
@@ -116,25 +104,6 @@ __device__ __forceinline__ float score_row_max(uint32_t sb, int r) {
     if (c + 2 < 8) tmem_ld16(sb + 16 * (c + 2), a);
     max_chunk<DIAG>(b, c + 1, r, m);
     if (c + 2 < 8) tmem_wait_ld_tied(a);
-  }
-  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
-}
-
-// Max of key columns [64*hh, 64*hh + 64) of row r (raw scores), same streaming.
-template <bool DIAG>
-__device__ __forceinline__ float score_half_max(uint32_t sb, int hh, int r) {
-  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-  uint32_t a[16], b[16];
-  tmem_ld16(sb + 64 * hh, a);
-  tmem_wait_ld_tied(a);
-#pragma unroll
-  for (int c = 0; c < 4; c += 2) {
-    tmem_ld16(sb + 64 * hh + 16 * (c + 1), b);
-    max_chunk<DIAG>(a, 4 * hh + c, r, m);
-    tmem_wait_ld_tied(b);
-    if (c + 2 < 4) tmem_ld16(sb + 64 * hh + 16 * (c + 2), a);
-    max_chunk<DIAG>(b, 4 * hh + c + 1, r, m);
-    if (c + 2 < 4) tmem_wait_ld_tied(a);
   }
   return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
 }
@@ -226,8 +195,7 @@ __device__ __forceinline__ float exp_half_regs(uint32_t sb, int hh, int r, float
 }
 
 template <int HD>
-__global__ void __launch_bounds__(AttnFwdCfg<HD>::THREADS, 2)
-    attn_fwd_kernel(const __grid_constant__ AttnFwdMaps maps, const AttnFwdParams p) {
+__global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ AttnFwdMaps maps, const AttnFwdParams p) {
   using Cfg = AttnFwdCfg<HD>;
   using Tile = HeadTile<HD>;
   constexpr int KS = Cfg::KS, VS = Cfg::VS;
@@ -261,12 +229,6 @@ __global__ void __launch_bounds__(AttnFwdCfg<HD>::THREADS, 2)
   const uint32_t q_free = s_full + 64;  // (SEP_P) the last score MMA has read Q
   const uint32_t gs_bar = s_full + 72;  // (SEP_P) sigmoid(g) tile landed in Q's buffer
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11 + 2 * KS + 2 * VS);
-  // (SEP_P) the online-max fallback's half-row maxima of lane quarter q, tile
-  // parity b, written (both groups' warps of that quarter arrive): xch_bar(b, q);
-  // the second group's row sums written for the epilogue: lsum_bar.
-  auto xch_bar = [&](int b, int q) { return b0 + 8u * (12 + 2 * KS + 2 * VS + 4 * b + q); };
-  const uint32_t lsum_bar = b0 + 8u * (20 + 2 * KS + 2 * VS);
-  static_assert(8 * (21 + 2 * KS + 2 * VS) <= 256, "attention forward: barrier region");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -291,7 +253,7 @@ __global__ void __launch_bounds__(AttnFwdCfg<HD>::THREADS, 2)
       mbar_init(v_empty(s), 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 128 * Cfg::SOFTMAX_GROUPS);
+    mbar_init(p_full, 128);
     mbar_init(o_bar, 1);
     mbar_init(drain_bar, 1);
     mbar_init(s_empty, 128);
@@ -300,9 +262,6 @@ __global__ void __launch_bounds__(AttnFwdCfg<HD>::THREADS, 2)
     mbar_init(s_empty_b, 128);
     mbar_init(q_free, 1);
     mbar_init(gs_bar, 1);
-    for (int b = 0; b < 2; ++b)
-      for (int q = 0; q < 4; ++q) mbar_init(xch_bar(b, q), 64);
-    mbar_init(lsum_bar, 128);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -453,7 +412,6 @@ __global__ void __launch_bounds__(AttnFwdCfg<HD>::THREADS, 2)
   } else {
     // ---------------- softmax + epilogue: warps 2..5 ----------------
     const int quarter = warp & 3;
-    const int hh = Cfg::SEP_P ? (warp - 2) >> 2 : 0;  // key half of this softmax group
     const int r = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
@@ -474,33 +432,26 @@ __global__ void __launch_bounds__(AttnFwdCfg<HD>::THREADS, 2)
     }
     float m_run = -INFINITY, l_run = 0.f;  // m_run in scaled log2 units
     bool ok = true;
-    bool run_epi = true;  // (SEP_P) only the first softmax group runs the epilogue
     if constexpr (Cfg::SEP_P) {
-      // Group hh turns key half hh of every score tile into bf16 P: it waits for
-      // its own half of S_j (s_full / s_full_b), releases it (s_empty /
-      // s_empty_b) once its exponentials are done, and writes its P columns once
-      // PV_{j-1} has consumed the previous P; p_full counts both groups.  Each
-      // group keeps the row sum of its half.  The online-max fallback exchanges
-      // the two half-row maxima of each row through shared memory, so both
-      // groups make the same rescaling decision; each rescales half of O.
+      // S_j arrives in two 64-key halves; each half is released (s_empty,
+      // s_empty_b) as soon as its exponentials are done, and its bf16 P
+      // columns are written right away (once PV_{j-1} has consumed the
+      // previous P).
       const uint32_t sb = lane_base + Cfg::S_COL;
-      const uint32_t full_h = hh ? s_full_b : s_full;
-      const uint32_t empty_h = hh ? s_empty_b : s_empty;
-      float* xch = reinterpret_cast<float*>(smem + Cfg::OFF_XCH);  // [tile parity][half][row]
       for (int j = 0; j < nkv && ok; ++j) {
-        ok = __all_sync(0xffffffffu, mbar_wait(full_h, j & 1, g, hh ? 17 : 6));
+        ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, g, 6));
         if (!ok) break;
         tc_fence_after();
         const bool diag = (j == qt);
         bool pv_seen = (j == 0);  // PV_{j-1} has completed (O and the P columns are free)
+        bool have_b = false;      // the half [64, 128) of S_j has landed
         if (mode == 0) {
-          const float hm = (diag ? score_half_max<true>(sb, hh, r) : score_half_max<false>(sb, hh, r)) * sl2;
-          float* xb = xch + (j & 1) * 256;
-          xb[hh * 128 + r] = hm;
-          mbar_arrive(xch_bar(j & 1, quarter));
-          ok = __all_sync(0xffffffffu, mbar_wait(xch_bar(j & 1, quarter), uint32_t((j >> 1) & 1), g, 21));
+          // The online max needs the whole score row.
+          ok = __all_sync(0xffffffffu, mbar_wait(s_full_b, j & 1, g, 17));
           if (!ok) break;
-          const float mx = fmaxf(xb[r], xb[128 + r]);
+          tc_fence_after();
+          have_b = true;
+          const float mx = (diag ? score_row_max<true>(sb, r) : score_row_max<false>(sb, r)) * sl2;
           // Lazy rescale: refresh the reference max only when it grows by > 8 (log2 units).
           const bool need = mx > m_run + 8.0f;
           if (__any_sync(0xffffffffu, need)) {
@@ -512,7 +463,7 @@ __global__ void __launch_bounds__(AttnFwdCfg<HD>::THREADS, 2)
               tc_fence_after();
               pv_seen = true;
 #pragma unroll
-              for (int c = hh * (HD / 2); c < (hh + 1) * (HD / 2); c += 16) {
+              for (int c = 0; c < HD; c += 16) {
                 uint32_t ov[16];
                 tmem_load16(lane_base + Cfg::O_COL + c, ov);
 #pragma unroll
@@ -526,9 +477,10 @@ __global__ void __launch_bounds__(AttnFwdCfg<HD>::THREADS, 2)
         }
         const float neg_m = mode != 0 ? -ref : -m_run;
         uint32_t pk[32];
-        l_run += diag ? exp_half_regs<true>(sb, hh, r, sl2, neg_m, pk) : exp_half_regs<false>(sb, hh, r, sl2, neg_m, pk);
+        // keys [0, 64)
+        l_run += diag ? exp_half_regs<true>(sb, 0, r, sl2, neg_m, pk) : exp_half_regs<false>(sb, 0, r, sl2, neg_m, pk);
         tc_fence_before();
-        mbar_arrive(empty_h);
+        mbar_arrive(s_empty);
         if (!pv_seen) {
           ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, g, 12));
           if (!ok) break;
@@ -536,20 +488,23 @@ __global__ void __launch_bounds__(AttnFwdCfg<HD>::THREADS, 2)
         }
 #pragma unroll
         for (int q2 = 0; q2 < 2; ++q2)
-          tmem_st16(lane_base + Cfg::P_COL + 32 * hh + 16 * q2, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * q2));
+          tmem_st16(lane_base + Cfg::P_COL + 16 * q2, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * q2));
+        tmem_st_wait();  // the registers of pk are rewritten below
+        // keys [64, 128)
+        if (!have_b) {
+          ok = __all_sync(0xffffffffu, mbar_wait(s_full_b, j & 1, g, 17));
+          if (!ok) break;
+          tc_fence_after();
+        }
+        l_run += diag ? exp_half_regs<true>(sb, 1, r, sl2, neg_m, pk) : exp_half_regs<false>(sb, 1, r, sl2, neg_m, pk);
+        tc_fence_before();
+        mbar_arrive(s_empty_b);
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2)
+          tmem_st16(lane_base + Cfg::P_COL + 32 + 16 * q2, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * q2));
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(p_full);
-      }
-      // The second group hands its row sums to the first, which runs the epilogue.
-      float* lsum = reinterpret_cast<float*>(smem + Cfg::OFF_LSUM);
-      if (hh) {
-        lsum[r] = l_run;
-        mbar_arrive(lsum_bar);
-        run_epi = false;
-      } else if (ok) {
-        ok = __all_sync(0xffffffffu, mbar_wait(lsum_bar, 0, g, 22));
-        if (ok) l_run += lsum[r];
       }
     } else
     for (int j = 0; j < nkv && ok; ++j) {
@@ -594,14 +549,13 @@ __global__ void __launch_bounds__(AttnFwdCfg<HD>::THREADS, 2)
     }
     // ---- epilogue: O / l, gate, repack ----
     if constexpr (Cfg::SEP_P) {
-      // The sigmoid(g) tile is in Q's buffer (gs_bar); each warp of the first
-      // softmax group writes its 32 rows of gated and O into the first K / V
-      // slots (free after the last S and PV MMAs) in the tensor maps' swizzle and
-      // stores them by TMA.
-      if (ok && run_epi) ok = __all_sync(0xffffffffu, mbar_wait(o_bar, 0, g, 8));
-      if (ok && run_epi) ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkv - 1) & 1, g, 15));
-      if (ok && run_epi) ok = __all_sync(0xffffffffu, mbar_wait(gs_bar, 0, g, 20));
-      if (ok && run_epi) {
+      // The sigmoid(g) tile is in Q's buffer (gs_bar); each warp writes its 32
+      // rows of gated and O into the first K / V slots (free after the last S and
+      // PV MMAs) in the tensor maps' swizzle and stores them by TMA.
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_bar, 0, g, 8));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkv - 1) & 1, g, 15));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(gs_bar, 0, g, 20));
+      if (ok) {
         tc_fence_after();
         const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
         if (mode != 0) m_run = ref;
@@ -719,7 +673,7 @@ static int launch_attn_fwd_t(const AttnFwdMaps& maps, const AttnFwdParams& p, cu
   if (!smem_attr_set(reinterpret_cast<const void*>(kern), int(Cfg::SMEM)))
     return set_error(MEA_ERR_CUDA, "cudaFuncSetAttribute(attn_fwd) failed");
   const int grid = p.B * p.H * (p.T / 128);
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(maps, p);
+  kern<<<grid, 192, Cfg::SMEM, st>>>(maps, p);
   return check_launch("attn_fwd_kernel");
 }
 
