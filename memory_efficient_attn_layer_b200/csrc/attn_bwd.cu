@@ -141,9 +141,10 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t (&sv)[16], const uint32
 // Half a row: key columns [64*hh, 64*hh + 64) of query row r.  S and dP stream
 // out of TMEM in 16-column chunks with the next chunk's loads in flight while
 // the current chunk is computed; P and dS are kept packed (bf16 pairs).
-template <bool DIAG>
+// `mid()` runs once the first two chunks are done (the caller stores them).
+template <bool DIAG, class Mid>
 __device__ __forceinline__ void bwd_half_row(uint32_t s_addr, uint32_t dp_addr, int hh, int r, float sl2, float neg_lse,
-                                             float dl, uint32_t (&pk)[32], uint32_t (&dsk)[32]) {
+                                             float dl, uint32_t (&pk)[32], uint32_t (&dsk)[32], Mid&& mid) {
   const float2 scale2 = make_float2(sl2, sl2), bias2 = make_float2(neg_lse, neg_lse);
   const int col0 = 64 * hh;
   uint32_t s0[16], d0[16], s1[16], d1[16];
@@ -161,6 +162,7 @@ __device__ __forceinline__ void bwd_half_row(uint32_t s_addr, uint32_t dp_addr, 
       tmem_ld16(dp_addr + col0 + 16 * (c + 2), d0);
     }
     bwd_chunk<DIAG>(s1, d1, c + 1, 4 * hh, r, scale2, bias2, dl, pk, dsk);
+    if (c == 0) mid();  // chunks 0 and 1 are in pk / dsk; the next loads are in flight
     if (c + 2 < 4) tmem_wait_ld_tied2(s0, d0);
   }
 }
@@ -224,6 +226,10 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
   const uint32_t stg_empty = st_full + 56;    // previous TMA reduce has read the staging tile
   const uint32_t kvacc_empty = st_full + 64;  // dK / dV of the previous work item read out of TMEM
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13 + 2 * STAGES);
+  // (N <= 64) the dV MMAs have read the P tile / the dK MMAs the dS tile (the
+  // slots after tmem_slot)
+  const uint32_t p_free = st_full + 80;
+  const uint32_t ds_free = st_full + 88;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -248,6 +254,8 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
     mbar_init(stg_full, 128);
     mbar_init(stg_empty, 1);
     mbar_init(kvacc_empty, 128);
+    mbar_init(p_free, 1);
+    mbar_init(ds_free, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -393,10 +401,12 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
           for (int kc = 0; kc < 8; ++kc)
             mma_ss(tmem + Cfg::DV_COL, ptile_mn(sP, kc), Tile::mnmajor(sdO(s), 128, kc), IDESC_KV,
                    (n > 0 || kc > 0) ? 1u : 0u);
+          if (OVERLAP) mma_commit(p_free);  // the next P may be stored once these have read the tile
 #pragma unroll
           for (int kc = 0; kc < 8; ++kc)
             mma_ss(tmem + Cfg::DK_COL, ptile_mn(sDS, kc), Tile::mnmajor(sQ(s), 128, kc), IDESC_KV,
                    (n > 0 || kc > 0) ? 1u : 0u);
+          if (OVERLAP) mma_commit(ds_free);
           if (OVERLAP && gstep > 0) {
             if (!mbar_wait(dq_empty, (gstep - 1) & 1, g, 6)) break;
             tc_fence_after();
@@ -449,23 +459,54 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
         const float neg_lse = -lse_s[s * 256 + r];
         const float dl = lse_s[s * 256 + 128 + r];
         uint32_t pk[32], dsk[32];
+        // N <= 64: the P tile is free once step g-1's dV MMAs have read it
+        // (p_free), usually while this step's exponentials are still running, so
+        // the first two P chunks go out mid-row and the rest right after; the dS
+        // tile follows its dK MMAs (ds_free), the dS TMEM columns its dQ MMAs
+        // (dq_full).  N = 128: everything after dq_full.
+        auto store_p_front = [&]() {
+          if (!OVERLAP) return;
+          if (gstep > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(p_free, (gstep - 1) & 1, g, 23));
+            if (!ok) return;
+            tc_fence_after();
+          }
+          st_tile_row16(sP, r, 4 * hh + 0, pk);
+          st_tile_row16(sP, r, 4 * hh + 1, pk + 8);
+        };
         if (n == 0)  // the item's first query tile is the diagonal one
-          bwd_half_row<true>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk);
+          bwd_half_row<true>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk,
+                             store_p_front);
         else
-          bwd_half_row<false>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk);
+          bwd_half_row<false>(lane_base + Cfg::S_COL, lane_base + Cfg::DP_COL, hh, r, sl2, neg_lse, dl, pk, dsk,
+                              store_p_front);
         if (OVERLAP) {  // every TMEM load of S_g / dP_g has completed
           tc_fence_before();
           mbar_arrive(st_empty);
         }
-        if (gstep > 0) {  // P/dS tiles and the dS TMEM columns are free once step g-1's MMAs are done
+        if (!ok) break;
+        if (OVERLAP) {
+          st_tile_row16(sP, r, 4 * hh + 2, pk + 16);
+          st_tile_row16(sP, r, 4 * hh + 3, pk + 24);
+          if (gstep > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(ds_free, (gstep - 1) & 1, g, 24));
+            if (!ok) break;
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) st_tile_row16(sDS, r, 4 * hh + c, dsk + 8 * c);
+        }
+        if (gstep > 0) {  // the dS TMEM columns (and for N = 128 both tiles) are free once step g-1's MMAs are done
           ok = __all_sync(0xffffffffu, mbar_wait(dq_full, (gstep - 1) & 1, g, 10));
           if (!ok) break;
           tc_fence_after();
         }
+        if (!OVERLAP) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          st_tile_row16(sP, r, 4 * hh + c, pk + 8 * c);
-          st_tile_row16(sDS, r, 4 * hh + c, dsk + 8 * c);
+          for (int c = 0; c < 4; ++c) {
+            st_tile_row16(sP, r, 4 * hh + c, pk + 8 * c);
+            st_tile_row16(sDS, r, 4 * hh + c, dsk + 8 * c);
+          }
         }
 #pragma unroll
         for (int c = 0; c < 2; ++c)
@@ -475,6 +516,12 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
         tc_fence_before();
         mbar_arrive(ds_full);
       }
+    }
+    // Tail: the last step's p_free / ds_free arrivals (tcgen05.commit) have landed
+    // before the CTA exits.
+    if (OVERLAP && ok && gstep > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(p_free, (gstep - 1) & 1, g, 25));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(ds_free, (gstep - 1) & 1, g, 26));
     }
     if (!ok) g.ok = false;
     finish();
