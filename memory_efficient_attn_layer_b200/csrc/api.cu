@@ -131,10 +131,13 @@ static FwdWs fwd_layout(const mea_block_dims& d) {
 struct BwdWs {
   size_t xn, rx, q, k, v, gs, rq, rk, gated, o, dO, delta, dacc, dqacc, dk, dxn, dw32, total;
 };
-// Two slots are shared between tensors whose lifetimes do not overlap (kernel
+// Three slots are shared between tensors whose lifetimes do not overlap (kernel
 // order of mea_block_backward_ex): gated is last read by the dWo GEMM and dK is
 // first written by the attention backward, after it; O is last read by the
-// gate backward and dx_n first written by the dx GEMM, after it.
+// gate backward and dx_n first written by the dx GEMM, after it; sigmoid(g) is
+// last read by the gate backward, whose epilogue writes dO over it (each warp
+// loads a head's sigmoid(g) rows before it stores that head's dO rows at the
+// same positions, and no other tile reads them).
 static BwdWs bwd_layout(const mea_block_dims& d) {
   const size_t M = size_t(d.B) * d.T, HN = size_t(d.H) * d.N, BHT = size_t(d.B) * d.H * d.T;
   BwdWs w;
@@ -149,7 +152,7 @@ static BwdWs bwd_layout(const mea_block_dims& d) {
   w.rk = c.take(BHT * 4);
   w.gated = c.take(M * HN * 2);
   w.o = c.take(M * HN * 2);
-  w.dO = c.take(M * HN * 2);
+  w.dO = w.gs;
   w.delta = c.take(BHT * 4);
   w.dacc = c.take(M * 4 * HN * 2);
   w.dqacc = c.take(M * HN * 4);
