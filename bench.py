@@ -592,9 +592,9 @@ def run_gpu(args, cfg, rank, world, device):
     if not eager:
         _lib.profile_enable(True)
     if overlap:
-        from memory_efficient_attn_layer_b200 import fused_attn as _fa
+        from memory_efficient_attn_layer_b200.fused_attn import record_exchange_waits
 
-        _fa.record_exchange_waits(True)
+        record_exchange_waits(True)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_wall0 = time.time()
     ev0.record()
@@ -610,7 +610,7 @@ def run_gpu(args, cfg, rank, world, device):
         _lib.profile_enable(False)
     exchange_wait = None
     if overlap:
-        waits = _fa.record_exchange_waits(False)
+        waits = record_exchange_waits(False)
         if waits:
             exchange_wait = {"ms_per_step": sum(waits) / len(waits), "max_ms": max(waits), "steps": len(waits),
                              "what": "time the caller's stream waited at the end of the backward for the "

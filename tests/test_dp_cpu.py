@@ -113,3 +113,17 @@ def test_no_exchange_outside_context_or_without_group():
     assert active_exchange() is None
     with overlap_grad_allreduce():
         assert active_exchange() is None  # no process group: nothing to exchange
+
+
+def test_bench_resolves_the_exchange_wait_instrument():
+    """bench.py --gpus N (N > 1) imports the exchange-wait instrument by name from
+    the fused_attn module (the package re-exports a function of the same name)."""
+    import ast
+    import os
+
+    src = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "bench.py")).read()
+    names = [(n.module, a.name) for n in ast.walk(ast.parse(src)) if isinstance(n, ast.ImportFrom) for a in n.names]
+    assert ("memory_efficient_attn_layer_b200.fused_attn", "record_exchange_waits") in names
+    from memory_efficient_attn_layer_b200.fused_attn import record_exchange_waits
+
+    assert record_exchange_waits(True) is None and record_exchange_waits(False) == []
