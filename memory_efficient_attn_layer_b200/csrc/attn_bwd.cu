@@ -407,6 +407,9 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
             mma_ss(tmem + Cfg::DK_COL, ptile_mn(sDS, kc), Tile::mnmajor(sQ(s), 128, kc), IDESC_KV,
                    (n > 0 || kc > 0) ? 1u : 0u);
           if (OVERLAP) mma_commit(ds_free);
+          // Q_g and dO_g are last read by the dV and dK MMAs (dQ reads dS from TMEM
+          // and K): their stage goes back to the producer before the dQ MMAs.
+          mma_commit(qdo_empty(s));
           if (OVERLAP && gstep > 0) {
             if (!mbar_wait(dq_empty, (gstep - 1) & 1, g, 6)) break;
             tc_fence_after();
@@ -416,7 +419,6 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
           for (int kc = 0; kc < 8; ++kc)
             mma_ts(tmem + Cfg::DQ_COL, tmem + Cfg::DS_COL + kc * 8, Tile::mnmajor(sK(kb), 128, kc), IDESC_DQ,
                    kc > 0 ? 1u : 0u);
-          mma_commit(qdo_empty(s));
           mma_commit(dq_full);
           if (last) mma_commit(kv_empty(kb));  // every MMA reading this K/V buffer is complete
           if (!OVERLAP && (!last || has_next)) {
