@@ -76,8 +76,9 @@ def stage_bytes(B, T, C, H, N):
     """Algorithmic HBM bytes of the bandwidth-bound stages."""
     M, HN = B * T, H * N
     return {
-        # forward: only the inverse RMS is written (the projection GEMM applies it); backward: x_n too
-        "fwd.rmsnorm": M * C * 2 + M * 4, "bwd.rmsnorm": M * C * 2 * 2 + M * 4,
+        # forward and backward recompute: only the inverse RMS is written (the projection GEMM and
+        # the dAcc writers apply it; x_n is never stored)
+        "fwd.rmsnorm": M * C * 2 + M * 4, "bwd.rmsnorm": M * C * 2 + M * 4,
         "bwd.qk_norm_rope_bwd": M * HN * (4 + 2 + 2 + 2 + 2 * 2) + 2 * B * H * T * 4,
         "bwd.rmsnorm_bwd": M * C * 2 * 3 + M * 4, "bwd.cast": 5 * HN * C * 6,
     }

@@ -129,7 +129,7 @@ static FwdWs fwd_layout(const mea_block_dims& d) {
 }
 
 struct BwdWs {
-  size_t xn, rx, q, k, v, gs, rq, rk, gated, o, dO, delta, dacc, dqacc, dk, dxn, dw32, total;
+  size_t rx, q, k, v, gs, rq, rk, gated, o, dO, delta, dacc, dqacc, dk, dxn, dw32, total;
 };
 // Three slots are shared between tensors whose lifetimes do not overlap (kernel
 // order of mea_block_backward_ex): gated is last read by the dWo GEMM and dK is
@@ -142,7 +142,6 @@ static BwdWs bwd_layout(const mea_block_dims& d) {
   const size_t M = size_t(d.B) * d.T, HN = size_t(d.H) * d.N, BHT = size_t(d.B) * d.H * d.T;
   BwdWs w;
   Carve c;
-  w.xn = c.take(M * d.C * 2);
   w.rx = c.take(M * 4);
   w.q = c.take(M * HN * 2);
   w.k = c.take(M * HN * 2);
@@ -211,8 +210,9 @@ static int qkvg(const mea_block_dims& d, const void* a, const float* row_scale, 
   return run_gemm(L, p, st);
 }
 
+// `row_scale` (may be NULL) multiplies each row of dg_pre.
 static int gate_bwd(const mea_block_dims& d, const void* dy, const void* wo, const void* o, const void* gs, void* dO,
-                    void* dg, long long ld_dg, float* delta, int* status, cudaStream_t st) {
+                    void* dg, long long ld_dg, float* delta, const float* row_scale, int* status, cudaStream_t st) {
   const int HN = d.H * d.N;
   GemmLaunch L{};
   L.M = d.B * d.T;
@@ -235,6 +235,7 @@ static int gate_bwd(const mea_block_dims& d, const void* dy, const void* wo, con
   L.out[1] = dg;
   L.ldo = ld_dg;
   p.delta = delta;
+  p.row_scale = row_scale;
   p.T = d.T;
   p.H = d.H;
   p.hd = d.N;
@@ -498,11 +499,16 @@ static int block_backward(const mea_block_dims* d, const void* x, const void* wq
   char* dacc = ws + w.dacc;
   const long long ld_dacc = 4LL * HN;
 
-  // Recompute: input norm, projections (+ inverse RMS of q/k), attention (+ O).
-  MEA_STAGE(ST_BWD_NORM, run_rmsnorm_fwd(M, C, d->eps, x, ws + w.xn, rx, st));
+  // Recompute: input norm (r only), projections (+ inverse RMS of q/k), attention (+ O).
+  MEA_STAGE(ST_BWD_NORM, run_rmsnorm_fwd(M, C, d->eps, x, nullptr, rx, st));
   // Same projection as the forward (x with the row scale), so the recomputed
-  // q/k/v/g match the forward's bit for bit and the saved LSE stays exact;
-  // x_n (written above) serves the weight and input gradients.
+  // q/k/v/g match the forward's bit for bit and the saved LSE stays exact.
+  // x_n itself is never stored: every writer of dAcc multiplies row m by r_m
+  // (dAcc' = diag(r) dAcc: the gate backward's epilogue, the attention
+  // backward's dV read-out, and the q/k backward through rq, rk, which this
+  // projection stores as r_q * r and r_k * r), so the weight gradient
+  // dAcc^T x_n = dAcc'^T x and the dx GEMM yields diag(r) dx_n, which the norm
+  // backward takes as is.
   MEA_STAGE(ST_BWD_QKVG, qkvg(*d, x, rx, wq, wk, wv, wg, factor1, factor2, ws + w.q, ws + w.k, ws + w.v, ws + w.gs, rq, rk,
                status, st));
   // The recompute takes the forward's LSE as its exp2 reference: P comes out
@@ -527,18 +533,18 @@ static int block_backward(const mea_block_dims* d, const void* x, const void* wq
   // o_proj backward: dWo = dY^T gated; dGated = dY Wo with the gate backward fused.
   MEA_STAGE(ST_BWD_DWO, weight_grad(C, HN, M, dy, C, ws + w.gated, HN, dwo32, status, st));
   MEA_TRY(record_event(ev_dwo_ready, st));
-  MEA_STAGE(ST_BWD_DGATE, gate_bwd(*d, dy, wo, o, ws + w.gs, ws + w.dO, dacc + size_t(3) * HN * 2, ld_dacc, delta, status,
-                   st));
+  MEA_STAGE(ST_BWD_DGATE, gate_bwd(*d, dy, wo, o, ws + w.gs, ws + w.dO, dacc + size_t(3) * HN * 2, ld_dacc, delta, rx,
+                                   status, st));
   // Attention backward: dq (fp32 accumulate), dk, dv -> v slot of dacc.
   MEA_STAGE(ST_BWD_ATTN, run_attn_bwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.dO, lse2, delta, dqacc, ws + w.dk,
-                       dacc + size_t(2) * HN * 2, ld_dacc, status, st));
+                       dacc + size_t(2) * HN * 2, ld_dacc, status, st, rx));
   // q/k norm + rotary backward -> q, k slots of dacc; rotary-table gradients.
   MEA_STAGE(ST_BWD_QK, run_qk_norm_rope_bwd(d->B, d->H, d->T, d->N, dqacc, ws + w.dk, ws + w.q, ws + w.k, rq, rk, factor1, factor2,
                                d->N, dacc, ld_dacc, dfactor1, dfactor2, st));
-  // Projection weight gradients: [4HN, C] = dacc^T xn.
-  MEA_STAGE(ST_BWD_DW, weight_grad(4 * HN, C, M, dacc, ld_dacc, ws + w.xn, C, dw32, status, st));
+  // Projection weight gradients: [4HN, C] = dacc^T xn = (diag(r) dacc)^T x.
+  MEA_STAGE(ST_BWD_DW, weight_grad(4 * HN, C, M, dacc, ld_dacc, x, C, dw32, status, st));
   MEA_TRY(record_event(ev_dw_ready, st));
-  // dx_normed = dacc [Wq; Wk; Wv; Wg]
+  // diag(r) dx_normed = (diag(r) dacc) [Wq; Wk; Wv; Wg]
   {
     GemmLaunch L{};
     L.M = M;
@@ -563,7 +569,7 @@ static int block_backward(const mea_block_dims* d, const void* x, const void* wq
     p.status = status;
     MEA_STAGE(ST_BWD_DX, run_gemm(L, p, st));
   }
-  MEA_STAGE(ST_BWD_NORM_BWD, run_rmsnorm_bwd(M, C, ws + w.dxn, x, rx, dx, st));
+  MEA_STAGE(ST_BWD_NORM_BWD, run_rmsnorm_bwd(M, C, ws + w.dxn, x, rx, dx, st, /*prescaled=*/true));
   const size_t wsz = size_t(HN) * C;
   StageScope cast_scope(ST_BWD_CAST, st);
   void* dst[5] = {dwq, dwk, dwv, dwg, dwo};
@@ -668,7 +674,7 @@ int mea_gemm_e4m3(int M, int N, int K, const void* a, long long lda, const void*
 int mea_gate_backward(const mea_block_dims* d, const void* dy, const void* wo, const void* o, const void* gs,
                       void* dO, void* dg, long long ld_dg, float* delta, int* status, void* stream) {
   MEA_TRY(validate(d));
-  return gate_bwd(*d, dy, wo, o, gs, dO, dg, ld_dg, delta, status, static_cast<cudaStream_t>(stream));
+  return gate_bwd(*d, dy, wo, o, gs, dO, dg, ld_dg, delta, nullptr, status, static_cast<cudaStream_t>(stream));
 }
 
 int mea_attention_backward(int B, int H, int T, int N, const void* q, const void* k, const void* v, const void* dO,

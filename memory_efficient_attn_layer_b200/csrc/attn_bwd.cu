@@ -51,6 +51,7 @@ struct AttnBwdParams {
   __nv_bfloat16* dk;  // [B,H,T,N]
   __nv_bfloat16* dv;  // dv[(b*T + t)*ld_dv + h*N + n]
   long long ld_dv;
+  const float* dv_scale;  // [B*T] factor on dV row (b, t), or NULL
   int* status;
 };
 
@@ -593,6 +594,9 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
       int bh, jt;
       it.get(bh, jt);
       const int nsteps = nq - jt;
+      // This thread's dV row factor, loaded now so its latency is spent under the dQ rounds.
+      const float dv_sc =
+          p.dv_scale ? __ldg(p.dv_scale + size_t(bh / p.H) * p.T + jt * 128 + r) : 1.0f;
       for (int k = 0; k < nsteps && ok; ++k, ++gstep) {
         ok = __all_sync(0xffffffffu, mbar_wait(dq_full, gstep & 1, g, 9));
         if (!ok) break;
@@ -652,7 +656,7 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
       for (int which = 0; which < 2 && ok; ++which) {
         if (!(ok = stage_begin())) break;
         const uint32_t col = which ? Cfg::DV_COL : Cfg::DK_COL;
-        const float sc = which ? 1.0f : p.scale;
+        const float sc = which ? dv_sc : p.scale;
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
           uint32_t a0[16], a1[16];
@@ -726,7 +730,7 @@ int check_attn_bwd_args(int B, int H, int T, int HD, const void* q, const void* 
 
 int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
                  const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv, int* status,
-                 cudaStream_t st) {
+                 cudaStream_t st, const float* dv_row_scale) {
   const int rc0 = check_attn_bwd_args(B, H, T, HD, q, k, v, dO, lse2, delta, dk, dv, ld_dv);
   if (rc0 != MEA_OK) return rc0;
   if (!dq_acc || (reinterpret_cast<uintptr_t>(dq_acc) & 15))
@@ -759,6 +763,7 @@ int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, cons
   p.dk = static_cast<__nv_bfloat16*>(dk);
   p.dv = static_cast<__nv_bfloat16*>(dv);
   p.ld_dv = ld_dv;
+  p.dv_scale = dv_row_scale;
   p.status = status;
   switch (HD) {
     case 32: return launch_attn_bwd_t<32>(maps, p, st);

@@ -110,15 +110,19 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_rows_kernel(int rows, float e
 // ---------------------------------------------------------------------------
 // Input RMSNorm backward (fast_triton_attn.py:663-669):
 //   dx = r * (g - xn * sum(g * xn) / C),  xn = bf16(x * r), g = d xn.
+// With `prescaled` the incoming rows are g' = r * g (the row scale applied
+// where g was produced), and the same identity reads
+//   dx = g' - xn * sum(g' * xn) / C.
 // ---------------------------------------------------------------------------
 __global__ void rmsnorm_bwd_kernel(int rows, int C, const __nv_bfloat16* __restrict__ dxn,
                                    const __nv_bfloat16* __restrict__ x, const float* __restrict__ rin,
-                                   __nv_bfloat16* __restrict__ dx) {
+                                   __nv_bfloat16* __restrict__ dx, bool prescaled) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const size_t off = size_t(warp) * C;
   const float r = rin[warp];
+  const float s = prescaled ? 1.0f : r;  // factor on the output
   float dot = 0.f;
   for (int c = lane * 8; c < C; c += 256) {
     const uint4 gv = *reinterpret_cast<const uint4*>(dxn + off + c);
@@ -143,7 +147,7 @@ __global__ void rmsnorm_bwd_kernel(int rows, int C, const __nv_bfloat16* __restr
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float n0 = round_bf16(bf16_lo(xw[e]) * r), n1 = round_bf16(bf16_hi(xw[e]) * r);
-      o[e] = pack_bf16(r * (bf16_lo(gw[e]) - n0 * k), r * (bf16_hi(gw[e]) - n1 * k));
+      o[e] = pack_bf16(s * (bf16_lo(gw[e]) - n0 * k), s * (bf16_hi(gw[e]) - n1 * k));
     }
     st_global_v4(dx + off + c, o[0], o[1], o[2], o[3]);
   }
@@ -163,6 +167,10 @@ __global__ void rmsnorm_bwd_kernel(int rows, int C, const __nv_bfloat16* __restr
 // backward in the rotated frame, which equals this only for orthogonal R_t.
 // Table gradients (:622-639), exact form:
 //   df1[t,n] += dq_rot[n] * qn[n],  df2[t,n] += dq_rot[n] * qn[n^1]  over (b,h), q and k.
+// rq / rk are the factors from the projection accumulator row to qn: the q/k
+// inverse RMS, times the input RMSNorm's r when the projection read x (the
+// block backward), which puts r into dacc as the weight and input gradients
+// then need.
 //
 // Grid: x = position t, y = chunk of the B*H rows; each block loops over its
 // (b,h) rows at fixed t so the table gradients reduce in registers and leave
@@ -491,7 +499,8 @@ int run_rmsnorm_fwd(int rows, int C, float eps, const void* x, void* xn, float* 
   return check_launch("rmsnorm_fwd_kernel");
 }
 
-int run_rmsnorm_bwd(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, cudaStream_t st) {
+int run_rmsnorm_bwd(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, cudaStream_t st,
+                    bool prescaled) {
   if (C % 8 || C <= 0 || rows <= 0) return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "rmsnorm bwd: C=%d must be a multiple of 8", C);
   if (!dxn || !x || !r || !dx ||
       (reinterpret_cast<uintptr_t>(dxn) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dx)) & 15)
@@ -500,7 +509,7 @@ int run_rmsnorm_bwd(int rows, int C, const void* dxn, const void* x, const float
   const int blocks = (rows * 32 + threads - 1) / threads;
   rmsnorm_bwd_kernel<<<blocks, threads, 0, st>>>(rows, C, static_cast<const __nv_bfloat16*>(dxn),
                                                  static_cast<const __nv_bfloat16*>(x), r,
-                                                 static_cast<__nv_bfloat16*>(dx));
+                                                 static_cast<__nv_bfloat16*>(dx), prescaled);
   return check_launch("rmsnorm_bwd_kernel");
 }
 

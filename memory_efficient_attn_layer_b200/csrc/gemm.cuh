@@ -27,9 +27,10 @@
 //   EPI_QKVG  : row scale (the fused input RMSNorm), per-head q/k RMSNorm +
 //               interleaved rotary, v copy, sigmoid(g), [B, H, T, N] outputs
 //               (fast_triton_attn.py:102-144); rotary-table rows come in by TMA
-//   EPI_DGATE : gate backward (dO = dGated*g, dg_pre = dGated*O*g(1-g)) and
-//               delta = rowsum(dO*O) for the attention backward
-//               (fast_triton_attn.py:581-584, :601); O and g rows come in by TMA
+//   EPI_DGATE : gate backward (dO = dGated*g, dg_pre = dGated*O*g(1-g), times
+//               an optional row scale) and delta = rowsum(dO*O) for the
+//               attention backward (fast_triton_attn.py:581-584, :601); O and g
+//               rows come in by TMA
 //   EPI_BF16 / EPI_F32 / EPI_RED_F32 : plain stores / split-K fp32 TMA reduce-add.
 #pragma once
 #include <cuda.h>
@@ -59,7 +60,9 @@ struct GemmParams {
   int b_kb_per_src;  // B_MN_KSPLIT4: k-blocks taken from each of the 4 B tensors
   int slab_rows;     // B_SLABS: rows of one slab (= head dim)
   int* status;
-  // EPI_QKVG
+  // EPI_QKVG (row_scale: x_n = diag(row_scale) x; rq, rk receive row_scale times
+  // the q/k inverse RMS, the factor from an accumulator row to the normalised
+  // row) and EPI_DGATE (row_scale on dg_pre).  row_scale may be NULL (1).
   float *rq, *rk;
   const float* row_scale;
   int T, H, hd;
@@ -278,11 +281,11 @@ __device__ __forceinline__ void qk_slab(const GemmParams& p, uint32_t tcol, uint
     }
   }
   const float inv = rsqrtf((ss0 + ss1) * (rs * rs) / float(HD) + p.eps);
+  const float sc = rs * inv;  // accumulator row -> normalised row
   if (valid) {
     float* rdst = typ == 0 ? p.rq : p.rk;
-    if (rdst) rdst[bht] = inv;
+    if (rdst) rdst[bht] = sc;
   }
-  const float sc = rs * inv;
 #pragma unroll
   for (int ci = 0; ci < NCH; ++ci) {
     uint32_t wbuf[32];
@@ -452,6 +455,9 @@ __device__ __forceinline__ void epi_dgate(const GemmMaps& maps, const GemmParams
   const int b = mq / p.T;
   const int tq = mq - b * p.T;
   const bool valid = mq + lane < p.M;
+  // Optional per-row factor on dg_pre (the input RMSNorm's r: the weight and
+  // input gradients then read x instead of x_n).
+  const float rs = p.row_scale ? __ldg(p.row_scale + (valid ? mq + lane : p.M - 1)) : 1.0f;
 #pragma unroll 1
   for (int j = 0; j < NJ; ++j, ++hc) {
     const int head = n0 / HD + wg + G * j;
@@ -498,7 +504,7 @@ __device__ __forceinline__ void epi_dgate(const GemmMaps& maps, const GemmParams
           dsum = fmaf(do0, o0, dsum);
           dsum = fmaf(do1, o1, dsum);
           pd[e] = pack_bf16(do0, do1);
-          pg[e] = pack_bf16(d0 * o0 * g0 * (1.0f - g0), d1 * o1 * g1 * (1.0f - g1));
+          pg[e] = pack_bf16(d0 * o0 * g0 * (1.0f - g0) * rs, d1 * o1 * g1 * (1.0f - g1) * rs);
         }
         sts_v4(ao, pd);
         sts_v4(ag, pg);

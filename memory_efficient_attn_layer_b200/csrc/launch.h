@@ -61,9 +61,11 @@ constexpr float ATTN_MAX_BOUND = 50.f;
 int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* gs, void* gated,
                  float* lse2, void* o_out, const float* bound, const float* lse_in, int* status, cudaStream_t st,
                  float* dq_zero = nullptr);
+// `dv_row_scale` ([B*T] fp32, may be NULL): dV row (b, t) is multiplied by
+// dv_row_scale[b*T + t] before it is stored.
 int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
                  const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv, int* status,
-                 cudaStream_t st);
+                 cudaStream_t st, const float* dv_row_scale = nullptr);
 // The shape, pointer and alignment checks of run_attn_bwd (all but dq_acc),
 // with no device work: MEA_OK or the error run_attn_bwd would return.
 int check_attn_bwd_args(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
@@ -71,7 +73,12 @@ int check_attn_bwd_args(int B, int H, int T, int HD, const void* q, const void* 
 
 // ---- elementwise (elementwise.cu) ----
 int run_rmsnorm_fwd(int rows, int C, float eps, const void* x, void* xn, float* r, cudaStream_t st);
-int run_rmsnorm_bwd(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, cudaStream_t st);
+// `prescaled`: dxn holds r * d(x_n) (the row scale already applied upstream),
+// so dx = dxn - x_n * sum(dxn * x_n) / C; otherwise dx = r * (dxn - x_n * sum(dxn * x_n) / C).
+int run_rmsnorm_bwd(int rows, int C, const void* dxn, const void* x, const float* r, void* dx, cudaStream_t st,
+                    bool prescaled = false);
+// rq, rk: the factors from projection accumulator rows to the normalised q, k
+// rows (as the fused projection stores them).
 int run_qk_norm_rope_bwd(int B, int H, int T, int HD, const float* dq_acc, const void* dk, const void* q_rot,
                          const void* k_rot, const float* rq, const float* rk, const void* f1, const void* f2,
                          long long ldf, void* dacc, long long ld_dacc, float* df1, float* df2, cudaStream_t st);
