@@ -131,15 +131,28 @@ static FwdWs fwd_layout(const mea_block_dims& d) {
 struct BwdWs {
   size_t rx, q, k, v, gs, rq, rk, gated, o, dO, delta, dacc, dqacc, dk, dxn, dw32, total;
 };
-// Three slots are shared between tensors whose lifetimes do not overlap (kernel
+// Slots are shared between tensors whose lifetimes do not overlap (kernel
 // order of mea_block_backward_ex): gated is last read by the dWo GEMM and dK is
-// first written by the attention backward, after it; O is last read by the
-// gate backward and dx_n first written by the dx GEMM, after it; sigmoid(g) is
-// last read by the gate backward, whose epilogue writes dO over it (each warp
-// loads a head's sigmoid(g) rows before it stores that head's dO rows at the
-// same positions, and no other tile reads them).
+// first written by the attention backward, after it; sigmoid(g) is last read by
+// the gate backward, whose epilogue writes dO over it (each warp loads a head's
+// sigmoid(g) rows before it stores that head's dO rows at the same positions,
+// and no other tile reads them).
+// The projection gradient dAcc = [dq | dk | dv | dg] (one row per token):
+//  * head dim >= 64: no buffer of its own.  Each part is written over the
+//    tensor its producer consumes last, in the same [B,H,T,N] layout: dg over
+//    O (gate backward epilogue, as dO over sigmoid(g)); dv over v (attention
+//    backward: V tile j is read only by the work item that writes dV tile j,
+//    before it writes it); dq, dk over q, k (q/k backward: each element is read
+//    by the thread that then writes it).  The dW and dx GEMMs read the four
+//    parts per head (A_MN_HEADS / A_K_HEADS), and dx_n goes to the gated/dK
+//    slot or the dQ accumulator's, both dead by then.
+//  * head dim 32 (a 64-wide GEMM box spans two heads): one [M, 4*H*N] buffer;
+//    dx_n takes O's slot (O is last read by the gate backward).
+static bool dacc_in_place(const mea_block_dims& d) { return d.N >= 64; }
+
 static BwdWs bwd_layout(const mea_block_dims& d) {
   const size_t M = size_t(d.B) * d.T, HN = size_t(d.H) * d.N, BHT = size_t(d.B) * d.H * d.T;
+  const bool inplace = dacc_in_place(d);
   BwdWs w;
   Carve c;
   w.rx = c.take(M * 4);
@@ -153,10 +166,14 @@ static BwdWs bwd_layout(const mea_block_dims& d) {
   w.o = c.take(M * HN * 2);
   w.dO = w.gs;
   w.delta = c.take(BHT * 4);
-  w.dacc = c.take(M * 4 * HN * 2);
+  w.dacc = inplace ? 0 : c.take(M * 4 * HN * 2);
   w.dqacc = c.take(M * HN * 4);
   w.dk = w.gated;
-  w.dxn = d.C <= HN ? w.o : c.take(M * d.C * 2);  // O's slot holds [M, H*N]; dx_n is [M, C]
+  // gated / O slots hold [M, H*N] bf16, the dQ accumulator [M, H*N] fp32; dx_n is [M, C] bf16
+  if (inplace)
+    w.dxn = size_t(d.C) <= HN ? w.gated : size_t(d.C) <= 2 * HN ? w.dqacc : c.take(M * d.C * 2);
+  else
+    w.dxn = size_t(d.C) <= HN ? w.o : c.take(M * d.C * 2);
   w.dw32 = c.take(5 * HN * d.C * 4);
   w.total = c.off;
   return w;
@@ -210,9 +227,11 @@ static int qkvg(const mea_block_dims& d, const void* a, const float* row_scale, 
   return run_gemm(L, p, st);
 }
 
-// `row_scale` (may be NULL) multiplies each row of dg_pre.
+// `row_scale` (may be NULL) multiplies each row of dg_pre; `dg_heads`: dg is
+// [B,H,T,N] (ld_dg unused), else [M, ld_dg] with head h at column h*N.
 static int gate_bwd(const mea_block_dims& d, const void* dy, const void* wo, const void* o, const void* gs, void* dO,
-                    void* dg, long long ld_dg, float* delta, const float* row_scale, int* status, cudaStream_t st) {
+                    void* dg, long long ld_dg, float* delta, const float* row_scale, bool dg_heads, int* status,
+                    cudaStream_t st) {
   const int HN = d.H * d.N;
   GemmLaunch L{};
   L.M = d.B * d.T;
@@ -236,21 +255,24 @@ static int gate_bwd(const mea_block_dims& d, const void* dy, const void* wo, con
   L.ldo = ld_dg;
   p.delta = delta;
   p.row_scale = row_scale;
+  p.dg_heads = dg_heads ? 1 : 0;
   p.T = d.T;
   p.H = d.H;
   p.hd = d.N;
   return run_gemm(L, p, st);
 }
 
-// Split-K weight-gradient GEMM: out[M', N'] += A^T B over the token dim.
+// Split-K weight-gradient GEMM: out[M', N'] += A^T B over the token dim.  With
+// `a_parts` (and `d`), A^T is the four per-head dAcc parts (M' = 4*H*N).
 static int weight_grad(int Mp, int Np, int tokens, const void* a, long long lda, const void* b, long long ldb,
-                       float* out, int* status, cudaStream_t st) {
+                       float* out, int* status, cudaStream_t st, const void* const* a_parts = nullptr,
+                       const mea_block_dims* d = nullptr) {
   GemmLaunch L{};
   L.M = Mp;
   L.N = Np;
   L.K = tokens;
   L.bn = pick_bn(Np);
-  L.amode = A_MN;
+  L.amode = a_parts ? A_MN_HEADS : A_MN;
   L.bmode = B_MN;
   L.epi = EPI_RED_F32;
   L.a = a;
@@ -260,6 +282,12 @@ static int weight_grad(int Mp, int Np, int tokens, const void* a, long long lda,
   L.k_splits = auto_splits(Mp / GEMM_BM, Np / L.bn, tokens / GEMM_BK, 8);
   GemmParams p{};
   p.status = status;
+  if (a_parts) {
+    for (int i = 0; i < 4; ++i) L.a4[i] = a_parts[i];
+    p.H = d->H;
+    p.T = d->T;
+    p.hd = d->N;
+  }
   L.out[0] = out;
   L.ldo = Np;
   return run_gemm(L, p, st);
@@ -496,7 +524,7 @@ static int block_backward(const mea_block_dims* d, const void* x, const void* wq
   float* dqacc = reinterpret_cast<float*>(ws + w.dqacc);
   float* dw32 = dweights_f32 ? dweights_f32 : reinterpret_cast<float*>(ws + w.dw32);
   float* dwo32 = dw32 + size_t(4) * HN * C;
-  char* dacc = ws + w.dacc;
+  char* dacc = dacc_in_place(*d) ? nullptr : ws + w.dacc;
   const long long ld_dacc = 4LL * HN;
 
   // Recompute: input norm (r only), projections (+ inverse RMS of q/k), attention (+ O).
@@ -533,16 +561,25 @@ static int block_backward(const mea_block_dims* d, const void* x, const void* wq
   // o_proj backward: dWo = dY^T gated; dGated = dY Wo with the gate backward fused.
   MEA_STAGE(ST_BWD_DWO, weight_grad(C, HN, M, dy, C, ws + w.gated, HN, dwo32, status, st));
   MEA_TRY(record_event(ev_dwo_ready, st));
-  MEA_STAGE(ST_BWD_DGATE, gate_bwd(*d, dy, wo, o, ws + w.gs, ws + w.dO, dacc + size_t(3) * HN * 2, ld_dacc, delta, rx,
+  // dAcc parts: in place over O, v, q, k (per-head layout), or the dacc buffer.
+  const bool inplace = dacc_in_place(*d);
+  const void* parts[4] = {ws + w.q, ws + w.k, ws + w.v, ws + w.o};
+  MEA_STAGE(ST_BWD_DGATE, gate_bwd(*d, dy, wo, o, ws + w.gs, ws + w.dO,
+                                   inplace ? ws + w.o : dacc + size_t(3) * HN * 2, ld_dacc, delta, rx, inplace,
                                    status, st));
-  // Attention backward: dq (fp32 accumulate), dk, dv -> v slot of dacc.
-  MEA_STAGE(ST_BWD_ATTN, run_attn_bwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.dO, lse2, delta, dqacc, ws + w.dk,
-                       dacc + size_t(2) * HN * 2, ld_dacc, status, st, rx));
-  // q/k norm + rotary backward -> q, k slots of dacc; rotary-table gradients.
-  MEA_STAGE(ST_BWD_QK, run_qk_norm_rope_bwd(d->B, d->H, d->T, d->N, dqacc, ws + w.dk, ws + w.q, ws + w.k, rq, rk, factor1, factor2,
-                               d->N, dacc, ld_dacc, dfactor1, dfactor2, st));
+  // Attention backward: dq (fp32 accumulate), dk, dv (over v, or the v part of dacc).
+  MEA_STAGE(ST_BWD_ATTN, run_attn_bwd(d->B, d->H, d->T, d->N, ws + w.q, ws + w.k, ws + w.v, ws + w.dO, lse2, delta,
+                                      dqacc, ws + w.dk, inplace ? ws + w.v : dacc + size_t(2) * HN * 2, ld_dacc,
+                                      status, st, rx, inplace));
+  // q/k norm + rotary backward -> dq, dk of dAcc; rotary-table gradients.
+  if (inplace)
+    MEA_STAGE(ST_BWD_QK, run_qk_norm_rope_bwd_inplace(d->B, d->H, d->T, d->N, dqacc, ws + w.dk, ws + w.q, ws + w.k,
+                                                      rq, rk, factor1, factor2, d->N, dfactor1, dfactor2, st));
+  else
+    MEA_STAGE(ST_BWD_QK, run_qk_norm_rope_bwd(d->B, d->H, d->T, d->N, dqacc, ws + w.dk, ws + w.q, ws + w.k, rq, rk,
+                                              factor1, factor2, d->N, dacc, ld_dacc, dfactor1, dfactor2, st));
   // Projection weight gradients: [4HN, C] = dacc^T xn = (diag(r) dacc)^T x.
-  MEA_STAGE(ST_BWD_DW, weight_grad(4 * HN, C, M, dacc, ld_dacc, x, C, dw32, status, st));
+  MEA_STAGE(ST_BWD_DW, weight_grad(4 * HN, C, M, dacc, ld_dacc, x, C, dw32, status, st, inplace ? parts : nullptr, d));
   MEA_TRY(record_event(ev_dw_ready, st));
   // diag(r) dx_normed = (diag(r) dacc) [Wq; Wk; Wv; Wg]
   {
@@ -551,11 +588,12 @@ static int block_backward(const mea_block_dims* d, const void* x, const void* wq
     L.N = C;
     L.K = 4 * HN;
     L.bn = pick_bn(C);
-    L.amode = A_K;
+    L.amode = inplace ? A_K_HEADS : A_K;
     L.bmode = B_MN_KSPLIT4;
     L.epi = EPI_BF16;
     L.a = dacc;
     L.lda = ld_dacc;
+    for (int i = 0; i < 4; ++i) L.a4[i] = parts[i];
     L.b[0] = wq;
     L.b[1] = wk;
     L.b[2] = wv;
@@ -567,6 +605,9 @@ static int block_backward(const mea_block_dims* d, const void* x, const void* wq
     L.ldo = C;
     GemmParams p{};
     p.status = status;
+    p.H = d->H;
+    p.T = d->T;
+    p.hd = d->N;
     MEA_STAGE(ST_BWD_DX, run_gemm(L, p, st));
   }
   MEA_STAGE(ST_BWD_NORM_BWD, run_rmsnorm_bwd(M, C, ws + w.dxn, x, rx, dx, st, /*prescaled=*/true));
@@ -674,7 +715,7 @@ int mea_gemm_e4m3(int M, int N, int K, const void* a, long long lda, const void*
 int mea_gate_backward(const mea_block_dims* d, const void* dy, const void* wo, const void* o, const void* gs,
                       void* dO, void* dg, long long ld_dg, float* delta, int* status, void* stream) {
   MEA_TRY(validate(d));
-  return gate_bwd(*d, dy, wo, o, gs, dO, dg, ld_dg, delta, nullptr, status, static_cast<cudaStream_t>(stream));
+  return gate_bwd(*d, dy, wo, o, gs, dO, dg, ld_dg, delta, nullptr, false, status, static_cast<cudaStream_t>(stream));
 }
 
 int mea_attention_backward(int B, int H, int T, int N, const void* q, const void* k, const void* v, const void* dO,

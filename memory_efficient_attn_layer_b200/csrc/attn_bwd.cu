@@ -49,8 +49,9 @@ struct AttnBwdParams {
   const float* delta;
   float* dq_acc;      // [B,H,T,N] fp32, accumulated
   __nv_bfloat16* dk;  // [B,H,T,N]
-  __nv_bfloat16* dv;  // dv[(b*T + t)*ld_dv + h*N + n]
+  __nv_bfloat16* dv;  // dv[(b*T + t)*ld_dv + h*N + n], or [B,H,T,N] like dk when dv_heads
   long long ld_dv;
+  int dv_heads;
   const float* dv_scale;  // [B*T] factor on dV row (b, t), or NULL
   int* status;
 };
@@ -59,7 +60,7 @@ struct AttnBwdMaps {
   CUtensorMap q, k, v, dO;
   CUtensorMap dq;  // dq_acc as [B*H*T, N] fp32, 32x128 boxes, 128-byte swizzle
   CUtensorMap dk;  // dk as [B*H*T, N] bf16, min(N,64) x 128 boxes
-  CUtensorMap dv;  // dv as [B*T, ld_dv] bf16 (head h at column h*N), min(N,64) x 128 boxes
+  CUtensorMap dv;  // dv as [B*T, ld_dv] bf16 (head h at column h*N), or as dk; min(N,64) x 128 boxes
 };
 
 template <int HD>
@@ -678,7 +679,9 @@ __global__ void __launch_bounds__(512, 1) attn_bwd_kernel(const __grid_constant_
         ok = stage_end([&] {
 #pragma unroll
           for (int bx = 0; bx < HD / BW; ++bx) {
-            if (which)
+            if (which && p.dv_heads)
+              tma_store_2d(&maps.dv, stg + bx * (128 * BW * 2), bx * BW, bh * p.T + jt * 128);
+            else if (which)
               tma_store_2d(&maps.dv, stg + bx * (128 * BW * 2), h * HD + bx * BW, b * p.T + jt * 128);
             else
               tma_store_2d(&maps.dk, stg + bx * (128 * BW * 2), bx * BW, bh * p.T + jt * 128);
@@ -730,7 +733,8 @@ int check_attn_bwd_args(int B, int H, int T, int HD, const void* q, const void* 
 
 int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
                  const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv, int* status,
-                 cudaStream_t st, const float* dv_row_scale) {
+                 cudaStream_t st, const float* dv_row_scale, bool dv_heads) {
+  if (dv_heads) ld_dv = (long long)H * HD;
   const int rc0 = check_attn_bwd_args(B, H, T, HD, q, k, v, dO, lse2, delta, dk, dv, ld_dv);
   if (rc0 != MEA_OK) return rc0;
   if (!dq_acc || (reinterpret_cast<uintptr_t>(dq_acc) & 15))
@@ -748,8 +752,11 @@ int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, cons
                      CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
   const uint32_t bw = HD < 64 ? uint32_t(HD) : 64u;
   rc |= make_tmap_2d(&maps.dk, dk, HD, rows, uint64_t(HD) * 2, bw, 128, swizzle_for(bw * 2));
-  rc |= make_tmap_2d(&maps.dv, dv, uint64_t(H) * HD, uint64_t(B) * T, uint64_t(ld_dv) * 2, bw, 128,
-                     swizzle_for(bw * 2));
+  if (dv_heads)
+    rc |= make_tmap_2d(&maps.dv, dv, HD, rows, uint64_t(HD) * 2, bw, 128, swizzle_for(bw * 2));
+  else
+    rc |= make_tmap_2d(&maps.dv, dv, uint64_t(H) * HD, uint64_t(B) * T, uint64_t(ld_dv) * 2, bw, 128,
+                       swizzle_for(bw * 2));
   if (rc) return set_error(MEA_ERR_CUDA, "attention backward: tensor map encode failed");
   AttnBwdParams p;
   p.B = B;
@@ -763,6 +770,7 @@ int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, cons
   p.dk = static_cast<__nv_bfloat16*>(dk);
   p.dv = static_cast<__nv_bfloat16*>(dv);
   p.ld_dv = ld_dv;
+  p.dv_heads = dv_heads ? 1 : 0;
   p.dv_scale = dv_row_scale;
   p.status = status;
   switch (HD) {

@@ -182,12 +182,12 @@ template <int HD>
 __global__ void __launch_bounds__(256) qk_bwd_kernel(int BH, int H, int T, int bh_per_block,
                                                      const float* __restrict__ dq_acc,
                                                      const __nv_bfloat16* __restrict__ dk,
-                                                     const __nv_bfloat16* __restrict__ q_rot,
-                                                     const __nv_bfloat16* __restrict__ k_rot,
+                                                     const __nv_bfloat16* q_rot, const __nv_bfloat16* k_rot,
                                                      const float* __restrict__ rq, const float* __restrict__ rk,
                                                      const __nv_bfloat16* __restrict__ f1,
                                                      const __nv_bfloat16* __restrict__ f2, long long ldf,
-                                                     __nv_bfloat16* __restrict__ dacc, long long ld_dacc,
+                                                     __nv_bfloat16* out_q, __nv_bfloat16* out_k, long long o_sb,
+                                                     long long o_sh, long long o_st,
                                                      float* __restrict__ df1, float* __restrict__ df2) {
   constexpr int EPT = 8;             // elements per thread
   constexpr int TPR = HD / EPT;      // threads per row (4, 8, 16)
@@ -197,7 +197,6 @@ __global__ void __launch_bounds__(256) qk_bwd_kernel(int BH, int H, int T, int b
   const int sub = threadIdx.x % TPR;
   const int grp = threadIdx.x / TPR;
   const int n0 = sub * EPT;
-  const int HN = H * HD;
 
   // This position's table entries for our 4 pairs, and each pair's inverse (recovers qn from q_rot).
   float tf1[EPT], tf2[EPT], inv[EPT / 2];
@@ -236,8 +235,9 @@ __global__ void __launch_bounds__(256) qk_bwd_kernel(int BH, int H, int T, int b
         gq[u][0] = __ldg(dqp);
         gq[u][1] = __ldg(dqp + 1);
         gk[u] = __ldg(reinterpret_cast<const uint4*>(dk + row * HD + n0));
-        yq[u] = __ldg(reinterpret_cast<const uint4*>(q_rot + row * HD + n0));
-        yk[u] = __ldg(reinterpret_cast<const uint4*>(k_rot + row * HD + n0));
+        // plain loads: the outputs may be q_rot / k_rot themselves
+        yq[u] = *reinterpret_cast<const uint4*>(q_rot + row * HD + n0);
+        yk[u] = *reinterpret_cast<const uint4*>(k_rot + row * HD + n0);
         r_q[u] = __ldg(rq + row);
         r_k[u] = __ldg(rk + row);
       } else {
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(256) qk_bwd_kernel(int BH, int H, int T, int b
       const int bh = base + u * RPB + grp;
       const bool valid = bh < bh_end;
       const int b = valid ? bh / H : 0, h = valid ? bh - (bh / H) * H : 0;
-      __nv_bfloat16* drow = dacc + (size_t(b) * T + t) * ld_dacc + size_t(h) * HD + n0;
+      const size_t ooff = size_t(b) * o_sb + size_t(h) * o_sh + size_t(t) * o_st + n0;
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         float g[EPT], y[EPT];
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(256) qk_bwd_kernel(int BH, int H, int T, int b
           a2[e] = fmaf(g[e], qb, a2[e]);
           a2[e + 1] = fmaf(g[e + 1], qa, a2[e + 1]);
         }
-        if (valid) st_global_v4(drow + (which == 0 ? 0 : HN), out[0], out[1], out[2], out[3]);
+        if (valid) st_global_v4((which == 0 ? out_q : out_k) + ooff, out[0], out[1], out[2], out[3]);
       }
     }
   }
@@ -513,9 +513,12 @@ int run_rmsnorm_bwd(int rows, int C, const void* dxn, const void* x, const float
   return check_launch("rmsnorm_bwd_kernel");
 }
 
-int run_qk_norm_rope_bwd(int B, int H, int T, int HD, const float* dq_acc, const void* dk, const void* q_rot,
+// The q/k backward with its two outputs at out_q / out_k, element (b, h, t, n)
+// at b*o_sb + h*o_sh + t*o_st + n.
+static int qk_bwd_launch(int B, int H, int T, int HD, const float* dq_acc, const void* dk, const void* q_rot,
                          const void* k_rot, const float* rq, const float* rk, const void* f1, const void* f2,
-                         long long ldf, void* dacc, long long ld_dacc, float* df1, float* df2, cudaStream_t st) {
+                         long long ldf, void* out_q, void* out_k, long long o_sb, long long o_sh, long long o_st,
+                         float* df1, float* df2, cudaStream_t st) {
   const int BH = B * H;
   // 2 passes x 256/(HD/8) rows per block iteration, 4 iterations per block at most
   const int rows_per_iter = 2 * 256 / (HD / 8);
@@ -523,31 +526,49 @@ int run_qk_norm_rope_bwd(int B, int H, int T, int HD, const float* dq_acc, const
   dim3 grid(T, (BH + bh_per_block - 1) / bh_per_block);
   if ((reinterpret_cast<uintptr_t>(dq_acc) | reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(q_rot) |
        reinterpret_cast<uintptr_t>(k_rot) | reinterpret_cast<uintptr_t>(f1) | reinterpret_cast<uintptr_t>(f2) |
-       reinterpret_cast<uintptr_t>(dacc)) & 15 || ldf % 8 || ld_dacc % 8)
+       reinterpret_cast<uintptr_t>(out_q) | reinterpret_cast<uintptr_t>(out_k)) & 15 ||
+      ldf % 8 || o_sb % 8 || o_sh % 8 || o_st % 8)
     return set_error(MEA_ERR_ALIGNMENT, "qk backward: operands must be 16-byte aligned");
   auto f1p = static_cast<const __nv_bfloat16*>(f1);
   auto f2p = static_cast<const __nv_bfloat16*>(f2);
   auto dkp = static_cast<const __nv_bfloat16*>(dk);
   auto qp = static_cast<const __nv_bfloat16*>(q_rot);
   auto kp = static_cast<const __nv_bfloat16*>(k_rot);
-  auto dp = static_cast<__nv_bfloat16*>(dacc);
+  auto oq = static_cast<__nv_bfloat16*>(out_q);
+  auto ok = static_cast<__nv_bfloat16*>(out_k);
   switch (HD) {
     case 32:
-      qk_bwd_kernel<32><<<grid, 256, 0, st>>>(BH, H, T, bh_per_block, dq_acc, dkp, qp, kp, rq, rk, f1p, f2p, ldf, dp,
-                                              ld_dacc, df1, df2);
+      qk_bwd_kernel<32><<<grid, 256, 0, st>>>(BH, H, T, bh_per_block, dq_acc, dkp, qp, kp, rq, rk, f1p, f2p, ldf, oq,
+                                              ok, o_sb, o_sh, o_st, df1, df2);
       break;
     case 64:
-      qk_bwd_kernel<64><<<grid, 256, 0, st>>>(BH, H, T, bh_per_block, dq_acc, dkp, qp, kp, rq, rk, f1p, f2p, ldf, dp,
-                                              ld_dacc, df1, df2);
+      qk_bwd_kernel<64><<<grid, 256, 0, st>>>(BH, H, T, bh_per_block, dq_acc, dkp, qp, kp, rq, rk, f1p, f2p, ldf, oq,
+                                              ok, o_sb, o_sh, o_st, df1, df2);
       break;
     case 128:
-      qk_bwd_kernel<128><<<grid, 256, 0, st>>>(BH, H, T, bh_per_block, dq_acc, dkp, qp, kp, rq, rk, f1p, f2p, ldf, dp,
-                                               ld_dacc, df1, df2);
+      qk_bwd_kernel<128><<<grid, 256, 0, st>>>(BH, H, T, bh_per_block, dq_acc, dkp, qp, kp, rq, rk, f1p, f2p, ldf, oq,
+                                               ok, o_sb, o_sh, o_st, df1, df2);
       break;
     default:
       return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "qk backward: head dim %d not in {32, 64, 128}", HD);
   }
   return check_launch("qk_bwd_kernel");
+}
+
+int run_qk_norm_rope_bwd(int B, int H, int T, int HD, const float* dq_acc, const void* dk, const void* q_rot,
+                         const void* k_rot, const float* rq, const float* rk, const void* f1, const void* f2,
+                         long long ldf, void* dacc, long long ld_dacc, float* df1, float* df2, cudaStream_t st) {
+  // q part of row (b, t) at dacc + (b*T + t)*ld_dacc + h*HD, k part H*HD further on
+  char* base = static_cast<char*>(dacc);
+  return qk_bwd_launch(B, H, T, HD, dq_acc, dk, q_rot, k_rot, rq, rk, f1, f2, ldf, dacc,
+                       base + size_t(H) * HD * 2, (long long)T * ld_dacc, HD, ld_dacc, df1, df2, st);
+}
+
+int run_qk_norm_rope_bwd_inplace(int B, int H, int T, int HD, const float* dq_acc, const void* dk, void* q_rot,
+                                 void* k_rot, const float* rq, const float* rk, const void* f1, const void* f2,
+                                 long long ldf, float* df1, float* df2, cudaStream_t st) {
+  return qk_bwd_launch(B, H, T, HD, dq_acc, dk, q_rot, k_rot, rq, rk, f1, f2, ldf, q_rot, k_rot,
+                       (long long)H * T * HD, (long long)T * HD, HD, df1, df2, st);
 }
 
 int run_cast_f32_bf16_parts(long long n, const float* src, void* const* dst, int parts, cudaStream_t st) {

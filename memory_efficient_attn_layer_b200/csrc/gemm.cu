@@ -85,6 +85,11 @@ static int dispatch(int bn, int am, int bmd, int epi, bool e4m3, const GemmMaps&
   MEA_GEMM_CASE(128, A_K, B_MN_KSPLIT4, EPI_BF16)
   MEA_GEMM_CASE(256, A_MN, B_MN, EPI_RED_F32)
   MEA_GEMM_CASE(128, A_MN, B_MN, EPI_RED_F32)
+  // the same two with dAcc read from its per-head parts (head dim >= 64)
+  MEA_GEMM_CASE(256, A_K_HEADS, B_MN_KSPLIT4, EPI_BF16)
+  MEA_GEMM_CASE(128, A_K_HEADS, B_MN_KSPLIT4, EPI_BF16)
+  MEA_GEMM_CASE(256, A_MN_HEADS, B_MN, EPI_RED_F32)
+  MEA_GEMM_CASE(128, A_MN_HEADS, B_MN, EPI_RED_F32)
   // generic fp32-output GEMMs (unit tests of every operand layout)
   MEA_GEMM_CASE(256, A_K, B_K, EPI_F32)
   MEA_GEMM_CASE(128, A_K, B_K, EPI_F32)
@@ -122,14 +127,34 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
   memset(&maps, 0, sizeof(maps));
   const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
   int rc;
-  // A operand (this CTA's 128 rows): K-major [M rows, K] or MN-major [K rows, M]
-  if (L.e4m3)
-    rc = make_tmap_2d(&maps.a, L.a, L.K, L.M, uint64_t(L.lda) * eb, kbe, 128, sw, CU_TENSOR_MAP_DATA_TYPE_UINT8);
-  else if (L.amode == A_K)
-    rc = make_tmap_2d(&maps.a, L.a, L.K, L.M, uint64_t(L.lda) * 2, 64, 128, sw);
-  else
-    rc = make_tmap_2d(&maps.a, L.a, L.M, L.K, uint64_t(L.lda) * 2, 64, 64, sw);
-  if (rc) return set_error(MEA_ERR_CUDA, "gemm: A tensor map failed (%d)", rc);
+  // A operand (this CTA's 128 rows): K-major [M rows, K] or MN-major [K rows, M],
+  // or (per-head modes) four [tokens*H, hd] parts with 64-wide boxes of 128
+  // (K-major) or 64 (MN-major) rows.
+  const bool a_heads = L.amode == A_K_HEADS || L.amode == A_MN_HEADS;
+  if (a_heads) {
+    const int hd = p.hd;
+    const long long tokens = L.amode == A_K_HEADS ? L.M : L.K;
+    const long long hn4 = 4LL * p.H * hd;
+    if (hd % 64 || hd <= 0 || p.H <= 0 || p.T % GEMM_BM || p.T <= 0 || tokens % p.T ||
+        (L.amode == A_K_HEADS ? L.K : L.M) != hn4)
+      return set_error(MEA_ERR_UNSUPPORTED_SHAPE, "gemm: per-head A needs hd %% 64 == 0, T %% 128 == 0, 4*H*hd = %s",
+                       L.amode == A_K_HEADS ? "K" : "M");
+    for (int i = 0; i < 4; ++i) {
+      if (!L.a4[i]) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: A part %d is null", i);
+      rc = make_tmap_2d(&maps.a[i], L.a4[i], uint64_t(hd), uint64_t(tokens) * p.H, uint64_t(hd) * 2, 64,
+                        L.amode == A_K_HEADS ? 128 : 64, sw);
+      if (rc) return set_error(MEA_ERR_CUDA, "gemm: A part map %d failed (%d)", i, rc);
+    }
+  } else {
+    if (L.e4m3)
+      rc = make_tmap_2d(&maps.a[0], L.a, L.K, L.M, uint64_t(L.lda) * eb, kbe, 128, sw, CU_TENSOR_MAP_DATA_TYPE_UINT8);
+    else if (L.amode == A_K)
+      rc = make_tmap_2d(&maps.a[0], L.a, L.K, L.M, uint64_t(L.lda) * 2, 64, 128, sw);
+    else
+      rc = make_tmap_2d(&maps.a[0], L.a, L.M, L.K, uint64_t(L.lda) * 2, 64, 64, sw);
+    if (rc) return set_error(MEA_ERR_CUDA, "gemm: A tensor map failed (%d)", rc);
+    for (int i = 1; i < 4; ++i) maps.a[i] = maps.a[0];
+  }
   // B operand (this CTA's bn/2 columns)
   const int nb = (L.bmode == B_K || L.bmode == B_MN) ? 1 : 4;
   for (int i = 0; i < nb; ++i) {
@@ -171,8 +196,11 @@ int run_gemm(const GemmLaunch& L, GemmParams p, cudaStream_t st) {
     }
     if (L.epi == EPI_DGATE) {
       if (!L.out[1]) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: dg output is null");
-      if ((rc = hd_map(&maps.out[1], L.out[1], uint64_t(L.M), hd, uint64_t(L.ldo), uint64_t(p.H) * hd)))
-        return set_error(MEA_ERR_CUDA, "gemm: dg output map failed (%d)", rc);
+      if (p.dg_heads)
+        rc = hd_map(&maps.out[1], L.out[1], bht, hd, hd, hd);
+      else
+        rc = hd_map(&maps.out[1], L.out[1], uint64_t(L.M), hd, uint64_t(L.ldo), uint64_t(p.H) * hd);
+      if (rc) return set_error(MEA_ERR_CUDA, "gemm: dg output map failed (%d)", rc);
     }
     for (int i = 0; i < 2; ++i) {
       if (!L.in[i]) return set_error(MEA_ERR_INVALID_ARGUMENT, "gemm: epilogue input %d is null", i);

@@ -39,7 +39,12 @@
 
 namespace mea {
 
-enum AMode : int { A_K = 0, A_MN = 1 };
+// A_K_HEADS / A_MN_HEADS: A as A_K / A_MN, but stored as four [B*H*T, hd]
+// tensors (per-head layout, hd a multiple of 64): logical column (A_K_HEADS)
+// or row (A_MN_HEADS) j = part*H*hd + h*hd + n of token (b, t) lives in part
+// `part` at row (b*H + h)*T + t, column n.  Every 64-wide chunk of j stays in
+// one head, so each is one TMA box.
+enum AMode : int { A_K = 0, A_MN = 1, A_K_HEADS = 2, A_MN_HEADS = 3 };
 enum BMode : int { B_K = 0, B_MN = 1, B_SLABS = 2, B_MN_KSPLIT4 = 3 };
 enum EpiMode : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_RED_F32 = 2, EPI_QKVG = 3, EPI_DGATE = 4 };
 
@@ -48,7 +53,7 @@ enum EpiMode : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_RED_F32 = 2, EPI_QKVG = 3, E
 // ([M, H*N] view of the g slot).  in: EPI_QKVG the rotary tables f1, f2
 // ([T_max, N]); EPI_DGATE O and sigmoid(g) ([B*H*T, N]).
 struct GemmMaps {
-  CUtensorMap a;
+  CUtensorMap a[4];  // [0] only, except A_K_HEADS / A_MN_HEADS (one per part)
   CUtensorMap b[4];
   CUtensorMap out[4];
   CUtensorMap in[2];
@@ -69,7 +74,18 @@ struct GemmParams {
   float eps;
   // EPI_DGATE
   float* delta;
+  int dg_heads;  // dg_pre stored [B*H*T, hd] (like dO) instead of [M, H*hd]
 };
+
+// Logical index j of the 4*H*hd dimension of an A_*_HEADS operand -> part,
+// head and column within the head.
+__device__ __forceinline__ void heads_coord(const GemmParams& p, int j, int& part, int& h, int& n) {
+  const int hn = p.H * p.hd;
+  part = j / hn;
+  const int rem = j - part * hn;
+  h = rem / p.hd;
+  n = rem - h * p.hd;
+}
 
 constexpr int GEMM_BM = 128;  // rows per CTA; a pair covers 256
 constexpr int GEMM_BK = 64;
@@ -518,7 +534,10 @@ __device__ __forceinline__ void epi_dgate(const GemmMaps& maps, const GemmParams
 #pragma unroll
       for (int bx = 0; bx < (HD + 63) / 64; ++bx) {
         tma_store_2d(&maps.out[0], buf + bx * 4096, 64 * bx, row);
-        tma_store_2d(&maps.out[1], buf + TILE + bx * 4096, head * HD + 64 * bx, mq);
+        if (p.dg_heads)
+          tma_store_2d(&maps.out[1], buf + TILE + bx * 4096, 64 * bx, row);
+        else
+          tma_store_2d(&maps.out[1], buf + TILE + bx * 4096, head * HD + 64 * bx, mq);
       }
       bulk_commit();
     }
@@ -539,9 +558,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
   constexpr int STAGES = Cfg::STAGES;
   static_assert(!E4M3 || (AM == A_K && BMD == B_K), "e4m3 GEMM: K-major operands only");
   constexpr int KBE = E4M3 ? 2 * GEMM_BK : GEMM_BK;  // K elements per stage
+  constexpr bool A_MNMAJ = AM == A_MN || AM == A_MN_HEADS;  // A tiles M-major in shared memory
   constexpr uint32_t IDESC =
       E4M3 ? idesc_e4m3(2 * GEMM_BM, BN)
-           : idesc_bf16(2 * GEMM_BM, BN, AM == A_MN ? 1u : 0u, (BMD == B_MN || BMD == B_MN_KSPLIT4) ? 1u : 0u);
+           : idesc_bf16(2 * GEMM_BM, BN, A_MNMAJ ? 1u : 0u, (BMD == B_MN || BMD == B_MN_KSPLIT4) ? 1u : 0u);
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
   constexpr int HB = BN / 2;  // B columns staged by each CTA
 
@@ -583,8 +603,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&maps.a);
-    for (int i = 0; i < 4; ++i) tma_prefetch_desc(&maps.b[i]);
+    for (int i = 0; i < 4; ++i) {
+      tma_prefetch_desc(&maps.a[i]);
+      tma_prefetch_desc(&maps.b[i]);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), Cfg::TMEM_COLS);
@@ -611,6 +633,34 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
         gemm_decode(p, BN, u, m0, n0, kb0, kb1);
         const int mc = m0 + int(rank) * GEMM_BM;  // this CTA's rows
         const int nc = n0 + int(rank) * HB;       // this CTA's B columns
+        // Per-head A and split B coordinates are set up once per unit and then
+        // stepped per k-block: no integer division on this thread's k-loop.
+        //  A_K_HEADS : (part, head, column) of the k-block; rows of one sequence.
+        //  A_MN_HEADS: (part, head, column) of each 64-row chunk; (sequence, position) of the k-block.
+        //  B_MN_KSPLIT4: source tensor and row of the k-block.
+        int a_part[2] = {0, 0}, a_h[2] = {0, 0}, a_n[2] = {0, 0}, a_b = 0, a_t = 0, b_src = 0, b_kr = 0;
+        if (AM == A_K_HEADS) {
+          heads_coord(p, kb0 * GEMM_BK, a_part[0], a_h[0], a_n[0]);
+          a_b = mc / p.T;
+          a_t = mc - a_b * p.T;
+        } else if (AM == A_MN_HEADS) {
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            // a chunk at or past M (a pair's second CTA past the end) reads part 0
+            // one row past its end: zero fill, the full box still counted.
+            if (mc + 64 * i < p.M) heads_coord(p, mc + 64 * i, a_part[i], a_h[i], a_n[i]);
+            else a_h[i] = -1;
+          }
+          a_b = (kb0 * GEMM_BK) / p.T;
+          a_t = kb0 * GEMM_BK - a_b * p.T;
+        }
+        if (BMD == B_MN_KSPLIT4) {
+          b_src = kb0 / p.b_kb_per_src;
+          b_kr = (kb0 - b_src * p.b_kb_per_src) * GEMM_BK;
+        }
+        // B_SLABS: slabs staged by each CTA, and the first one's index
+        const int sl_half = BMD == B_SLABS ? BN / p.slab_rows / 2 : 0;
+        const int sl_sg0 = BMD == B_SLABS ? nc / p.slab_rows : 0;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, g, 1)) break;
           // both CTAs' copies count on the leader's barrier; the leader expects their sum
@@ -619,10 +669,30 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
           const uint32_t a_dst = sA + stage * GEMM_A_BYTES;
           const uint32_t b_dst = sB + stage * Cfg::B_BYTES;
           if (AM == A_K) {
-            tma_load_2d_pair(a_dst, &maps.a, fb, kb * KBE, mc);
+            tma_load_2d_pair(a_dst, &maps.a[0], fb, kb * KBE, mc);
+          } else if (AM == A_MN) {
+            tma_load_2d_pair(a_dst, &maps.a[0], fb, mc, kb * GEMM_BK);
+            tma_load_2d_pair(a_dst + 8192, &maps.a[0], fb, mc + 64, kb * GEMM_BK);
+          } else if (AM == A_K_HEADS) {
+            // 128 token rows (one sequence: T % 128 == 0) x the 64 columns of one head
+            tma_load_2d_pair(a_dst, &maps.a[a_part[0]], fb, a_n[0], (a_b * p.H + a_h[0]) * p.T + a_t);
+            if ((a_n[0] += GEMM_BK) == p.hd) {
+              a_n[0] = 0;
+              if (++a_h[0] == p.H) {
+                a_h[0] = 0;
+                ++a_part[0];
+              }
+            }
           } else {
-            tma_load_2d_pair(a_dst, &maps.a, fb, mc, kb * GEMM_BK);
-            tma_load_2d_pair(a_dst + 8192, &maps.a, fb, mc + 64, kb * GEMM_BK);
+            // 64 tokens (one sequence) x two 64-wide row chunks, each within one head
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+              tma_load_2d_pair(a_dst + 8192 * i, &maps.a[a_part[i]], fb, a_n[i],
+                               a_h[i] < 0 ? p.K * p.H : (a_b * p.H + a_h[i]) * p.T + a_t);
+            if ((a_t += GEMM_BK) == p.T) {
+              a_t = 0;
+              ++a_b;
+            }
           }
           if (BMD == B_K) {
             tma_load_2d_pair(b_dst, &maps.b[0], fb, kb * KBE, nc);
@@ -631,18 +701,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
             for (int i = 0; i < HB / 64; ++i)
               tma_load_2d_pair(b_dst + 8192 * i, &maps.b[0], fb, nc + 64 * i, kb * GEMM_BK);
           } else if (BMD == B_SLABS) {
-            const int half = BN / p.slab_rows / 2;  // slabs staged by each CTA
-            for (int s = 0; s < half; ++s) {
-              const int sg = nc / p.slab_rows + s;
+            for (int s = 0; s < sl_half; ++s) {
+              const int sg = sl_sg0 + s;
               tma_load_2d_pair(b_dst + s * p.slab_rows * 128, &maps.b[sg & 3], fb, kb * GEMM_BK,
                                (sg >> 2) * p.slab_rows);
             }
           } else {
-            const int src = kb / p.b_kb_per_src;
-            const int kr = (kb - src * p.b_kb_per_src) * GEMM_BK;
 #pragma unroll
             for (int i = 0; i < HB / 64; ++i)
-              tma_load_2d_pair(b_dst + 8192 * i, &maps.b[src], fb, nc + 64 * i, kr);
+              tma_load_2d_pair(b_dst + 8192 * i, &maps.b[b_src], fb, nc + 64 * i, b_kr);
+            if ((b_kr += GEMM_BK) == p.b_kb_per_src * GEMM_BK) {
+              b_kr = 0;
+              ++b_src;
+            }
           }
           last_par[stage] = int(phase);
           if (++stage == STAGES) {
@@ -686,8 +757,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, EPI, HD>::THREADS, 1)
           const uint32_t b_base = sB + stage * Cfg::B_BYTES;
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 16; ++k) {
-            const uint64_t ad = AM == A_K ? smem_desc(a_base + 32 * k, 16, 1024, SW_128B)
-                                          : smem_desc(a_base + 2048 * k, 8192, 1024, SW_128B);
+            const uint64_t ad = !A_MNMAJ ? smem_desc(a_base + 32 * k, 16, 1024, SW_128B)
+                                         : smem_desc(a_base + 2048 * k, 8192, 1024, SW_128B);
             const uint64_t bd = (BMD == B_K || BMD == B_SLABS) ? smem_desc(b_base + 32 * k, 16, 1024, SW_128B)
                                                                 : smem_desc(b_base + 2048 * k, 8192, 1024, SW_128B);
             if constexpr (E4M3)

@@ -24,11 +24,13 @@ struct GemmParams;
 struct GemmLaunch {
   int M, N, K;
   int bn;      // 128 or 256
-  int amode;   // A_K / A_MN
+  int amode;   // A_K / A_MN / A_K_HEADS / A_MN_HEADS
   int bmode;   // B_K / B_MN / B_SLABS / B_MN_KSPLIT4
   int epi;     // EpiMode
   const void* a;
   long long lda;        // elements between rows of A as stored
+  const void* a4[4];    // A_K_HEADS / A_MN_HEADS: the four [tokens*H, hd] parts of A
+                        // (GemmParams H, T, hd describe them)
   const void* b[4];
   long long ldb;        // elements between rows of B as stored
   int b_rows;           // B_SLABS / B_MN_KSPLIT4: rows of each B tensor
@@ -39,7 +41,8 @@ struct GemmLaunch {
   //   EPI_QKVG : out[0..3] = q, k, v, sigmoid(g) [B*H*T, hd]; in[0..1] = rotary
   //              tables [in_rows, hd] with row pitch ldin
   //   EPI_DGATE: out[0] = dO [B*H*T, hd]; out[1] = dg_pre [M, H*hd] with row
-  //              pitch ldo; in[0..1] = O, sigmoid(g) [B*H*T, hd]
+  //              pitch ldo, or [B*H*T, hd] when GemmParams.dg_heads is set;
+  //              in[0..1] = O, sigmoid(g) [B*H*T, hd]
   void* out[4];
   long long ldo;
   const void* in[2];
@@ -62,10 +65,12 @@ int run_attn_fwd(int B, int H, int T, int HD, const void* q, const void* k, cons
                  float* lse2, void* o_out, const float* bound, const float* lse_in, int* status, cudaStream_t st,
                  float* dq_zero = nullptr);
 // `dv_row_scale` ([B*T] fp32, may be NULL): dV row (b, t) is multiplied by
-// dv_row_scale[b*T + t] before it is stored.
+// dv_row_scale[b*T + t] before it is stored.  `dv_heads`: dv is [B,H,T,N] like
+// dk (ld_dv ignored); it may then be v itself, since each V tile is read only
+// by the work item that writes its dV tile, and only before that write.
 int run_attn_bwd(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
                  const float* lse2, const float* delta, float* dq_acc, void* dk, void* dv, long long ld_dv, int* status,
-                 cudaStream_t st, const float* dv_row_scale = nullptr);
+                 cudaStream_t st, const float* dv_row_scale = nullptr, bool dv_heads = false);
 // The shape, pointer and alignment checks of run_attn_bwd (all but dq_acc),
 // with no device work: MEA_OK or the error run_attn_bwd would return.
 int check_attn_bwd_args(int B, int H, int T, int HD, const void* q, const void* k, const void* v, const void* dO,
@@ -82,6 +87,11 @@ int run_rmsnorm_bwd(int rows, int C, const void* dxn, const void* x, const float
 int run_qk_norm_rope_bwd(int B, int H, int T, int HD, const float* dq_acc, const void* dk, const void* q_rot,
                          const void* k_rot, const float* rq, const float* rk, const void* f1, const void* f2,
                          long long ldf, void* dacc, long long ld_dacc, float* df1, float* df2, cudaStream_t st);
+// The same with the projection gradients written over q_rot / k_rot ([B,H,T,N]):
+// every element is read by the thread that writes it, before it writes it.
+int run_qk_norm_rope_bwd_inplace(int B, int H, int T, int HD, const float* dq_acc, const void* dk, void* q_rot,
+                                 void* k_rot, const float* rq, const float* rk, const void* f1, const void* f2,
+                                 long long ldf, float* df1, float* df2, cudaStream_t st);
 int run_cast_f32_bf16(long long n, const float* src, void* dst, cudaStream_t st);
 // gated[b,t,h*N+n] = o[b,h,t,n] * gs[b,h,t,n] (all bf16).
 int run_gate_repack(int B, int H, int T, int HD, const void* o, const void* gs, void* gated, cudaStream_t st);
