@@ -95,6 +95,16 @@ def test_block_large_table_takes_online_max():
     check(run_block(inp, 2, 128), block_fwd_bwd(inp, 2, 128), ["y", *GRAD_NAMES])
 
 
+@pytest.mark.parametrize("H,N", [(3, 128), (6, 64)])
+def test_block_head_counts_off_the_tile_grid(H, N):
+    """H*N = 384: not a multiple of 256, so the q/k/v/g parts of the projection
+    gradient (4*H*N rows of the weight-gradient GEMM, columns of the dx GEMM's K)
+    start in the middle of a CTA pair's 256-row tile, and the gate GEMM takes
+    128-wide tiles."""
+    inp = make_inputs(2, 256, 256, H, N, seed=13)
+    check(run_block(inp, H, N), block_fwd_bwd(inp, H, N), ["y", *GRAD_NAMES])
+
+
 def test_block_without_factor_grads():
     inp = make_inputs(1, 256, 256, 4, 64, seed=8)
     got = run_block(inp, 4, 64, factor_grads=False)
