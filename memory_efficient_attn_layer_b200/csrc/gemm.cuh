@@ -50,7 +50,7 @@ enum EpiMode : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_RED_F32 = 2, EPI_QKVG = 3, E
 
 // out: EPI_BF16/F32/RED_F32 out[0] = D; EPI_QKVG out[0..3] = q, k, v, sigmoid(g)
 // ([B*H*T, N] views); EPI_DGATE out[0] = dO ([B*H*T, N]), out[1] = dg_pre
-// ([M, H*N] view of the g slot).  in: EPI_QKVG the rotary tables f1, f2
+// ([M, H*N] view of the g slot, or [B*H*T, N] with dg_heads).  in: EPI_QKVG the rotary tables f1, f2
 // ([T_max, N]); EPI_DGATE O and sigmoid(g) ([B*H*T, N]).
 struct GemmMaps {
   CUtensorMap a[4];  // [0] only, except A_K_HEADS / A_MN_HEADS (one per part)
