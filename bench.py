@@ -49,7 +49,7 @@ LAUNCHES_PER_STAGE = {"bwd.memset": 0, "fwd.attention": 2}
 # DRAM bytes per launch and per sequence, dram__bytes.sum from ncu captures of the c2 kernels at
 # B=16 (every sequence is independent, so the traffic scales with B); the roofline's "traffic".
 DRAM_BYTES_PER_SEQ = {
-    "c2": {"bwd.attention_bwd": 291.9e6 / 16, "fwd.attention": 154.6e6 / 16,
+    "c2": {"bwd.attention_bwd": 287.0e6 / 16, "fwd.attention": 154.6e6 / 16,
            "bwd.attention_recompute": 179.1e6 / 16, "fwd.qkvg_gemm": 116.8e6 / 16,
            "bwd.qk_norm_rope_bwd": 216.5e6 / 16},
 }
