@@ -647,7 +647,9 @@ def run_gpu(args, cfg, rank, world, device):
     xh = x.detach().cpu().pin_memory()
     dyh = dy.detach().cpu().pin_memory()
     loss_h = torch.empty(1, dtype=torch.float32).pin_memory()
-    e2e_steps = max(10, args.steps // 10)
+    # enough steps that the pipeline's fill (the first copy, exposed, and the last step's compute) is a
+    # small share of the timed region
+    e2e_steps = max(30, args.steps // 4)
     comp = torch.cuda.current_stream(device)
     copy_stream = torch.cuda.Stream(device)
     xbuf = [torch.empty_like(x) for _ in range(2)]
