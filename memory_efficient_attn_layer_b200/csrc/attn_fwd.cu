@@ -477,32 +477,29 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         }
         const float neg_m = mode != 0 ? -ref : -m_run;
         uint32_t pk[32];
-        // keys [0, 64)
-        l_run += diag ? exp_half_regs<true>(sb, 0, r, sl2, neg_m, pk) : exp_half_regs<false>(sb, 0, r, sl2, neg_m, pk);
-        tc_fence_before();
-        mbar_arrive(s_empty);
-        if (!pv_seen) {
-          ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, g, 12));
-          if (!ok) break;
-          tc_fence_after();
-        }
+        // Keys [0, 64), then [64, 128): one loop (not unrolled), so the exponential
+        // code exists once and stays resident in the instruction cache.
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          if (hh == 1 && !have_b) {
+            ok = __all_sync(0xffffffffu, mbar_wait(s_full_b, j & 1, g, 17));
+            if (!ok) break;
+            tc_fence_after();
+          }
+          l_run += diag ? exp_half_regs<true>(sb, hh, r, sl2, neg_m, pk) : exp_half_regs<false>(sb, hh, r, sl2, neg_m, pk);
+          tc_fence_before();
+          mbar_arrive(hh ? s_empty_b : s_empty);
+          if (hh == 0 && !pv_seen) {
+            ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, g, 12));
+            if (!ok) break;
+            tc_fence_after();
+          }
 #pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2)
-          tmem_st16(lane_base + Cfg::P_COL + 16 * q2, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * q2));
-        tmem_st_wait();  // the registers of pk are rewritten below
-        // keys [64, 128)
-        if (!have_b) {
-          ok = __all_sync(0xffffffffu, mbar_wait(s_full_b, j & 1, g, 17));
-          if (!ok) break;
-          tc_fence_after();
+          for (int q2 = 0; q2 < 2; ++q2)
+            tmem_st16(lane_base + Cfg::P_COL + 32 * hh + 16 * q2, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * q2));
+          tmem_st_wait();  // the registers of pk are rewritten by the next half
         }
-        l_run += diag ? exp_half_regs<true>(sb, 1, r, sl2, neg_m, pk) : exp_half_regs<false>(sb, 1, r, sl2, neg_m, pk);
-        tc_fence_before();
-        mbar_arrive(s_empty_b);
-#pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2)
-          tmem_st16(lane_base + Cfg::P_COL + 32 + 16 * q2, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16 * q2));
-        tmem_st_wait();
+        if (!ok) break;
         tc_fence_before();
         mbar_arrive(p_full);
       }
