@@ -194,7 +194,9 @@ __device__ __forceinline__ float exp_half_regs(uint32_t sb, int hh, int r, float
   return (acc0.x + acc0.y) + (acc1.x + acc1.y);
 }
 
-template <int HD>
+// RECOMP: the backward's recompute against the saved LSE (p.lse_in set): P comes
+// out normalised, so no row max or row sum is formed and no LSE is written.
+template <int HD, bool RECOMP>
 __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ AttnFwdMaps maps, const AttnFwdParams p) {
   using Cfg = AttnFwdCfg<HD>;
   using Tile = HeadTile<HD>;
@@ -420,7 +422,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     // Reference for exp2 (uniform over the CTA): 2 = saved LSE, 1 = score bound, 0 = online max.
     int mode = 0;
     float ref = 0.f;
-    if (p.lse_in) {
+    if constexpr (RECOMP) {
       mode = 2;
       ref = p.lse_in[bht];
     } else if (p.bound) {
@@ -586,7 +588,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
                            "r"(oo[2]), "r"(oo[3]) : "memory");
           }
         }
-        if (p.lse2) p.lse2[bht] = m_run + __log2f(l_run);
+        if (!RECOMP && p.lse2) p.lse2[bht] = m_run + __log2f(l_run);
         fence_proxy_async_smem();
         __syncwarp();
         if (p.dq_zero) {
@@ -649,7 +651,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
           st_global_v4(orow + c + 8, oo[4], oo[5], oo[6], oo[7]);
         }
       }
-      if (p.lse2) p.lse2[bht] = m_run + __log2f(l_run);
+      if (!RECOMP && p.lse2) p.lse2[bht] = m_run + __log2f(l_run);
     }
     }
     if (!ok) g.ok = false;
@@ -666,7 +668,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
 template <int HD>
 static int launch_attn_fwd_t(const AttnFwdMaps& maps, const AttnFwdParams& p, cudaStream_t st) {
   using Cfg = AttnFwdCfg<HD>;
-  auto kern = attn_fwd_kernel<HD>;
+  auto kern = p.lse_in ? attn_fwd_kernel<HD, true> : attn_fwd_kernel<HD, false>;
   if (!smem_attr_set(reinterpret_cast<const void*>(kern), int(Cfg::SMEM)))
     return set_error(MEA_ERR_CUDA, "cudaFuncSetAttribute(attn_fwd) failed");
   const int grid = p.B * p.H * (p.T / 128);
