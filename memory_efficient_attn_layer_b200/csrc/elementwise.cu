@@ -361,21 +361,26 @@ __device__ __forceinline__ float pair_sigma2(float a, float d, float b, float c)
   return 0.5f * (fro + sqrtf(fmaxf(fro * fro - 4.f * det * det, 0.f)));
 }
 
-// One CTA of 1024 threads; each thread reads 16-byte pieces (4 rotary pairs of
-// each table), all of its loads issued before any is used.
-__global__ void __launch_bounds__(1024) rope_bound_kernel(int T, int HD, const __nv_bfloat16* __restrict__ f1,
-                                                          const __nv_bfloat16* __restrict__ f2, long long ldf,
-                                                          float* __restrict__ out) {
-  __shared__ float red[32];
+// A grid of CTAs (256 threads) striding over the tables' 16-byte pieces (4
+// rotary pairs of each table), every thread's loads issued before any is used.
+// Each CTA maps its partial maximum through the bound's (increasing) formula
+// and folds it into *out with an integer atomicMax: the bounds are positive, so
+// integer order is float order, and the result equals the bound of the global
+// maximum.  *out must be zero on entry.
+__global__ void __launch_bounds__(256) rope_bound_kernel(int T, int HD, const __nv_bfloat16* __restrict__ f1,
+                                                         const __nv_bfloat16* __restrict__ f2, long long ldf,
+                                                         float* __restrict__ out) {
+  __shared__ float red[8];
   const int per_row = HD / 8;  // 16-byte pieces per table row
   const int n = T * per_row;
+  const int stride = gridDim.x * blockDim.x;
   float s2 = 0.f;
   constexpr int U = 4;
-  for (int base = threadIdx.x; base < n; base += U * blockDim.x) {
+  for (int base = blockIdx.x * blockDim.x + threadIdx.x; base < n; base += U * stride) {
     uint4 a[U], b[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int i = base + u * blockDim.x;
+      const int i = base + u * stride;
       if (i < n) {
         const int t = i / per_row, e = (i - t * per_row) * 8;
         a[u] = __ldg(reinterpret_cast<const uint4*>(f1 + size_t(t) * ldf + e));
@@ -401,7 +406,8 @@ __global__ void __launch_bounds__(1024) rope_bound_kernel(int T, int HD, const _
     float m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
 #pragma unroll
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (threadIdx.x == 0) *out = (m * sqrtf(float(HD)) * 1.4426950408889634f) * 1.01f + 0.05f;
+    if (threadIdx.x == 0)
+      atomicMax(reinterpret_cast<int*>(out), __float_as_int((m * sqrtf(float(HD)) * 1.4426950408889634f) * 1.01f + 0.05f));
   }
 }
 
@@ -457,8 +463,12 @@ int run_rope_bound(int T, int HD, const void* f1, const void* f2, long long ldf,
     return set_error(MEA_ERR_INVALID_ARGUMENT, "rope bound: bad arguments");
   if ((reinterpret_cast<uintptr_t>(f1) | reinterpret_cast<uintptr_t>(f2)) & 15)
     return set_error(MEA_ERR_ALIGNMENT, "rope bound: tables must be 16-byte aligned");
-  rope_bound_kernel<<<1, 1024, 0, st>>>(T, HD, static_cast<const __nv_bfloat16*>(f1),
-                                       static_cast<const __nv_bfloat16*>(f2), ldf, out);
+  if (cudaMemsetAsync(out, 0, sizeof(float), st) != cudaSuccess)
+    return set_error(MEA_ERR_CUDA, "rope bound: clearing the output failed");
+  const int pieces = T * (HD / 8);
+  const int blocks = std::max(1, std::min((pieces + 4 * 256 - 1) / (4 * 256), num_sms()));
+  rope_bound_kernel<<<blocks, 256, 0, st>>>(T, HD, static_cast<const __nv_bfloat16*>(f1),
+                                            static_cast<const __nv_bfloat16*>(f2), ldf, out);
   return check_launch("rope_bound_kernel");
 }
 
